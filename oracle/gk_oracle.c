@@ -1,0 +1,556 @@
+/*
+ * gk_oracle.c - CPU oracle for the batched self-play path (TEST INFRASTRUCTURE).
+ *
+ * This file restates, in plain C on the int32[170] wire record, the reference
+ * algorithms the CUDA path must reproduce bit for bit:
+ *   - rules:   State::play        engine/src/State.cpp:92-167
+ *              placement_error    engine/src/State.cpp:72-90
+ *              score              engine/src/State.cpp:48-61
+ *              claim_territory    engine/src/State.cpp:63-70
+ *              Board::territory   engine/src/Board.cpp:149-198
+ *              collect_group      engine/src/Board.cpp:41-61
+ *              wire updates       python/kingdom_ai/gpu_rules.py:185-252
+ *   - encoder: encode             mcts/src/BatchedPUCT.cpp:25-50
+ *   - search:  PUCT::search       mcts/src/PUCT.cpp:177-268
+ *              expand             mcts/src/PUCT.cpp:53-86
+ *              select_edge        mcts/src/PUCT.cpp:118-142
+ *              better_move        mcts/src/PUCT.cpp:151-157
+ * plus the harness definitions that have no reference counterpart (the PCG32
+ * playout and position generators and the injected evaluator, which live in
+ * include/gk_common.h and are shared with the kernels).
+ *
+ * Only tests, the smoke check and the benchmark's CPU-baseline leg may load
+ * this code; the product never does. Build with -ffp-contract=off.
+ */
+#include "gk_oracle.h"
+
+#include <math.h>
+#include <pthread.h>
+#include <stdlib.h>
+#include <string.h>
+
+#include "../include/gk_common.h"
+
+/* ---------------------------------------------------------------- rules */
+
+static int nbrs(int i, int* out) {
+    int row = i / 9, col = i % 9, n = 0;
+    if (row > 0) out[n++] = i - 9;
+    if (row < 8) out[n++] = i + 9;
+    if (col > 0) out[n++] = i - 1;
+    if (col < 8) out[n++] = i + 1;
+    return n;
+}
+
+static unsigned edge_mask(int i) {
+    int row = i / 9, col = i % 9;
+    return (row == 0 ? 1u : 0u) | (row == 8 ? 2u : 0u) | (col == 0 ? 4u : 0u) | (col == 8 ? 8u : 0u);
+}
+
+/* Board.cpp:41-61: breadth-first group of the stone at `start`. */
+static int collect_group(const int32_t* cells, int start, int* queue) {
+    int player = cells[start];
+    if (player != 1 && player != 2) return 0;
+    unsigned char visited[GK_CELLS];
+    memset(visited, 0, sizeof visited);
+    int length = 1;
+    queue[0] = start;
+    visited[start] = 1;
+    for (int cursor = 0; cursor < length; ++cursor) {
+        int nb[4];
+        int count = nbrs(queue[cursor], nb);
+        for (int n = 0; n < count; ++n) {
+            int next = nb[n];
+            if (!visited[next] && cells[next] == player) {
+                visited[next] = 1;
+                queue[length++] = next;
+            }
+        }
+    }
+    return length;
+}
+
+static int group_has_liberty(const int32_t* cells, const int* group, int length) {
+    for (int i = 0; i < length; ++i) {
+        int nb[4];
+        int count = nbrs(group[i], nb);
+        for (int n = 0; n < count; ++n)
+            if (cells[nb[n]] == 0) return 1;
+    }
+    return 0;
+}
+
+/* Board.cpp:149-198 with allow_single_edge = true: owners[i] in {0,1,2}. */
+static void territory(const int32_t* cells, int* owners) {
+    for (int i = 0; i < GK_CELLS; ++i) owners[i] = 0;
+    for (int player = 1; player <= 2; ++player) {
+        int enemy = 3 - player;
+        unsigned char visited[GK_CELLS];
+        int queue[GK_CELLS];
+        memset(visited, 0, sizeof visited);
+        for (int start = 0; start < GK_CELLS; ++start) {
+            if (visited[start] || cells[start] != 0) continue;
+            int length = 1;
+            queue[0] = start;
+            visited[start] = 1;
+            int contains_enemy = 0, has_own_boundary = 0;
+            unsigned edges = 0;
+            for (int cursor = 0; cursor < length; ++cursor) {
+                int current = queue[cursor];
+                edges |= edge_mask(current);
+                contains_enemy |= cells[current] == enemy;
+                int nb[4];
+                int count = nbrs(current, nb);
+                for (int n = 0; n < count; ++n) {
+                    int next = nb[n];
+                    if (cells[next] == player) {
+                        has_own_boundary = 1;
+                    } else if (cells[next] != 3 && !visited[next]) {
+                        visited[next] = 1;
+                        queue[length++] = next;
+                    }
+                }
+            }
+            if (contains_enemy || !has_own_boundary || edges == 15u) continue;
+            for (int i = 0; i < length; ++i)
+                if (cells[queue[i]] == 0) owners[queue[i]] = player;
+        }
+    }
+}
+
+static void claim_territory(int32_t* rec) {
+    int detected[GK_CELLS];
+    territory(rec, detected);
+    for (int i = 0; i < GK_CELLS; ++i)
+        if (rec[GK_CELLS + i] == 0 && detected[i] != 0) rec[GK_CELLS + i] = detected[i];
+}
+
+void gko_score(const int32_t* rec, int* black, int* white) {
+    int b = 0, w = 0;
+    for (int i = 0; i < GK_CELLS; ++i) {
+        if (rec[i] != 0) continue;
+        b += rec[GK_CELLS + i] == 1;
+        w += rec[GK_CELLS + i] == 2;
+    }
+    *black = b;
+    *white = w;
+}
+
+void gko_initial(int32_t* rec, int neutral_cell) {
+    memset(rec, 0, GK_STATE_WIDTH * sizeof(int32_t));
+    if (neutral_cell >= 0 && neutral_cell < GK_CELLS) rec[neutral_cell] = 3;
+    rec[GK_ACTOR] = 1;
+    rec[GK_BLACK_STOCK] = GK_STONES;
+    rec[GK_WHITE_STOCK] = GK_STONES;
+}
+
+int gko_legal(const int32_t* rec, int action) {
+    if (rec[GK_REASON] != GK_NONE || action < 0 || action >= GK_ACTIONS) return 0;
+    if (action == GK_PASS) return 1;
+    int stock = rec[rec[GK_ACTOR] == 1 ? GK_BLACK_STOCK : GK_WHITE_STOCK];
+    return rec[action] == 0 && rec[GK_CELLS + action] == 0 && stock > 0;
+}
+
+int gko_play(int32_t* rec, int action) {
+    if (!gko_legal(rec, action)) return 0;
+    int actor = rec[GK_ACTOR], enemy = 3 - actor;
+    if (action == GK_PASS) {
+        ++rec[GK_PASSES];
+        rec[GK_ACTOR] = enemy;
+        if (rec[GK_PASSES] == 2) {
+            int b, w;
+            gko_score(rec, &b, &w);
+            rec[GK_REASON] = GK_TWO_PASSES;
+            rec[GK_WINNER] = b - w >= 3 ? 1 : 2;
+            rec[GK_CAPTURED] = 0;
+        }
+        return 1;
+    }
+    rec[action] = actor;
+    unsigned char examined[GK_CELLS], captured[GK_CELLS];
+    memset(examined, 0, sizeof examined);
+    memset(captured, 0, sizeof captured);
+    int captured_count = 0;
+    int nb[4], group[GK_CELLS];
+    int count = nbrs(action, nb);
+    for (int n = 0; n < count; ++n) {
+        int next = nb[n];
+        if (rec[next] != enemy || examined[next]) continue;
+        int length = collect_group(rec, next, group);
+        int surrounded = !group_has_liberty(rec, group, length);
+        for (int i = 0; i < length; ++i) {
+            examined[group[i]] = 1;
+            if (surrounded) {
+                captured[group[i]] = 1;
+                ++captured_count;
+            }
+        }
+    }
+    int suicide = 0;
+    if (captured_count == 0) {
+        int length = collect_group(rec, action, group);
+        suicide = !group_has_liberty(rec, group, length);
+    }
+    --rec[actor == 1 ? GK_BLACK_STOCK : GK_WHITE_STOCK];
+    rec[GK_PASSES] = 0;
+    rec[GK_ACTOR] = enemy;
+    if (captured_count > 0) {
+        for (int i = 0; i < GK_CELLS; ++i)
+            if (captured[i]) rec[i] = 0;
+        rec[GK_REASON] = GK_CAPTURE;
+        rec[GK_WINNER] = actor;
+        rec[GK_CAPTURED] = captured_count;
+    } else if (suicide) {
+        rec[GK_REASON] = GK_SUICIDE;
+        rec[GK_WINNER] = enemy;
+        rec[GK_CAPTURED] = 0;
+    } else {
+        claim_territory(rec);
+    }
+    return 1;
+}
+
+void gko_encode(const int32_t* rec, float* features, uint8_t* mask) {
+    int actor = rec[GK_ACTOR], enemy = 3 - actor;
+    int own_stock = rec[actor == 1 ? GK_BLACK_STOCK : GK_WHITE_STOCK];
+    int enemy_stock = rec[actor == 1 ? GK_WHITE_STOCK : GK_BLACK_STOCK];
+    float own_remaining = (float)((double)own_stock / 41.0);
+    float enemy_remaining = (float)((double)enemy_stock / 41.0);
+    float passes = (float)((double)rec[GK_PASSES] / 2.0);
+    for (int a = 0; a < GK_ACTIONS; ++a) mask[a] = (uint8_t)gko_legal(rec, a);
+    for (int i = 0; i < GK_CELLS; ++i) {
+        features[0 * 81 + i] = rec[i] == actor ? 1.0f : 0.0f;
+        features[1 * 81 + i] = rec[i] == enemy ? 1.0f : 0.0f;
+        features[2 * 81 + i] = rec[i] == 3 ? 1.0f : 0.0f;
+        features[3 * 81 + i] = rec[GK_CELLS + i] == actor ? 1.0f : 0.0f;
+        features[4 * 81 + i] = rec[GK_CELLS + i] == enemy ? 1.0f : 0.0f;
+        features[5 * 81 + i] = actor == 1 ? 1.0f : 0.0f;
+        features[6 * 81 + i] = own_remaining;
+        features[7 * 81 + i] = enemy_remaining;
+        features[8 * 81 + i] = passes;
+        features[9 * 81 + i] = mask[i] ? 1.0f : 0.0f;
+    }
+}
+
+void gko_play_batch(int32_t* recs, const int32_t* actions, uint8_t* accepted, int64_t n) {
+    for (int64_t i = 0; i < n; ++i) accepted[i] = (uint8_t)gko_play(recs + i * GK_STATE_WIDTH, actions[i]);
+}
+
+void gko_encode_batch(const int32_t* recs, float* features, uint8_t* masks, int64_t n) {
+    for (int64_t i = 0; i < n; ++i)
+        gko_encode(recs + i * GK_STATE_WIDTH, features + i * GK_FEATURES, masks + i * GK_ACTIONS);
+}
+
+/* ------------------------------------------------------ random playouts */
+
+/* Legal actions in index order (placements by row*9+col, then pass), the
+ * order of State::legal_moves (engine/src/State.cpp:183-198). */
+static int legal_list(const int32_t* rec, int* out) {
+    int n = 0;
+    for (int a = 0; a < GK_ACTIONS; ++a)
+        if (gko_legal(rec, a)) out[n++] = a;
+    return n;
+}
+
+static int cpp_reason(int wire) {
+    return wire == GK_CAPTURE ? GK_CPP_CAPTURE
+         : wire == GK_SUICIDE ? GK_CPP_SUICIDE
+         : wire == GK_TWO_PASSES ? GK_CPP_TWO_PASSES
+                                 : GK_CPP_NONE;
+}
+
+void gko_random_playout(uint64_t seed, uint64_t game, int neutral_cell, int8_t* board, int32_t* info) {
+    int32_t rec[GK_STATE_WIDTH];
+    int legal[GK_ACTIONS];
+    gk_pcg32 rng = gk_pcg32_seed(seed, game);
+    gko_initial(rec, neutral_cell);
+    int plies = 0;
+    while (rec[GK_REASON] == GK_NONE) {
+        int n = legal_list(rec, legal);
+        int j = (int)gk_pcg32_bounded(&rng, (uint32_t)n);
+        gko_play(rec, legal[j]);
+        ++plies;
+    }
+    for (int i = 0; i < GK_CELLS; ++i) board[i] = (int8_t)rec[i];
+    int b, w;
+    gko_score(rec, &b, &w);
+    info[0] = rec[GK_WINNER];
+    info[1] = cpp_reason(rec[GK_REASON]);
+    info[2] = b;
+    info[3] = w;
+    info[4] = plies;
+}
+
+void gko_random_playouts(uint64_t seed, uint64_t first_game, int64_t n, int neutral_cell, int8_t* boards,
+                         int32_t* infos) {
+    for (int64_t i = 0; i < n; ++i)
+        gko_random_playout(seed, first_game + (uint64_t)i, neutral_cell, boards + i * GK_CELLS, infos + i * 5);
+}
+
+/* Position generator: stream (seed, index); draw k in [0, 60], play k uniform
+ * legal moves from the default start; if the game ends within those k moves,
+ * draw a fresh k from the same stream and restart (at most 64 attempts, then
+ * the start position). */
+void gko_gen_position(uint64_t seed, uint64_t index, int32_t* rec) {
+    int legal[GK_ACTIONS];
+    gk_pcg32 rng = gk_pcg32_seed(seed, index);
+    for (int attempt = 0; attempt < 64; ++attempt) {
+        int k = (int)gk_pcg32_bounded(&rng, 61u);
+        gko_initial(rec, 40);
+        int ok = 1;
+        for (int i = 0; i < k; ++i) {
+            int n = legal_list(rec, legal);
+            int j = (int)gk_pcg32_bounded(&rng, (uint32_t)n);
+            gko_play(rec, legal[j]);
+            if (rec[GK_REASON] != GK_NONE) {
+                ok = 0;
+                break;
+            }
+        }
+        if (ok) return;
+    }
+    gko_initial(rec, 40);
+}
+
+void gko_gen_positions(uint64_t seed, uint64_t first, int64_t n, int32_t* recs) {
+    for (int64_t i = 0; i < n; ++i) gko_gen_position(seed, first + (uint64_t)i, recs + i * GK_STATE_WIDTH);
+}
+
+void gko_eval(const int32_t* rec, float* weights, float* value) {
+    uint64_t words[GK_EVAL_WORDS];
+    gk_eval_words_from_record(rec, words);
+    uint64_t h = gk_eval_hash_words(words);
+    for (int a = 0; a < GK_ACTIONS; ++a) weights[a] = gk_eval_weight(h, a);
+    *value = gk_eval_value(h);
+}
+
+/* ------------------------------------------------------------------ PUCT */
+
+typedef struct {
+    int move;
+    double prior;
+    int64_t visits;
+    double value_sum;
+    int child; /* -1: none */
+} o_edge;
+
+typedef struct {
+    int player;
+    int64_t visits;
+    int expanded;
+    int nedges;
+    o_edge* edges;
+} o_node;
+
+static double edge_value(const o_edge* e) { return e->visits == 0 ? 0.0 : e->value_sum / (double)e->visits; }
+
+/* PUCT.cpp:53-86 */
+static int expand(o_node* node, const int32_t* rec, o_edge* storage, double* leaf_value, int64_t* evaluations) {
+    int moves[GK_ACTIONS];
+    int n = legal_list(rec, moves);
+    if (n == 0) return -1;
+    float w[GK_ACTIONS], v;
+    gko_eval(rec, w, &v);
+    ++*evaluations;
+    if (!isfinite(v) || v < -1.0f || v > 1.0f) return -2;
+    for (int a = 0; a < GK_ACTIONS; ++a)
+        if (!isfinite(w[a]) || w[a] < 0.0f) return -2;
+    double largest = 0.0;
+    for (int i = 0; i < n; ++i) largest = fmax(largest, (double)w[moves[i]]);
+    if (largest == 0.0) return -2;
+    double total = 0.0;
+    for (int i = 0; i < n; ++i) total += (double)w[moves[i]] / largest;
+    node->edges = storage;
+    node->nedges = n;
+    for (int i = 0; i < n; ++i) {
+        storage[i].move = moves[i];
+        storage[i].prior = ((double)w[moves[i]] / largest) / total;
+        storage[i].visits = 0;
+        storage[i].value_sum = 0.0;
+        storage[i].child = -1;
+    }
+    node->expanded = 1;
+    *leaf_value = (double)v;
+    return 0;
+}
+
+/* PUCT.cpp:118-142 */
+static int select_edge(const o_node* node, double c_puct) {
+    double parent_scale = sqrt((double)node->visits);
+    int best = 0;
+    double best_score = -INFINITY;
+    for (int i = 0; i < node->nedges; ++i) {
+        const o_edge* e = &node->edges[i];
+        double exploration = e->prior * parent_scale / (1.0 + (double)e->visits);
+        double score = c_puct >= 1.0 ? edge_value(e) / c_puct + exploration : edge_value(e) + c_puct * exploration;
+        const o_edge* prev = &node->edges[best];
+        if (score > best_score ||
+            (score == best_score && (e->prior > prev->prior || (e->prior == prev->prior && e->move < prev->move)))) {
+            best = i;
+            best_score = score;
+        }
+    }
+    return best;
+}
+
+static double terminal_value(const int32_t* rec) { return rec[GK_WINNER] == rec[GK_ACTOR] ? 1.0 : -1.0; }
+
+int gko_puct_search(const int32_t* root, int simulations, double c_puct, int32_t* visits, double* priors,
+                    int32_t* stats, double* values) {
+    for (int a = 0; a < GK_ACTIONS; ++a) {
+        visits[a] = 0;
+        priors[a] = 0.0;
+    }
+    stats[0] = -1;
+    stats[1] = 0;
+    stats[2] = 0;
+    stats[3] = 0;
+    values[1] = 0.0;
+    if (root[GK_REASON] != GK_NONE) {
+        values[0] = terminal_value(root);
+        return 0;
+    }
+    int capacity = simulations + 1;
+    o_node* tree = (o_node*)calloc((size_t)capacity, sizeof(o_node));
+    o_edge* pool = (o_edge*)malloc((size_t)capacity * GK_ACTIONS * sizeof(o_edge));
+    int* path_node = (int*)malloc((size_t)capacity * sizeof(int));
+    int* path_edge = (int*)malloc((size_t)capacity * sizeof(int));
+    int size = 1, status = 0;
+    int64_t evaluations = 0;
+    double ignored;
+    tree[0].player = root[GK_ACTOR];
+    if (expand(&tree[0], root, pool, &ignored, &evaluations) != 0) {
+        status = -2;
+        goto done;
+    }
+    int64_t completed = 0;
+    for (int iteration = 0; iteration < simulations; ++iteration) {
+        int32_t sim[GK_STATE_WIDTH];
+        memcpy(sim, root, sizeof sim);
+        int node = 0, depth = 0;
+        double leaf_value = 0.0;
+        for (;;) {
+            if (sim[GK_REASON] != GK_NONE) {
+                leaf_value = terminal_value(sim);
+                break;
+            }
+            if (!tree[node].expanded) {
+                if (expand(&tree[node], sim, pool + (size_t)node * GK_ACTIONS, &leaf_value, &evaluations) != 0) {
+                    status = -2;
+                    goto done;
+                }
+                break;
+            }
+            int e = select_edge(&tree[node], c_puct);
+            o_edge* edge = &tree[node].edges[e];
+            if (!gko_play(sim, edge->move)) {
+                status = -1;
+                goto done;
+            }
+            path_node[depth] = node;
+            path_edge[depth] = e;
+            ++depth;
+            if (edge->child < 0) {
+                if (size >= capacity) {
+                    status = -1;
+                    goto done;
+                }
+                edge->child = size;
+                tree[size].player = sim[GK_ACTOR];
+                ++size;
+            }
+            node = edge->child;
+        }
+        ++tree[0].visits;
+        for (int d = 0; d < depth; ++d) {
+            o_edge* edge = &tree[path_node[d]].edges[path_edge[d]];
+            double value = tree[path_node[d]].player == sim[GK_ACTOR] ? leaf_value : -leaf_value;
+            ++edge->visits;
+            edge->value_sum += value;
+            ++tree[edge->child].visits;
+        }
+        ++completed;
+    }
+    {
+        double root_sum = 0.0;
+        const o_edge* best = NULL;
+        for (int i = 0; i < tree[0].nedges; ++i) {
+            const o_edge* e = &tree[0].edges[i];
+            visits[e->move] = (int32_t)e->visits;
+            priors[e->move] = e->prior;
+            root_sum += e->value_sum;
+            if (best == NULL) {
+                best = e;
+                continue;
+            }
+            /* PUCT.cpp:151-157 over moves sorted by index (edge order). */
+            int better;
+            if (e->visits != best->visits) better = e->visits > best->visits;
+            else if (edge_value(e) != edge_value(best)) better = edge_value(e) > edge_value(best);
+            else if (e->prior != best->prior) better = e->prior > best->prior;
+            else better = e->move < best->move;
+            if (better) best = e;
+        }
+        stats[0] = best ? best->move : -1;
+        stats[1] = (int32_t)completed;
+        stats[2] = size;
+        stats[3] = (int32_t)evaluations;
+        values[0] = root_sum / (double)completed;
+        values[1] = best ? edge_value(best) : 0.0;
+    }
+done:
+    free(tree);
+    free(pool);
+    free(path_node);
+    free(path_edge);
+    return status;
+}
+
+typedef struct {
+    const int32_t* recs;
+    int64_t begin, end;
+    int simulations;
+    double c_puct;
+    int32_t* visits;
+    int32_t* best;
+    double* root_values;
+    int status;
+} batch_job;
+
+static void* batch_worker(void* arg) {
+    batch_job* job = (batch_job*)arg;
+    double priors[GK_ACTIONS];
+    for (int64_t i = job->begin; i < job->end; ++i) {
+        int32_t stats[4];
+        double values[2];
+        int s = gko_puct_search(job->recs + i * GK_STATE_WIDTH, job->simulations, job->c_puct,
+                                job->visits + i * GK_ACTIONS, priors, stats, values);
+        if (s != 0) job->status = s;
+        job->best[i] = stats[0];
+        job->root_values[i] = values[0];
+    }
+    return NULL;
+}
+
+int gko_puct_search_batch(const int32_t* recs, int64_t n, int simulations, double c_puct, int32_t* visits,
+                          int32_t* best, double* root_values, int threads) {
+    if (threads < 1) threads = 1;
+    if (threads > 256) threads = 256;
+    pthread_t tid[256];
+    batch_job jobs[256];
+    int64_t per = (n + threads - 1) / threads;
+    int started = 0;
+    for (int t = 0; t < threads; ++t) {
+        int64_t b = (int64_t)t * per, e = b + per < n ? b + per : n;
+        if (b >= e) break;
+        jobs[t] = (batch_job){recs, b, e, simulations, c_puct, visits, best, root_values, 0};
+        pthread_create(&tid[t], NULL, batch_worker, &jobs[t]);
+        ++started;
+    }
+    int status = 0;
+    for (int t = 0; t < started; ++t) {
+        pthread_join(tid[t], NULL);
+        if (jobs[t].status) status = jobs[t].status;
+    }
+    return status;
+}

@@ -1,0 +1,51 @@
+/*
+ * gk_oracle.h - CPU oracle (test infrastructure only).
+ *
+ * A plain-C restatement of the reference rules, encoder and PUCT search,
+ * operating on the int32[170] wire record. It is the checker for the CUDA
+ * path: only tests, the smoke check and the benchmark's CPU-baseline leg use
+ * it. Nothing in the product links or calls it.
+ *
+ * Parity is pinned: tests compare it with the reference C++ engine compiled
+ * from its own sources (oracle/_ref) and with golden vectors taken from the
+ * reference's tests (tests/golden).
+ */
+#ifndef GK_ORACLE_H
+#define GK_ORACLE_H
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+void gko_initial(int32_t* rec, int neutral_cell);
+int gko_legal(const int32_t* rec, int action);
+int gko_play(int32_t* rec, int action);
+void gko_score(const int32_t* rec, int* black, int* white);
+void gko_encode(const int32_t* rec, float* features, uint8_t* mask);
+void gko_play_batch(int32_t* recs, const int32_t* actions, uint8_t* accepted, int64_t n);
+void gko_encode_batch(const int32_t* recs, float* features, uint8_t* masks, int64_t n);
+
+/* Uniform-random playout: info = {winner, cpp_reason, score_black, score_white, plies}. */
+void gko_random_playout(uint64_t seed, uint64_t game, int neutral_cell, int8_t* board, int32_t* info);
+void gko_random_playouts(uint64_t seed, uint64_t first_game, int64_t n, int neutral_cell, int8_t* boards,
+                         int32_t* infos);
+/* Random mid-game position generator: k ~ U[0,60] uniform legal moves, non-terminal. */
+void gko_gen_position(uint64_t seed, uint64_t index, int32_t* rec);
+void gko_gen_positions(uint64_t seed, uint64_t first, int64_t n, int32_t* recs);
+
+void gko_eval(const int32_t* rec, float* weights, float* value);
+
+/* PUCT search with the injected evaluator and no root noise.
+ * Outputs: visits[82], priors[82] (0 for illegal), stats = {best_action,
+ * simulations, nodes, network_evaluations}, values = {root_value, best_value}. */
+int gko_puct_search(const int32_t* rec, int simulations, double c_puct, int32_t* visits, double* priors,
+                    int32_t* stats, double* values);
+int gko_puct_search_batch(const int32_t* recs, int64_t n, int simulations, double c_puct, int32_t* visits,
+                          int32_t* best, double* root_values, int threads);
+
+#ifdef __cplusplus
+}
+#endif
+#endif

@@ -1,0 +1,261 @@
+"""ctypes bindings for the CPU checkers (TEST INFRASTRUCTURE ONLY).
+
+``Oracle`` loads ``oracle/_build/libgkoracle.so`` (the plain-C restatement in
+``oracle/gk_oracle.c``). ``Reference`` loads ``oracle/_ref/libgkref.so`` (the
+reference C++ engine compiled from its own sources plus
+``oracle/ref_harness.cpp``); it exists only where it was built.
+
+Only ``tests/``, ``__graft_entry__.smoke()`` and ``bench.py``'s CPU-baseline
+leg may import this module. The product never does.
+"""
+
+from __future__ import annotations
+
+import ctypes
+import os
+import subprocess
+from pathlib import Path
+
+import numpy as np
+
+HERE = Path(__file__).resolve().parent
+ORACLE_SO = HERE / "_build" / "libgkoracle.so"
+REF_SO = HERE / "_ref" / "libgkref.so"
+REFERENCE_ROOT = Path(os.environ.get("GK_REFERENCE_ROOT", "/root/reference"))
+
+STATE_WIDTH = 170
+ACTIONS = 82
+FEATURES = 810
+
+_i32p = np.ctypeslib.ndpointer(dtype=np.int32, flags="C_CONTIGUOUS")
+_u8p = np.ctypeslib.ndpointer(dtype=np.uint8, flags="C_CONTIGUOUS")
+_i8p = np.ctypeslib.ndpointer(dtype=np.int8, flags="C_CONTIGUOUS")
+_f32p = np.ctypeslib.ndpointer(dtype=np.float32, flags="C_CONTIGUOUS")
+_f64p = np.ctypeslib.ndpointer(dtype=np.float64, flags="C_CONTIGUOUS")
+_u64 = ctypes.c_uint64
+_i64 = ctypes.c_int64
+_int = ctypes.c_int
+
+
+def build_oracle(force: bool = False) -> Path:
+    """Compile the plain-C oracle with gcc (seconds) if it is missing."""
+    if force or not ORACLE_SO.exists():
+        subprocess.run(["make", "-s", "-C", str(HERE), "all"], check=True)
+    return ORACLE_SO
+
+
+def build_reference(force: bool = False) -> Path | None:
+    """Compile the reference engine from its sources when they are present."""
+    if REF_SO.exists() and not force:
+        return REF_SO
+    if not (REFERENCE_ROOT / "engine" / "src" / "State.cpp").exists():
+        return None
+    subprocess.run(["make", "-s", "-C", str(HERE), "ref", f"REF={REFERENCE_ROOT}"], check=True)
+    return REF_SO
+
+
+def _bind(lib, name, args, res=None):
+    fn = getattr(lib, name)
+    fn.argtypes = args
+    fn.restype = res
+    return fn
+
+
+class Oracle:
+    """The plain-C restatement of rules, encoder, generators and PUCT."""
+
+    def __init__(self):
+        self.lib = ctypes.CDLL(str(build_oracle()))
+        L = self.lib
+        _bind(L, "gko_initial", [_i32p, _int])
+        _bind(L, "gko_play", [_i32p, _int], _int)
+        _bind(L, "gko_legal", [_i32p, _int], _int)
+        _bind(L, "gko_play_batch", [_i32p, _i32p, _u8p, _i64])
+        _bind(L, "gko_encode_batch", [_i32p, _f32p, _u8p, _i64])
+        _bind(L, "gko_random_playouts", [_u64, _u64, _i64, _int, _i8p, _i32p])
+        _bind(L, "gko_gen_positions", [_u64, _u64, _i64, _i32p])
+        _bind(L, "gko_eval", [_i32p, _f32p, _f32p])
+        _bind(L, "gko_puct_search", [_i32p, _int, ctypes.c_double, _i32p, _f64p, _i32p, _f64p], _int)
+        _bind(L, "gko_puct_search_batch", [_i32p, _i64, _int, ctypes.c_double, _i32p, _i32p, _f64p, _int], _int)
+
+    def initial(self, n: int = 1, neutral: int = 40) -> np.ndarray:
+        recs = np.zeros((n, STATE_WIDTH), dtype=np.int32)
+        for i in range(n):
+            row = np.zeros(STATE_WIDTH, dtype=np.int32)
+            self.lib.gko_initial(row, neutral)
+            recs[i] = row
+        return recs
+
+    def play(self, recs: np.ndarray, actions) -> np.ndarray:
+        """In-place batched transition; returns accepted flags (uint8)."""
+        recs = np.ascontiguousarray(recs, dtype=np.int32)
+        actions = np.ascontiguousarray(actions, dtype=np.int32)
+        accepted = np.zeros(len(recs), dtype=np.uint8)
+        self.lib.gko_play_batch(recs, actions, accepted, len(recs))
+        return recs, accepted
+
+    def encode(self, recs: np.ndarray):
+        recs = np.ascontiguousarray(recs, dtype=np.int32)
+        features = np.zeros((len(recs), FEATURES), dtype=np.float32)
+        masks = np.zeros((len(recs), ACTIONS), dtype=np.uint8)
+        self.lib.gko_encode_batch(recs, features, masks, len(recs))
+        return features.reshape(len(recs), 10, 9, 9), masks.astype(bool)
+
+    def random_playouts(self, seed: int, n: int, first: int = 0, neutral: int = 40):
+        boards = np.zeros((n, 81), dtype=np.int8)
+        infos = np.zeros((n, 5), dtype=np.int32)
+        self.lib.gko_random_playouts(seed, first, n, neutral, boards, infos)
+        return boards, infos
+
+    def gen_positions(self, seed: int, n: int, first: int = 0) -> np.ndarray:
+        recs = np.zeros((n, STATE_WIDTH), dtype=np.int32)
+        self.lib.gko_gen_positions(seed, first, n, recs)
+        return recs
+
+    def evaluate(self, rec: np.ndarray):
+        w = np.zeros(ACTIONS, dtype=np.float32)
+        v = np.zeros(1, dtype=np.float32)
+        self.lib.gko_eval(np.ascontiguousarray(rec, dtype=np.int32), w, v)
+        return w, float(v[0])
+
+    def puct(self, rec: np.ndarray, simulations: int, c_puct: float = 1.5):
+        visits = np.zeros(ACTIONS, dtype=np.int32)
+        priors = np.zeros(ACTIONS, dtype=np.float64)
+        stats = np.zeros(4, dtype=np.int32)
+        values = np.zeros(2, dtype=np.float64)
+        status = self.lib.gko_puct_search(np.ascontiguousarray(rec, dtype=np.int32), simulations, c_puct,
+                                          visits, priors, stats, values)
+        if status != 0:
+            raise RuntimeError(f"oracle PUCT failed ({status})")
+        return dict(visits=visits, priors=priors, best=int(stats[0]), simulations=int(stats[1]),
+                    nodes=int(stats[2]), evaluations=int(stats[3]), root_value=float(values[0]),
+                    best_value=float(values[1]))
+
+    def puct_batch(self, recs: np.ndarray, simulations: int, c_puct: float = 1.5, threads: int = 1):
+        recs = np.ascontiguousarray(recs, dtype=np.int32)
+        n = len(recs)
+        visits = np.zeros((n, ACTIONS), dtype=np.int32)
+        best = np.zeros(n, dtype=np.int32)
+        roots = np.zeros(n, dtype=np.float64)
+        status = self.lib.gko_puct_search_batch(recs, n, simulations, c_puct, visits, best, roots, threads)
+        if status != 0:
+            raise RuntimeError(f"oracle PUCT failed ({status})")
+        return visits, best, roots
+
+
+class Reference:
+    """Driver for the reference C++ engine compiled from its own sources."""
+
+    def __init__(self):
+        path = build_reference()
+        if path is None:
+            raise FileNotFoundError("the reference engine was not built (oracle/_ref)")
+        self.lib = ctypes.CDLL(str(path))
+        L = self.lib
+        vp = ctypes.c_void_p
+        _bind(L, "gkr_state_new", [_int], vp)
+        _bind(L, "gkr_state_from_board", [_i32p, _int], vp)
+        _bind(L, "gkr_state_copy", [vp], vp)
+        _bind(L, "gkr_state_free", [vp])
+        _bind(L, "gkr_state_play", [vp, _int], _int)
+        _bind(L, "gkr_state_record", [vp, _i32p])
+        _bind(L, "gkr_state_score", [vp, _i32p])
+        _bind(L, "gkr_state_legal", [vp, _i32p], _int)
+        _bind(L, "gkr_state_encode", [vp, _f32p, _u8p])
+        _bind(L, "gkr_random_playouts", [_u64, _u64, _i64, _int, _int, _int, _i8p, _i32p])
+        _bind(L, "gkr_gen_positions", [_u64, _u64, _i64, _int, _i32p])
+        _bind(L, "gkr_gen_position_state", [_u64, _u64], vp)
+        _bind(L, "gkr_encode_positions", [_u64, _u64, _i64, _int, _f32p, _u8p])
+        _bind(L, "gkr_puct_search", [vp, _int, ctypes.c_double, _i32p, _f64p, _i32p, _f64p], _int)
+        _bind(L, "gkr_puct_positions", [_u64, _u64, _i64, _int, ctypes.c_double, _int, _i32p, _i32p], _int)
+
+    def random_playouts(self, seed, n, first=0, neutral=40, fast=False, threads=1):
+        boards = np.zeros((n, 81), dtype=np.int8)
+        infos = np.zeros((n, 5), dtype=np.int32)
+        self.lib.gkr_random_playouts(seed, first, n, neutral, int(fast), threads, boards, infos)
+        return boards, infos
+
+    def gen_positions(self, seed, n, first=0, threads=1):
+        recs = np.zeros((n, STATE_WIDTH), dtype=np.int32)
+        self.lib.gkr_gen_positions(seed, first, n, threads, recs)
+        return recs
+
+    def encode_positions(self, seed, n, first=0, threads=1):
+        features = np.zeros((n, FEATURES), dtype=np.float32)
+        masks = np.zeros((n, ACTIONS), dtype=np.uint8)
+        self.lib.gkr_encode_positions(seed, first, n, threads, features, masks)
+        return features.reshape(n, 10, 9, 9), masks.astype(bool)
+
+    def puct_positions(self, seed, n, simulations, c_puct=1.5, first=0, threads=1):
+        visits = np.zeros((n, ACTIONS), dtype=np.int32)
+        best = np.zeros(n, dtype=np.int32)
+        status = self.lib.gkr_puct_positions(seed, first, n, simulations, c_puct, threads, visits, best)
+        if status != 0:
+            raise RuntimeError("reference PUCT failed")
+        return visits, best
+
+
+class RefState:
+    """A reference ``kingdom::State`` held through the harness."""
+
+    def __init__(self, ref: Reference, handle):
+        if not handle:
+            raise ValueError("the reference rejected this position")
+        self.ref, self.h = ref, handle
+
+    @classmethod
+    def initial(cls, ref, neutral=40):
+        return cls(ref, ref.lib.gkr_state_new(neutral))
+
+    @classmethod
+    def from_board(cls, ref, cells, to_play):
+        cells = np.ascontiguousarray(cells, dtype=np.int32).reshape(81)
+        return cls(ref, ref.lib.gkr_state_from_board(cells, int(to_play)))
+
+    @classmethod
+    def generated(cls, ref, seed, index):
+        return cls(ref, ref.lib.gkr_gen_position_state(seed, index))
+
+    def copy(self):
+        return RefState(self.ref, self.ref.lib.gkr_state_copy(self.h))
+
+    def __del__(self):
+        try:
+            self.ref.lib.gkr_state_free(self.h)
+        except Exception:
+            pass
+
+    def play(self, action: int) -> bool:
+        return bool(self.ref.lib.gkr_state_play(self.h, int(action)))
+
+    def record(self) -> np.ndarray:
+        rec = np.zeros(STATE_WIDTH, dtype=np.int32)
+        self.ref.lib.gkr_state_record(self.h, rec)
+        return rec
+
+    def score(self):
+        out = np.zeros(2, dtype=np.int32)
+        self.ref.lib.gkr_state_score(self.h, out)
+        return int(out[0]), int(out[1])
+
+    def legal(self):
+        out = np.zeros(ACTIONS, dtype=np.int32)
+        n = self.ref.lib.gkr_state_legal(self.h, out)
+        return out[:n].tolist()
+
+    def encode(self):
+        features = np.zeros(FEATURES, dtype=np.float32)
+        mask = np.zeros(ACTIONS, dtype=np.uint8)
+        self.ref.lib.gkr_state_encode(self.h, features, mask)
+        return features.reshape(10, 9, 9), mask.astype(bool)
+
+    def puct(self, simulations, c_puct=1.5):
+        visits = np.zeros(ACTIONS, dtype=np.int32)
+        priors = np.zeros(ACTIONS, dtype=np.float64)
+        stats = np.zeros(4, dtype=np.int32)
+        values = np.zeros(2, dtype=np.float64)
+        if self.ref.lib.gkr_puct_search(self.h, simulations, c_puct, visits, priors, stats, values) != 0:
+            raise RuntimeError("reference PUCT failed")
+        return dict(visits=visits, priors=priors, best=int(stats[0]), simulations=int(stats[1]),
+                    nodes=int(stats[2]), evaluations=int(stats[3]), root_value=float(values[0]),
+                    best_value=float(values[1]))
