@@ -1,0 +1,260 @@
+// gk_device.cuh - device-side rules on register-resident 96-bit bitboards.
+//
+// Every function here runs in one thread on one packed state (gk_bits, 64 B).
+// The algorithms are bitboard restatements of the reference rules:
+//   State::play            engine/src/State.cpp:92-167  (gpu_play, gpu_rules.py:185-252)
+//   Board::territory       engine/src/Board.cpp:149-198 (gpu_claim_territory, gpu_rules.py:124-172)
+//   legal placements       gpu_legal, gpu_rules.py:174-183
+// Flood fills are iterated 4-neighbour dilations masked by the passable set;
+// the padding column (bit r*10+9) is outside every mask, so horizontal shifts
+// need no column masks.
+#pragma once
+
+#include <cstdint>
+
+#include "../../include/gk_common.h"
+
+namespace gk {
+
+__device__ __forceinline__ gk_b96 lowest_bit(gk_b96 a) {
+    gk_b96 r = gk_b(0u, 0u, 0u);
+    if (a.w[0]) r.w[0] = a.w[0] & (0u - a.w[0]);
+    else if (a.w[1]) r.w[1] = a.w[1] & (0u - a.w[1]);
+    else r.w[2] = a.w[2] & (0u - a.w[2]);
+    return r;
+}
+
+// Index of the j-th (0-based) set bit of a 96-bit value, j < popcount.
+__device__ __forceinline__ int select_bit(gk_b96 a, int j) {
+    int word = 0;
+    int c0 = __popc(a.w[0]);
+    uint32_t v = a.w[0];
+    if (j >= c0) {
+        j -= c0;
+        int c1 = __popc(a.w[1]);
+        if (j >= c1) {
+            j -= c1;
+            v = a.w[2];
+            word = 2;
+        } else {
+            v = a.w[1];
+            word = 1;
+        }
+    }
+    // Binary search inside the 32-bit word.
+    int base = 0;
+#pragma unroll
+    for (int width = 16; width >= 1; width >>= 1) {
+        uint32_t lowmask = (width == 32) ? 0xffffffffu : ((1u << width) - 1u);
+        int c = __popc(v & lowmask);
+        if (j >= c) {
+            j -= c;
+            v >>= width;
+            base += width;
+        }
+    }
+    return word * 32 + base;
+}
+
+__device__ __forceinline__ gk_b96 empty_cells(const gk_bits& s) {
+    gk_b96 occ = gk_or(gk_or(gk_get(&s, GK_PLANE_BLACK), gk_get(&s, GK_PLANE_WHITE)), gk_get(&s, GK_PLANE_NEUTRAL));
+    return gk_andnot(gk_valid(), occ);
+}
+
+// Legal placements of the player to move (not including pass); empty if finished.
+__device__ __forceinline__ gk_b96 legal_placements(const gk_bits& s) {
+    if (gk_reason(&s) != GK_NONE) return gk_b(0u, 0u, 0u);
+    int actor = gk_actor(&s);
+    if (gk_stock(&s, actor) <= 0) return gk_b(0u, 0u, 0u);
+    gk_b96 owned = gk_or(gk_get(&s, GK_PLANE_OWN_BLACK), gk_get(&s, GK_PLANE_OWN_WHITE));
+    return gk_andnot(empty_cells(s), owned);
+}
+
+// Board::territory + State::claim_territory on bitboards. A territory for
+// player P is an empty component that (1) has no opponent-adjacent cell (the
+// reference flood passes through enemy stones and rejects such components),
+// (2) touches a P stone, (3) does not touch all four edges. Ownership is sticky.
+__device__ __forceinline__ void claim_territory(gk_bits& s) {
+    const gk_b96 black = gk_get(&s, GK_PLANE_BLACK), white = gk_get(&s, GK_PLANE_WHITE);
+    const gk_b96 E = empty_cells(s);
+    const gk_b96 near_black = gk_flood(E, gk_and(E, gk_neighbours(black)));
+    const gk_b96 near_white = gk_flood(E, gk_and(E, gk_neighbours(white)));
+    gk_b96 pb = gk_andnot(near_black, near_white);
+    gk_b96 pw = gk_andnot(near_white, near_black);
+    const gk_b96 C = gk_or(pb, pw);
+    if (!gk_any(C)) return;
+    // Components touching all four edges: nested floods by edge.
+    gk_b96 t = gk_flood(C, gk_and(C, gk_b(GK_ROW0_0, 0u, 0u)));
+    if (gk_any(t)) t = gk_flood(t, gk_and(t, gk_b(0u, 0u, GK_ROW8_2)));
+    if (gk_any(t)) t = gk_flood(t, gk_and(t, gk_b(GK_COL0_0, GK_COL0_1, GK_COL0_2)));
+    if (gk_any(t)) t = gk_flood(t, gk_and(t, gk_b(GK_COL8_0, GK_COL8_1, GK_COL8_2)));
+    pb = gk_andnot(pb, t);
+    pw = gk_andnot(pw, t);
+    const gk_b96 ob = gk_get(&s, GK_PLANE_OWN_BLACK), ow = gk_get(&s, GK_PLANE_OWN_WHITE);
+    const gk_b96 unowned = gk_andnot(gk_valid(), gk_or(ob, ow));
+    gk_put(&s, GK_PLANE_OWN_BLACK, gk_or(ob, gk_and(pb, unowned)));
+    gk_put(&s, GK_PLANE_OWN_WHITE, gk_or(ow, gk_and(pw, unowned)));
+}
+
+// One transition; returns false (state unchanged) for rejected actions.
+__device__ __forceinline__ bool play(gk_bits& s, int action) {
+    const uint32_t meta = s.w[15];
+    if (((meta >> GK_META_REASON_SHIFT) & 3u) != GK_NONE) return false;
+    if (action < 0 || action >= GK_ACTIONS) return false;
+    const int actor = (int)(meta & 3u);
+    const int enemy = 3 - actor;
+    int bstock = (int)((meta >> GK_META_BSTOCK_SHIFT) & 63u);
+    int wstock = (int)((meta >> GK_META_WSTOCK_SHIFT) & 63u);
+    int passes = (int)((meta >> GK_META_PASSES_SHIFT) & 3u);
+    if (action == GK_PASS) {
+        ++passes;
+        int reason = GK_NONE, winner = gk_winner(&s);
+        if (passes == 2) {
+            const gk_b96 E = empty_cells(s);
+            const int b = gk_popc(gk_and(E, gk_get(&s, GK_PLANE_OWN_BLACK)));
+            const int w = gk_popc(gk_and(E, gk_get(&s, GK_PLANE_OWN_WHITE)));
+            reason = GK_TWO_PASSES;
+            winner = b - w >= 3 ? 1 : 2;
+        }
+        const int captured = reason == GK_NONE ? gk_captured(&s) : 0;
+        s.w[15] = gk_pack_meta(enemy, bstock, wstock, passes, reason, winner, captured) |
+                  (meta & 0xf8000000u);
+        return true;
+    }
+    const int bit = gk_cell_bit(action);
+    const gk_b96 here = gk_single(bit);
+    gk_b96 black = gk_get(&s, GK_PLANE_BLACK), white = gk_get(&s, GK_PLANE_WHITE);
+    const gk_b96 neutral = gk_get(&s, GK_PLANE_NEUTRAL);
+    const gk_b96 owned = gk_or(gk_get(&s, GK_PLANE_OWN_BLACK), gk_get(&s, GK_PLANE_OWN_WHITE));
+    const int stock = actor == 1 ? bstock : wstock;
+    if (gk_test(gk_or(gk_or(black, white), gk_or(neutral, owned)), bit) || stock <= 0) return false;
+    gk_b96 own = actor == 1 ? black : white;
+    gk_b96 opp = actor == 1 ? white : black;
+    own = gk_or(own, here);
+    const gk_b96 E = gk_andnot(gk_valid(), gk_or(gk_or(own, opp), neutral));
+    // Enemy groups adjacent to the new stone with no liberty are captured.
+    gk_b96 captured = gk_b(0u, 0u, 0u);
+    gk_b96 pending = gk_and(gk_neighbours(here), opp);
+    while (gk_any(pending)) {
+        const gk_b96 group = gk_flood(opp, lowest_bit(pending));
+        pending = gk_andnot(pending, group);
+        if (!gk_any(gk_and(gk_neighbours(group), E))) captured = gk_or(captured, group);
+    }
+    const int captured_count = gk_popc(captured);
+    bool suicide = false;
+    if (captured_count == 0) {
+        const gk_b96 group = gk_flood(own, here);
+        suicide = !gk_any(gk_and(gk_neighbours(group), E));
+    }
+    if (actor == 1) --bstock;
+    else --wstock;
+    opp = gk_andnot(opp, captured);
+    gk_put(&s, actor == 1 ? GK_PLANE_BLACK : GK_PLANE_WHITE, own);
+    gk_put(&s, actor == 1 ? GK_PLANE_WHITE : GK_PLANE_BLACK, opp);
+    int reason = GK_NONE, winner = gk_winner(&s), captured_field = gk_captured(&s);
+    if (captured_count > 0) {
+        reason = GK_CAPTURE;
+        winner = actor;
+        captured_field = captured_count;
+    } else if (suicide) {
+        reason = GK_SUICIDE;
+        winner = enemy;
+        captured_field = 0;
+    }
+    s.w[15] = gk_pack_meta(enemy, bstock, wstock, 0, reason, winner, captured_field) | (meta & 0xf8000000u);
+    if (reason == GK_NONE) claim_territory(s);
+    return true;
+}
+
+__device__ __forceinline__ gk_bits initial_bits(int neutral_cell) {
+    gk_bits s;
+#pragma unroll
+    for (int i = 0; i < 16; ++i) s.w[i] = 0u;
+    if (neutral_cell >= 0 && neutral_cell < GK_CELLS) gk_put(&s, GK_PLANE_NEUTRAL, gk_single(gk_cell_bit(neutral_cell)));
+    s.w[15] = gk_pack_meta(1, GK_STONES, GK_STONES, 0, GK_NONE, 0, 0);
+    return s;
+}
+
+// Wire record (int32[170], possibly in shared memory) -> packed state.
+__device__ __forceinline__ gk_bits pack_record(const int32_t* rec) {
+    gk_bits s;
+#pragma unroll
+    for (int i = 0; i < 16; ++i) s.w[i] = 0u;
+    for (int i = 0; i < GK_CELLS; ++i) {
+        const int bit = gk_cell_bit(i);
+        const uint32_t m = 1u << (bit & 31);
+        const int word = bit >> 5;
+        const int c = rec[i];
+        if (c == 1) s.w[word] |= m;
+        else if (c == 2) s.w[3 + word] |= m;
+        else if (c == 3) s.w[6 + word] |= m;
+        const int o = rec[GK_CELLS + i];
+        if (o == 1) s.w[9 + word] |= m;
+        else if (o == 2) s.w[12 + word] |= m;
+    }
+    s.w[15] = gk_pack_meta(rec[GK_ACTOR] & 3, rec[GK_BLACK_STOCK] & 63, rec[GK_WHITE_STOCK] & 63,
+                           rec[GK_PASSES] & 3, rec[GK_REASON] & 3, rec[GK_WINNER] & 3, rec[GK_CAPTURED] & 127);
+    return s;
+}
+
+// True when the record's fields lie inside the ranges the packed state holds.
+__device__ __forceinline__ bool record_in_range(const int32_t* rec) {
+    bool ok = true;
+    for (int i = 0; i < GK_CELLS; ++i) {
+        ok &= (unsigned)rec[i] <= 3u;
+        ok &= (unsigned)rec[GK_CELLS + i] <= 2u;
+    }
+    ok &= rec[GK_ACTOR] == 1 || rec[GK_ACTOR] == 2;
+    ok &= (unsigned)rec[GK_BLACK_STOCK] <= 41u && (unsigned)rec[GK_WHITE_STOCK] <= 41u;
+    ok &= (unsigned)rec[GK_PASSES] <= 2u && (unsigned)rec[GK_REASON] <= 3u;
+    ok &= (unsigned)rec[GK_WINNER] <= 2u && (unsigned)rec[GK_CAPTURED] <= 81u;
+    return ok;
+}
+
+// Packed state -> wire record fields 0..168 (169, reserved, is left alone).
+__device__ __forceinline__ void unpack_record(const gk_bits& s, int32_t* rec) {
+    for (int i = 0; i < GK_CELLS; ++i) {
+        const int bit = gk_cell_bit(i);
+        const int word = bit >> 5, sh = bit & 31;
+        const int b = (s.w[word] >> sh) & 1u, w = (s.w[3 + word] >> sh) & 1u, n = (s.w[6 + word] >> sh) & 1u;
+        rec[i] = b ? 1 : w ? 2 : n ? 3 : 0;
+        const int ob = (s.w[9 + word] >> sh) & 1u, ow = (s.w[12 + word] >> sh) & 1u;
+        rec[GK_CELLS + i] = ob ? 1 : ow ? 2 : 0;
+    }
+    rec[GK_ACTOR] = gk_actor(&s);
+    rec[GK_BLACK_STOCK] = gk_stock(&s, 1);
+    rec[GK_WHITE_STOCK] = gk_stock(&s, 2);
+    rec[GK_PASSES] = gk_passes(&s);
+    rec[GK_REASON] = gk_reason(&s);
+    rec[GK_WINNER] = gk_winner(&s);
+    rec[GK_CAPTURED] = gk_captured(&s);
+}
+
+// Actor-relative planes used by the encoder and by the network's stem.
+struct EncodePlanes {
+    gk_b96 own, enemy, neutral, own_terr, enemy_terr, legal;
+    float black_to_play, own_remaining, enemy_remaining, passes;
+    bool pass_legal;
+};
+
+__device__ __forceinline__ EncodePlanes encode_planes(const gk_bits& s) {
+    EncodePlanes p;
+    const int actor = gk_actor(&s);
+    const gk_b96 black = gk_get(&s, GK_PLANE_BLACK), white = gk_get(&s, GK_PLANE_WHITE);
+    const gk_b96 ob = gk_get(&s, GK_PLANE_OWN_BLACK), ow = gk_get(&s, GK_PLANE_OWN_WHITE);
+    p.own = actor == 1 ? black : white;
+    p.enemy = actor == 1 ? white : black;
+    p.neutral = gk_get(&s, GK_PLANE_NEUTRAL);
+    p.own_terr = actor == 1 ? ob : ow;
+    p.enemy_terr = actor == 1 ? ow : ob;
+    p.legal = legal_placements(s);
+    p.pass_legal = gk_reason(&s) == GK_NONE;
+    p.black_to_play = actor == 1 ? 1.0f : 0.0f;
+    // float(double(k) / 41.0) as in mcts/src/BatchedPUCT.cpp:34-35.
+    p.own_remaining = (float)((double)gk_stock(&s, actor) / 41.0);
+    p.enemy_remaining = (float)((double)gk_stock(&s, 3 - actor) / 41.0);
+    p.passes = (float)gk_passes(&s) * 0.5f;
+    return p;
+}
+
+}  // namespace gk

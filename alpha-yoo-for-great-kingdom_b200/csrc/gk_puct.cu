@@ -1,0 +1,615 @@
+// gk_puct.cu - batched PUCT over structure-of-arrays trees in HBM.
+//
+// One warp owns one tree in select, expand/backup and finish: lanes score the
+// 82 edges of a node in parallel (3 per lane) and a warp argmax picks the
+// edge; the serial dependencies of the reference (the prior normaliser and the
+// root value are sums in action order) are evaluated in action order through
+// warp shuffles so every double is bit-identical to the reference search.
+//
+// Reference semantics followed:
+//   select            mcts/src/PUCT.cpp:118-142, python/kingdom_ai/gpu_puct.py:182-258
+//   expand (priors)   mcts/src/PUCT.cpp:53-86,  gpu_puct.py:277-324
+//   root noise mix    gpu_puct.py:308-321 (mix and renormalise as PUCT.cpp:88-116)
+//   backup            mcts/src/PUCT.cpp:228-236, gpu_puct.py:325-340
+//   finish            mcts/src/PUCT.cpp:246-267, gpu_puct.py:343-379
+// Double arithmetic goes through GK_DADD/GK_DMUL (__dadd_rn/__dmul_rn) so no
+// FMA contraction changes a bit; division and sqrt are IEEE round-to-nearest.
+#include <cuda_runtime.h>
+
+#include <cmath>
+#include <cstdint>
+
+#include "../../include/gk.h"
+#include "gk_device.cuh"
+#include "gk_launch.cuh"
+#include "gk_puct.cuh"
+
+namespace gk {
+
+constexpr unsigned kFull = 0xffffffffu;
+constexpr int kWarpsPerBlock = 4;
+
+__device__ __forceinline__ bool action_legal(const gk_b96& placements, bool pass_ok, int a) {
+    return a == GK_PASS ? pass_ok : gk_test(placements, a + a / 9) != 0;
+}
+
+__device__ __forceinline__ float terminal_value(const gk_bits& s) {
+    return gk_winner(&s) == gk_actor(&s) ? 1.0f : -1.0f;
+}
+
+// Sum of per-lane values v[k] (action a = lane + 32k) over selected actions in
+// increasing action order; every lane returns the same total.
+__device__ __forceinline__ double ordered_sum(const double (&v)[3], const bool (&use)[3]) {
+    double total = 0.0;
+    for (int a = 0; a < GK_ACTIONS; ++a) {
+        const int k = a >> 5, src = a & 31;
+        const double x = __shfl_sync(kFull, k == 0 ? v[0] : k == 1 ? v[1] : v[2], src);
+        const bool u = __shfl_sync(kFull, k == 0 ? use[0] : k == 1 ? use[1] : use[2], src);
+        if (u) total = GK_DADD(total, x);
+    }
+    return total;
+}
+
+__global__ void puct_begin_kernel(PuctView v, int64_t B, int C, const gk_bits* roots) {
+    for (int64_t t = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; t < B; t += (int64_t)gridDim.x * blockDim.x) {
+        const gk_bits r = roots[t];
+        const int64_t vtx = t * C;
+        const bool live = gk_reason(&r) == GK_NONE;
+        v.node_state[vtx] = r;
+        v.node_visits[vtx] = 0;
+        v.node_value[vtx] = 0.0f;
+        v.expanded[vtx] = 0;
+        v.node_count[t] = live ? 1 : 0;
+        v.leaf[t] = 0;
+        v.path_len[t] = 0;
+        v.sims[t] = 0;
+        v.evals[t] = 0;
+        v.errors[t] = 0u;
+        v.needs_eval[t] = live ? 1 : 0;
+        v.leaf_bits[t] = r;
+        v.leaf_value[t] = live ? 0.0f : terminal_value(r);
+    }
+}
+
+__global__ void __launch_bounds__(32 * kWarpsPerBlock) puct_select_kernel(PuctView v, int64_t B, int C, PuctOptions o) {
+    const int lane = threadIdx.x & 31;
+    const int64_t t = (blockIdx.x * (int64_t)blockDim.x + threadIdx.x) >> 5;
+    if (t >= B) return;
+    const int P = path_cap(C);
+    if (lane == 0) v.needs_eval[t] = 0;
+    if (v.node_count[t] == 0) {  // terminal root: no tree, value fixed at begin
+        if (lane == 0) v.path_len[t] = 0;
+        return;
+    }
+    const int64_t tbase = t * C;
+    int node = 0, depth = 0;
+    // The current node's state stays in registers; a child created during this
+    // pass is known to be unexpanded, so no lane reads memory another lane of
+    // this warp has just written.
+    gk_bits st = v.node_state[tbase];
+    bool fresh = false;
+    for (;;) {
+        const int64_t vtx = tbase + node;
+        if (gk_reason(&st) != GK_NONE) {
+            if (lane == 0) v.leaf_value[t] = terminal_value(st);
+            break;
+        }
+        if (fresh || !v.expanded[vtx]) {
+            if (lane == 0) {
+                v.needs_eval[t] = 1;
+                v.leaf_bits[t] = st;
+            }
+            break;
+        }
+        const double scale = sqrt((double)v.node_visits[vtx]);
+        const gk_b96 placements = legal_placements(st);
+        const int64_t ebase = vtx * GK_ACTIONS;
+        int best = -1;
+        double best_score = 0.0, best_prior = 0.0;
+        for (int a = lane; a < GK_ACTIONS; a += 32) {
+            if (!action_legal(placements, true, a)) continue;
+            const int n = v.visits[ebase + a];
+            const double p = v.prior[ebase + a];
+            double q;
+            if (n == 0) q = o.fpu_enabled != 0.0 ? GK_DSUB((double)v.node_value[vtx], o.fpu_reduction) : 0.0;
+            else q = v.wsum[ebase + a] / (double)n;
+            const double expl = GK_DMUL(p, scale) / GK_DADD(1.0, (double)n);
+            const double score = o.c_puct >= 1.0 ? GK_DADD(q / o.c_puct, expl) : GK_DADD(q, GK_DMUL(o.c_puct, expl));
+            if (best < 0 || score > best_score || (score == best_score && p > best_prior)) {
+                best = a;
+                best_score = score;
+                best_prior = p;
+            }
+        }
+        // Warp argmax: higher score, then higher prior, then lower action index.
+#pragma unroll
+        for (int off = 16; off; off >>= 1) {
+            const double os = __shfl_down_sync(kFull, best_score, off);
+            const double op = __shfl_down_sync(kFull, best_prior, off);
+            const int oa = __shfl_down_sync(kFull, best, off);
+            if (oa >= 0 && (best < 0 || os > best_score ||
+                            (os == best_score && (op > best_prior || (op == best_prior && oa < best))))) {
+                best = oa;
+                best_score = os;
+                best_prior = op;
+            }
+        }
+        best = __shfl_sync(kFull, best, 0);
+        if (best < 0 || depth >= P) {
+            if (lane == 0) {
+                v.errors[t] |= GK_ERR_CAPACITY;
+                v.leaf_value[t] = 0.0f;
+            }
+            break;
+        }
+        int ch = v.child[ebase + best];
+        if (ch < 0) {
+            gk_bits next = st;
+            const bool ok = play(next, best);
+            if (lane == 0) ch = v.node_count[t]++;
+            ch = __shfl_sync(kFull, ch, 0);
+            if (!ok || ch >= C) {
+                if (lane == 0) {
+                    v.errors[t] |= GK_ERR_CAPACITY;
+                    v.leaf_value[t] = 0.0f;
+                }
+                break;
+            }
+            if (lane == 0) {
+                v.node_state[tbase + ch] = next;
+                v.node_visits[tbase + ch] = 0;
+                v.node_value[tbase + ch] = 0.0f;
+                v.expanded[tbase + ch] = 0;
+                v.child[ebase + best] = ch;
+            }
+            st = next;
+            fresh = true;
+        } else {
+            st = v.node_state[tbase + ch];
+            fresh = false;
+        }
+        if (lane == 0) {
+            v.path_nodes[t * P + depth] = node;
+            v.path_actions[t * P + depth] = best;
+        }
+        ++depth;
+        node = ch;
+    }
+    if (lane == 0) {
+        v.leaf[t] = node;
+        v.path_len[t] = depth;
+    }
+}
+
+__global__ void __launch_bounds__(32 * kWarpsPerBlock) puct_expand_backup_kernel(PuctView v, int64_t B, int C,
+                                                                                 PuctOptions o, int backup) {
+    const int lane = threadIdx.x & 31;
+    const int64_t t = (blockIdx.x * (int64_t)blockDim.x + threadIdx.x) >> 5;
+    if (t >= B) return;
+    if (v.node_count[t] == 0) return;
+    const int P = path_cap(C);
+    const int node = v.leaf[t];
+    const int64_t vtx = t * C + node;
+    const gk_bits st = v.node_state[vtx];
+    float leaf_value = v.leaf_value[t];
+    if (v.needs_eval[t]) {
+        const gk_b96 placements = legal_placements(st);
+        const int64_t ebase = vtx * GK_ACTIONS, row = t * GK_ACTIONS;
+        bool bad = !(isfinite(leaf_value) && fabsf(leaf_value) <= 1.0f);
+        bool use[3];
+        double w[3], nz[3];
+        double largest = 0.0;
+        int legal_count = 0;
+#pragma unroll
+        for (int k = 0; k < 3; ++k) {
+            const int a = lane + 32 * k;
+            use[k] = a < GK_ACTIONS && action_legal(placements, true, a);
+            w[k] = 0.0;
+            nz[k] = 0.0;
+            if (use[k]) {
+                const float p = v.policy[row + a];
+                bad |= !(isfinite(p) && p >= 0.0f);
+                w[k] = (double)p;
+                nz[k] = (double)v.noise[row + a];
+                largest = fmax(largest, w[k]);
+                ++legal_count;
+            }
+        }
+#pragma unroll
+        for (int off = 16; off; off >>= 1) {
+            largest = fmax(largest, __shfl_xor_sync(kFull, largest, off));
+            legal_count += __shfl_xor_sync(kFull, legal_count, off);
+        }
+        bad = __any_sync(kFull, bad);
+        double total = 0.0;
+        if (!bad && largest > 0.0) {
+            double scaled[3];
+#pragma unroll
+            for (int k = 0; k < 3; ++k) scaled[k] = use[k] ? w[k] / largest : 0.0;
+            total = ordered_sum(scaled, use);
+        }
+        if (bad || legal_count == 0 || !(total > 0.0) || !isfinite(total)) {
+            // Mirrors the reference's handling of a bad evaluation: flag it,
+            // use a uniform policy over legal actions and a zero value.
+            bad = true;
+#pragma unroll
+            for (int k = 0; k < 3; ++k) w[k] = use[k] ? 1.0 : 0.0;
+            largest = 1.0;
+            total = (double)legal_count;
+            leaf_value = 0.0f;
+        }
+        const bool mix = node == 0 && o.epsilon != 0.0;
+        double noise_total = 0.0;
+        if (mix) noise_total = ordered_sum(nz, use);
+        double prior[3];
+#pragma unroll
+        for (int k = 0; k < 3; ++k) {
+            prior[k] = 0.0;
+            if (!use[k]) continue;
+            double weight = (w[k] / largest) / total;
+            if (mix) {
+                const double sampled = noise_total > 0.0 ? nz[k] / noise_total : 1.0 / (double)legal_count;
+                weight = GK_DADD(GK_DMUL(GK_DSUB(1.0, o.epsilon), weight), GK_DMUL(o.epsilon, sampled));
+            }
+            prior[k] = weight;
+        }
+        if (mix) {
+            bool all[3] = {true, true, lane + 64 < GK_ACTIONS};
+            const double combined = ordered_sum(prior, all);
+#pragma unroll
+            for (int k = 0; k < 3; ++k) prior[k] = prior[k] / combined;
+        }
+#pragma unroll
+        for (int k = 0; k < 3; ++k) {
+            const int a = lane + 32 * k;
+            if (a < GK_ACTIONS) {
+                v.prior[ebase + a] = prior[k];
+                v.wsum[ebase + a] = 0.0;
+                v.visits[ebase + a] = 0;
+                v.child[ebase + a] = -1;
+            }
+        }
+        if (lane == 0) {
+            if (bad) v.errors[t] |= GK_ERR_BAD_EVAL;
+            v.leaf_value[t] = leaf_value;
+            v.node_value[vtx] = leaf_value;
+            v.expanded[vtx] = 1;
+            v.evals[t] += 1;
+        }
+    }
+    if (!backup) return;
+    const int leaf_actor = gk_actor(&st);
+    const double lv = (double)leaf_value;
+    const int64_t tbase = t * C;
+    const int len = v.path_len[t];
+    if (lane == 0) v.node_visits[tbase] += 1;
+    for (int d = lane; d < len; d += 32) {
+        const int parent = v.path_nodes[t * P + d];
+        const int a = v.path_actions[t * P + d];
+        const int64_t pv = tbase + parent;
+        const int64_t e = pv * GK_ACTIONS + a;
+        const int parent_actor = (int)(v.node_state[pv].w[15] & 3u);
+        const double value = parent_actor == leaf_actor ? lv : -lv;
+        v.visits[e] += 1;
+        v.wsum[e] = GK_DADD(v.wsum[e], value);
+        v.node_visits[tbase + v.child[e]] += 1;
+    }
+    if (lane == 0) v.sims[t] += 1;
+}
+
+struct PuctOutputs {
+    int64_t* actions;
+    int32_t* visits;
+    float* policy;
+    float* values;
+    int32_t* sims;
+    int32_t* evals;
+    double* priors;
+    float* best_values;
+    int32_t* nodes;
+    double* root_values;
+    uint32_t* status;
+};
+
+__global__ void __launch_bounds__(32 * kWarpsPerBlock) puct_finish_kernel(PuctView v, int64_t B, int C, PuctOutputs out) {
+    const int lane = threadIdx.x & 31;
+    const int64_t t = (blockIdx.x * (int64_t)blockDim.x + threadIdx.x) >> 5;
+    if (t >= B) return;
+    const int64_t vtx = t * C, ebase = vtx * GK_ACTIONS, row = t * GK_ACTIONS;
+    const gk_bits root = v.node_state[vtx];
+    const uint32_t err = v.errors[t];
+    if (lane == 0 && err && out.status) atomicOr(out.status, err);
+    if (v.node_count[t] == 0) {
+        for (int a = lane; a < GK_ACTIONS; a += 32) {
+            if (out.visits) out.visits[row + a] = 0;
+            if (out.policy) out.policy[row + a] = 0.0f;
+            if (out.priors) out.priors[row + a] = 0.0;
+        }
+        if (lane == 0) {
+            if (out.actions) out.actions[t] = -1;
+            if (out.values) out.values[t] = terminal_value(root);
+            if (out.best_values) out.best_values[t] = 0.0f;
+            if (out.sims) out.sims[t] = 0;
+            if (out.evals) out.evals[t] = 0;
+            if (out.nodes) out.nodes[t] = 0;
+            if (out.root_values) out.root_values[t] = (double)terminal_value(root);
+        }
+        return;
+    }
+    const int sims = v.sims[t];
+    const gk_b96 placements = legal_placements(root);
+    const bool expanded = v.expanded[vtx] != 0;
+    bool use[3];
+    double ws[3];
+    int best = -1, best_n = 0;
+    double best_q = 0.0, best_p = 0.0;
+#pragma unroll
+    for (int k = 0; k < 3; ++k) {
+        const int a = lane + 32 * k;
+        use[k] = expanded && a < GK_ACTIONS && action_legal(placements, true, a);
+        ws[k] = 0.0;
+        if (a >= GK_ACTIONS) continue;
+        const int n = expanded ? v.visits[ebase + a] : 0;
+        const double p = expanded ? v.prior[ebase + a] : 0.0;
+        if (out.visits) out.visits[row + a] = n;
+        if (out.policy) out.policy[row + a] = sims > 0 ? __fdiv_rn((float)n, (float)sims) : 0.0f;
+        if (out.priors) out.priors[row + a] = p;
+        if (!use[k]) continue;
+        ws[k] = v.wsum[ebase + a];
+        const double q = n == 0 ? 0.0 : ws[k] / (double)n;
+        if (best < 0 || n > best_n || (n == best_n && (q > best_q || (q == best_q && p > best_p)))) {
+            best = a;
+            best_n = n;
+            best_q = q;
+            best_p = p;
+        }
+    }
+#pragma unroll
+    for (int off = 16; off; off >>= 1) {
+        const int oa = __shfl_down_sync(kFull, best, off);
+        const int on = __shfl_down_sync(kFull, best_n, off);
+        const double oq = __shfl_down_sync(kFull, best_q, off);
+        const double op = __shfl_down_sync(kFull, best_p, off);
+        if (oa >= 0 && (best < 0 || on > best_n ||
+                        (on == best_n && (oq > best_q || (oq == best_q && (op > best_p || (op == best_p && oa < best))))))) {
+            best = oa;
+            best_n = on;
+            best_q = oq;
+            best_p = op;
+        }
+    }
+    const double root_sum = ordered_sum(ws, use);
+    if (lane == 0) {
+        const double rv = sims > 0 ? root_sum / (double)sims : 0.0;
+        if (out.actions) out.actions[t] = best;
+        if (out.values) out.values[t] = (float)rv;
+        if (out.best_values) out.best_values[t] = (float)best_q;
+        if (out.sims) out.sims[t] = sims;
+        if (out.evals) out.evals[t] = v.evals[t];
+        if (out.nodes) out.nodes[t] = v.node_count[t];
+        if (out.root_values) out.root_values[t] = rv;
+    }
+}
+
+// Injected evaluator (include/gk_common.h): weights and value per leaf.
+__global__ void puct_hash_eval_kernel(PuctView v, int64_t B) {
+    for (int64_t t = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; t < B; t += (int64_t)gridDim.x * blockDim.x) {
+        if (!v.needs_eval[t]) continue;
+        uint64_t words[GK_EVAL_WORDS];
+        const gk_bits s = v.leaf_bits[t];
+        gk_eval_words_from_bits(&s, words);
+        const uint64_t h = gk_eval_hash_words(words);
+        for (int a = 0; a < GK_ACTIONS; ++a) v.policy[t * GK_ACTIONS + a] = gk_eval_weight(h, a);
+        v.leaf_value[t] = gk_eval_value(h);
+    }
+}
+
+// ---- root Dirichlet noise ---------------------------------------------------
+// Gamma(alpha) by Marsaglia & Tsang (2000), "A simple method for generating
+// gamma variables", with the alpha < 1 boost Gamma(alpha+1) * U^(1/alpha);
+// normals by Box-Muller. Stream per tree: PCG32 (seed, stream_base + tree).
+__device__ __forceinline__ double uniform01(gk_pcg32& r) {
+    const uint64_t hi = gk_pcg32_next(&r) >> 5, lo = gk_pcg32_next(&r) >> 6;  // 27 + 26 bits
+    return ((double)(hi * 67108864ull + lo) + 0.5) * (1.0 / 9007199254740992.0);
+}
+__device__ __forceinline__ double normal01(gk_pcg32& r) {
+    const double u1 = uniform01(r), u2 = uniform01(r);
+    return sqrt(-2.0 * log(u1)) * cospi(2.0 * u2);
+}
+__device__ double gamma_draw(double alpha, gk_pcg32& r) {
+    double boost = 1.0;
+    if (alpha < 1.0) {
+        boost = pow(uniform01(r), 1.0 / alpha);
+        alpha += 1.0;
+    }
+    const double d = alpha - 1.0 / 3.0, c = 1.0 / sqrt(9.0 * d);
+    for (int it = 0; it < 64; ++it) {
+        const double x = normal01(r);
+        double y = 1.0 + c * x;
+        if (y <= 0.0) continue;
+        y = y * y * y;
+        const double u = uniform01(r);
+        if (u < 1.0 - 0.0331 * x * x * x * x || log(u) < 0.5 * x * x + d * (1.0 - y + log(y))) return d * y * boost;
+    }
+    return d * boost;
+}
+
+__global__ void puct_noise_kernel(PuctView v, int64_t B, int C, uint64_t seed, uint64_t stream_base, double alpha) {
+    for (int64_t t = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; t < B; t += (int64_t)gridDim.x * blockDim.x) {
+        const gk_bits root = v.node_state[t * C];
+        const gk_b96 placements = legal_placements(root);
+        const bool live = gk_reason(&root) == GK_NONE;
+        gk_pcg32 r = gk_pcg32_seed(seed, stream_base + (uint64_t)t);
+        double g[GK_ACTIONS];
+        double largest = 0.0;
+        for (int a = 0; a < GK_ACTIONS; ++a) {
+            g[a] = 0.0;
+            if (live && action_legal(placements, true, a)) {
+                double x = gamma_draw(alpha, r);
+                if (!isfinite(x) || x < 0.0) x = 0.0;
+                g[a] = x;
+                largest = fmax(largest, x);
+            }
+        }
+        const double scale = largest > 2.2250738585072014e-308 ? largest : 2.2250738585072014e-308;
+        for (int a = 0; a < GK_ACTIONS; ++a) v.noise[t * GK_ACTIONS + a] = (float)(g[a] / scale);
+    }
+}
+
+// Ordered compaction of trees whose leaf needs the evaluator (single block).
+__global__ void __launch_bounds__(1024) puct_compact_kernel(PuctView v, int64_t B) {
+    __shared__ int warp_sums[32];
+    __shared__ int carry;
+    if (threadIdx.x == 0) carry = 0;
+    __syncthreads();
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    for (int64_t base = 0; base < B; base += blockDim.x) {
+        const int64_t t = base + threadIdx.x;
+        const int flag = (t < B && v.needs_eval[t]) ? 1 : 0;
+        const unsigned ballot = __ballot_sync(kFull, flag);
+        const int in_warp = __popc(ballot & ((1u << lane) - 1u));
+        if (lane == 31) warp_sums[warp] = in_warp + flag;
+        __syncthreads();
+        if (warp == 0) {
+            int x = lane < (int)(blockDim.x >> 5) ? warp_sums[lane] : 0;
+#pragma unroll
+            for (int off = 1; off < 32; off <<= 1) {
+                const int y = __shfl_up_sync(kFull, x, off);
+                if (lane >= off) x += y;
+            }
+            warp_sums[lane] = x;  // inclusive prefix over warps
+        }
+        __syncthreads();
+        const int before = (warp > 0 ? warp_sums[warp - 1] : 0) + in_warp;
+        if (flag) v.active[carry + before] = (int32_t)t;
+        __syncthreads();
+        if (threadIdx.x == 0) carry += warp_sums[(blockDim.x >> 5) - 1];
+        __syncthreads();
+    }
+    if (threadIdx.x == 0) *v.active_count = carry;
+}
+
+inline PuctOptions make_options(const gk_puct_options* o) {
+    PuctOptions p;
+    p.c_puct = o ? o->c_puct : 1.5;
+    p.epsilon = o ? o->dirichlet_epsilon : 0.0;
+    p.fpu_enabled = o ? (double)o->fpu_enabled : 0.0;
+    p.fpu_reduction = o ? o->fpu_reduction : 0.0;
+    return p;
+}
+
+inline int warp_grid(int64_t B) {
+    const int64_t blocks = (B + kWarpsPerBlock - 1) / kWarpsPerBlock;
+    return (int)(blocks < 1 ? 1 : blocks);
+}
+
+inline bool valid_ws(const void* ws, int64_t B, int C) { return ws != nullptr && B > 0 && C >= 1 && C < (1 << 24); }
+
+}  // namespace gk
+
+using namespace gk;
+
+extern "C" {
+
+size_t gk_puct_workspace_bytes(int64_t batch, int capacity) {
+    if (batch <= 0 || capacity < 1) return 0;
+    return puct_layout(nullptr, batch, capacity, nullptr);
+}
+
+int gk_puct_buffers(void* ws, int64_t batch, int capacity, gk_puct_buffers_t* out) {
+    if (!valid_ws(ws, batch, capacity) || out == nullptr) return GK_EINVAL;
+    PuctView v;
+    puct_layout(ws, batch, capacity, &v);
+    out->needs_eval = v.needs_eval;
+    out->leaf_bits = reinterpret_cast<uint32_t*>(v.leaf_bits);
+    out->leaf_value = v.leaf_value;
+    out->policy = v.policy;
+    out->noise = v.noise;
+    out->active = v.active;
+    out->active_count = v.active_count;
+    out->errors = v.errors;
+    return 0;
+}
+
+int gk_puct_begin(void* ws, int64_t batch, int capacity, const uint32_t* root_bits, void* stream) {
+    if (!valid_ws(ws, batch, capacity) || root_bits == nullptr) return GK_EINVAL;
+    PuctView v;
+    puct_layout(ws, batch, capacity, &v);
+    puct_begin_kernel<<<blocks_for(batch, 256, kSmCount * 8), 256, 0, as_stream(stream)>>>(
+        v, batch, capacity, reinterpret_cast<const gk_bits*>(root_bits));
+    return launch_status();
+}
+
+int gk_puct_noise(void* ws, int64_t batch, int capacity, uint64_t seed, uint64_t stream_base, double alpha,
+                  void* stream) {
+    if (!valid_ws(ws, batch, capacity) || !(alpha > 0.0)) return GK_EINVAL;
+    PuctView v;
+    puct_layout(ws, batch, capacity, &v);
+    puct_noise_kernel<<<blocks_for(batch, 128, kSmCount * 8), 128, 0, as_stream(stream)>>>(v, batch, capacity, seed,
+                                                                                             stream_base, alpha);
+    return launch_status();
+}
+
+int gk_puct_hash_eval(void* ws, int64_t batch, int capacity, void* stream) {
+    if (!valid_ws(ws, batch, capacity)) return GK_EINVAL;
+    PuctView v;
+    puct_layout(ws, batch, capacity, &v);
+    puct_hash_eval_kernel<<<blocks_for(batch, 128, kSmCount * 8), 128, 0, as_stream(stream)>>>(v, batch);
+    return launch_status();
+}
+
+int gk_puct_compact(void* ws, int64_t batch, int capacity, void* stream) {
+    if (!valid_ws(ws, batch, capacity)) return GK_EINVAL;
+    PuctView v;
+    puct_layout(ws, batch, capacity, &v);
+    puct_compact_kernel<<<1, 1024, 0, as_stream(stream)>>>(v, batch);
+    return launch_status();
+}
+
+int gk_puct_select(void* ws, int64_t batch, int capacity, const gk_puct_options* options, void* stream) {
+    if (!valid_ws(ws, batch, capacity) || options == nullptr || !(options->c_puct > 0.0)) return GK_EINVAL;
+    PuctView v;
+    puct_layout(ws, batch, capacity, &v);
+    puct_select_kernel<<<warp_grid(batch), 32 * kWarpsPerBlock, 0, as_stream(stream)>>>(v, batch, capacity,
+                                                                                         make_options(options));
+    return launch_status();
+}
+
+int gk_puct_expand_backup(void* ws, int64_t batch, int capacity, const gk_puct_options* options, int backup,
+                          void* stream) {
+    if (!valid_ws(ws, batch, capacity) || options == nullptr) return GK_EINVAL;
+    PuctView v;
+    puct_layout(ws, batch, capacity, &v);
+    puct_expand_backup_kernel<<<warp_grid(batch), 32 * kWarpsPerBlock, 0, as_stream(stream)>>>(
+        v, batch, capacity, make_options(options), backup);
+    return launch_status();
+}
+
+int gk_puct_finish(void* ws, int64_t batch, int capacity, const gk_puct_results_t* results, void* stream) {
+    if (!valid_ws(ws, batch, capacity) || results == nullptr) return GK_EINVAL;
+    PuctView v;
+    puct_layout(ws, batch, capacity, &v);
+    PuctOutputs o{results->actions, results->visits, results->policy, results->values, results->simulations,
+                  results->network_evaluations, results->priors, results->best_values, results->nodes,
+                  results->root_values, results->status};
+    puct_finish_kernel<<<warp_grid(batch), 32 * kWarpsPerBlock, 0, as_stream(stream)>>>(v, batch, capacity, o);
+    return launch_status();
+}
+
+int gk_puct_search_hash(void* ws, int64_t batch, int simulations, const uint32_t* root_bits,
+                        const gk_puct_options* options, const gk_puct_results_t* results, void* stream) {
+    if (simulations < 1 || options == nullptr || results == nullptr) return GK_EINVAL;
+    const int capacity = simulations + 1;
+    int s = gk_puct_begin(ws, batch, capacity, root_bits, stream);
+    if (s) return s;
+    if ((s = gk_puct_hash_eval(ws, batch, capacity, stream))) return s;
+    if ((s = gk_puct_expand_backup(ws, batch, capacity, options, 0, stream))) return s;
+    for (int i = 0; i < simulations; ++i) {
+        if ((s = gk_puct_select(ws, batch, capacity, options, stream))) return s;
+        if ((s = gk_puct_hash_eval(ws, batch, capacity, stream))) return s;
+        if ((s = gk_puct_expand_backup(ws, batch, capacity, options, 1, stream))) return s;
+    }
+    return gk_puct_finish(ws, batch, capacity, results, stream);
+}
+
+}  // extern "C"

@@ -1,0 +1,180 @@
+/*
+ * gk.h - C ABI of libgk.so, the B200-native batched self-play engine.
+ *
+ * Conventions (all entry points)
+ *   - Pointers are device pointers unless a parameter says "host".
+ *   - `stream` is a cudaStream_t passed as void* (NULL = legacy default stream);
+ *     work is enqueued on it and the call returns without synchronising.
+ *   - Return value: 0 on success, GK_EINVAL (-22) for a rejected argument
+ *     (nothing is launched), otherwise the cudaError_t of a failed launch.
+ *   - Hot entry points allocate nothing; scratch comes from the caller, sized
+ *     by the matching *_workspace_bytes function.
+ *   - Device-side failures never trap: they set bits (GK_ERR_* in
+ *     gk_common.h) in a caller-supplied uint32 status word or per-lane word.
+ *
+ * Each declaration names the reference interface it replaces. The reference
+ * launches NVRTC kernels through ctypes (python/kingdom_ai/gpu_runtime.py:179-221,
+ * CudaModule.launch); these functions are what that FFI binds instead.
+ */
+#ifndef GK_H
+#define GK_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#include "gk_common.h"
+
+#if defined(__GNUC__)
+#define GK_API __attribute__((visibility("default")))
+#else
+#define GK_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---------------------------------------------------------------- rules */
+
+/* Initial states in wire format. Replaces gpu_initial_batch
+ * (python/kingdom_ai/gpu_rules.py:284-293) behind GpuStateBatch.initial
+ * (gpu_rules.py:353-374). neutral_cell = row*9+col, or -1 for none. */
+GK_API int gk_initial_records(int32_t* recs, int64_t n, int neutral_cell, void* stream);
+
+/* Initial states in packed format (uint32[n,16]). Same semantics as
+ * gk_initial_records (reference gpu_initial_batch, gpu_rules.py:284-293). */
+GK_API int gk_initial_bits(uint32_t* bits, int64_t n, int neutral_cell, void* stream);
+
+/* One transition per wire record, in place; accepted[n] gets 1/0 and rejected
+ * records stay unchanged. actions are int32 (action_bytes 4) or int64 (8);
+ * int64 values outside [0,82) are rejected without wrapping. Replaces
+ * gpu_play_batch (gpu_rules.py:295-301) behind GpuStateBatch.play (:418-443). */
+GK_API int gk_play_records(int32_t* recs, const void* actions, int action_bytes, uint8_t* accepted, int64_t n,
+                    void* stream);
+
+/* Schema-1 observation planes fp32[n,10,9,9] and legal mask bool[n,82].
+ * Replaces gpu_encode_batch (gpu_rules.py:303-311) behind GpuStateBatch.encode
+ * (:445-454) and the CPU encode_puct_batch (bindings/batched_puct.cpp:140-148). */
+GK_API int gk_encode_records(const int32_t* recs, float* features, uint8_t* masks, int64_t n, void* stream);
+
+/* Wire record -> packed state. If `status` is non-null, GK_ERR_BAD_INPUT is
+ * OR-ed into it when a record holds a value outside the wire format's ranges.
+ * Replaces the record copy of gpu_search_initialize (gpu_puct.py:163-180). */
+GK_API int gk_records_to_bits(const int32_t* recs, uint32_t* bits, uint32_t* status, int64_t n, void* stream);
+
+/* Packed state -> wire record (reserved field 169 written as 0); the export
+ * side of the wire format of python/kingdom_ai/gpu_rules.py:16-33. */
+GK_API int gk_bits_to_records(const uint32_t* bits, int32_t* recs, int64_t n, void* stream);
+
+/* One transition per packed state, in place (the HBM-bound rules kernel).
+ * Same rules as gpu_play (gpu_rules.py:185-252) / State::play (engine/src/State.cpp:92-167). */
+GK_API int gk_play_bits(uint32_t* bits, const void* actions, int action_bytes, uint8_t* accepted, int64_t n, void* stream);
+
+/* Encoder from packed states; same outputs as gk_encode_records (reference
+ * gpu_encode, gpu_rules.py:258-282; encode, mcts/src/BatchedPUCT.cpp:25-50). */
+GK_API int gk_encode_bits(const uint32_t* bits, float* features, uint8_t* masks, int64_t n, void* stream);
+
+/* Uniform-random complete playouts from the default start, one PCG32 stream
+ * per game (seed, first_game + i). boards int8[n,81]; infos int32[n,5] =
+ * {winner, C++ EndReason, score black, score white, plies}. No reference API
+ * (the reference samples legal_moves() in tests/board_test.cpp:131-162). */
+GK_API int gk_random_playouts(uint64_t seed, uint64_t first_game, int64_t n, int neutral_cell, int8_t* boards,
+                       int32_t* infos, void* stream);
+
+/* Random non-terminal mid-game positions (k ~ U[0,60] uniform legal moves,
+ * stream (seed, first + i)) as packed states. No reference counterpart: a
+ * workload generator for the encoder, search and network benchmarks. */
+GK_API int gk_gen_positions(uint64_t seed, uint64_t first, int64_t n, uint32_t* bits, void* stream);
+
+/* ----------------------------------------------------------------- PUCT */
+
+/* Search options (python/kingdom_ai/gpu_puct.py:26-63, GpuPUCTOptions;
+ * the device copy is the `options` tensor of gpu_puct.py:465-468). */
+typedef struct {
+    double c_puct;
+    double dirichlet_epsilon; /* root noise weight; 0 disables */
+    int fpu_enabled;          /* nonzero: unvisited edges start at node value - fpu_reduction */
+    double fpu_reduction;
+} gk_puct_options;
+
+/* Device pointers into a search workspace that an external evaluator reads
+ * and writes between gk_puct_select and gk_puct_expand_backup. */
+typedef struct {
+    uint8_t* needs_eval;   /* [B] 1: leaf_bits[t] needs policy/value */
+    uint32_t* leaf_bits;   /* [B,16] packed leaf states */
+    float* leaf_value;     /* [B] evaluator writes the value (current player's view) */
+    float* policy;         /* [B,82] evaluator writes probabilities or weights >= 0 */
+    float* noise;          /* [B,82] root noise written by gk_puct_noise */
+    int32_t* active;       /* [B] compacted tree indices (gk_puct_compact) */
+    int32_t* active_count; /* [1] */
+    uint32_t* errors;      /* [B] GK_ERR_* per tree */
+} gk_puct_buffers_t;
+
+/* Search outputs (GpuSearchResult, gpu_puct.py:66-76); any pointer may be
+ * NULL to skip that output. `status` receives the OR of all tree errors. */
+typedef struct {
+    int64_t* actions;             /* [B] best action, -1 for a terminal root */
+    int32_t* visits;              /* [B,82] root visit counts */
+    float* policy;                /* [B,82] visits / simulations */
+    float* values;                /* [B] mean backed-up value for the root player */
+    int32_t* simulations;         /* [B] */
+    int32_t* network_evaluations; /* [B] */
+    double* priors;               /* [B,82] root priors (after noise) */
+    float* best_values;           /* [B] mean value of the best action */
+    int32_t* nodes;               /* [B] tree size */
+    double* root_values;          /* [B] root value in double (for exact comparison) */
+    uint32_t* status;             /* [1] OR of GK_ERR_* bits */
+} gk_puct_results_t;
+
+/* Bytes of device workspace for `batch` trees of `capacity` nodes
+ * (capacity = simulations + 1, gpu_puct.py:439). 0 for invalid sizes. */
+GK_API size_t gk_puct_workspace_bytes(int64_t batch, int capacity);
+
+/* Fill `out` (host struct) with device pointers into the workspace: the
+ * leaf tensors the reference allocates in GpuPUCT._search (gpu_puct.py:445-471). */
+GK_API int gk_puct_buffers(void* ws, int64_t batch, int capacity, gk_puct_buffers_t* out);
+
+/* Reset the trees at the given packed roots. Replaces gpu_search_initialize
+ * (gpu_puct.py:163-180). */
+GK_API int gk_puct_begin(void* ws, int64_t batch, int capacity, const uint32_t* root_bits, void* stream);
+
+/* Root Dirichlet noise over each root's legal actions, max-normalised, from
+ * PCG32 stream (seed, stream_base + tree). Replaces the torch._standard_gamma
+ * block of GpuPUCT._search (gpu_puct.py:509-517). */
+GK_API int gk_puct_noise(void* ws, int64_t batch, int capacity, uint64_t seed, uint64_t stream_base, double alpha,
+                  void* stream);
+
+/* One selection pass per tree (one leaf per tree). Replaces gpu_search_select
+ * (gpu_puct.py:182-258). */
+GK_API int gk_puct_select(void* ws, int64_t batch, int capacity, const gk_puct_options* options, void* stream);
+
+/* The injected evaluator: weights w_a = exp(z_a) and a uniform value, pure
+ * functions of the leaf (gk_common.h). No reference counterpart: it stands in
+ * for the evaluator callback of PUCT::search (mcts/include/PUCT.h:34). */
+GK_API int gk_puct_hash_eval(void* ws, int64_t batch, int capacity, void* stream);
+
+/* Ordered list of trees whose leaf needs evaluation (device-side; replaces
+ * the host-synchronising nonzero() of gpu_puct.py:482). */
+GK_API int gk_puct_compact(void* ws, int64_t batch, int capacity, void* stream);
+
+/* Expand evaluated leaves ((w/max)/sum priors, root noise mix) and, when
+ * `backup` is nonzero, back the leaf value up the path. Replaces
+ * gpu_search_expand_backup (gpu_puct.py:260-341). */
+GK_API int gk_puct_expand_backup(void* ws, int64_t batch, int capacity, const gk_puct_options* options, int backup,
+                          void* stream);
+
+/* Root statistics and best action. Replaces gpu_search_finish
+ * (gpu_puct.py:343-379). `results` is a host struct of device pointers. */
+GK_API int gk_puct_finish(void* ws, int64_t batch, int capacity, const gk_puct_results_t* results, void* stream);
+
+/* A complete search with the injected evaluator, no host synchronisation:
+ * begin, root evaluation, `simulations` x (select, evaluate, expand/backup),
+ * finish. The workspace must be sized for capacity = simulations + 1.
+ * Equivalent of PUCT::search (mcts/src/PUCT.cpp:177-268) per tree. */
+GK_API int gk_puct_search_hash(void* ws, int64_t batch, int simulations, const uint32_t* root_bits,
+                        const gk_puct_options* options, const gk_puct_results_t* results, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* GK_H */

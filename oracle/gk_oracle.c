@@ -344,13 +344,22 @@ typedef struct {
 
 static double edge_value(const o_edge* e) { return e->visits == 0 ? 0.0 : e->value_sum / (double)e->visits; }
 
+/* Evaluator used by the search: 0 = injected hash evaluator, 1 = uniform
+ * (weight 1 for every action, value 0 - what a zero-weight network gives). */
+static __thread int g_uniform_evaluator = 0;
+
 /* PUCT.cpp:53-86 */
 static int expand(o_node* node, const int32_t* rec, o_edge* storage, double* leaf_value, int64_t* evaluations) {
     int moves[GK_ACTIONS];
     int n = legal_list(rec, moves);
     if (n == 0) return -1;
     float w[GK_ACTIONS], v;
-    gko_eval(rec, w, &v);
+    if (g_uniform_evaluator) {
+        for (int a = 0; a < GK_ACTIONS; ++a) w[a] = 1.0f;
+        v = 0.0f;
+    } else {
+        gko_eval(rec, w, &v);
+    }
     ++*evaluations;
     if (!isfinite(v) || v < -1.0f || v > 1.0f) return -2;
     for (int a = 0; a < GK_ACTIONS; ++a)
@@ -503,6 +512,14 @@ done:
     free(pool);
     free(path_node);
     free(path_edge);
+    return status;
+}
+
+int gko_puct_search_uniform(const int32_t* rec, int simulations, double c_puct, int32_t* visits, double* priors,
+                            int32_t* stats, double* values) {
+    g_uniform_evaluator = 1;
+    int status = gko_puct_search(rec, simulations, c_puct, visits, priors, stats, values);
+    g_uniform_evaluator = 0;
     return status;
 }
 

@@ -42,6 +42,9 @@ void gko_eval(const int32_t* rec, float* weights, float* value);
  * simulations, nodes, network_evaluations}, values = {root_value, best_value}. */
 int gko_puct_search(const int32_t* rec, int simulations, double c_puct, int32_t* visits, double* priors,
                     int32_t* stats, double* values);
+/* Same search with a uniform evaluator (all weights 1, value 0). */
+int gko_puct_search_uniform(const int32_t* rec, int simulations, double c_puct, int32_t* visits, double* priors,
+                            int32_t* stats, double* values);
 int gko_puct_search_batch(const int32_t* recs, int64_t n, int simulations, double c_puct, int32_t* visits,
                           int32_t* best, double* root_values, int threads);
 

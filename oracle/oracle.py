@@ -76,6 +76,7 @@ class Oracle:
         _bind(L, "gko_gen_positions", [_u64, _u64, _i64, _i32p])
         _bind(L, "gko_eval", [_i32p, _f32p, _f32p])
         _bind(L, "gko_puct_search", [_i32p, _int, ctypes.c_double, _i32p, _f64p, _i32p, _f64p], _int)
+        _bind(L, "gko_puct_search_uniform", [_i32p, _int, ctypes.c_double, _i32p, _f64p, _i32p, _f64p], _int)
         _bind(L, "gko_puct_search_batch", [_i32p, _i64, _int, ctypes.c_double, _i32p, _i32p, _f64p, _int], _int)
 
     def initial(self, n: int = 1, neutral: int = 40) -> np.ndarray:
@@ -118,13 +119,13 @@ class Oracle:
         self.lib.gko_eval(np.ascontiguousarray(rec, dtype=np.int32), w, v)
         return w, float(v[0])
 
-    def puct(self, rec: np.ndarray, simulations: int, c_puct: float = 1.5):
+    def puct(self, rec: np.ndarray, simulations: int, c_puct: float = 1.5, uniform: bool = False):
         visits = np.zeros(ACTIONS, dtype=np.int32)
         priors = np.zeros(ACTIONS, dtype=np.float64)
         stats = np.zeros(4, dtype=np.int32)
         values = np.zeros(2, dtype=np.float64)
-        status = self.lib.gko_puct_search(np.ascontiguousarray(rec, dtype=np.int32), simulations, c_puct,
-                                          visits, priors, stats, values)
+        fn = self.lib.gko_puct_search_uniform if uniform else self.lib.gko_puct_search
+        status = fn(np.ascontiguousarray(rec, dtype=np.int32), simulations, c_puct, visits, priors, stats, values)
         if status != 0:
             raise RuntimeError(f"oracle PUCT failed ({status})")
         return dict(visits=visits, priors=priors, best=int(stats[0]), simulations=int(stats[1]),

@@ -1,0 +1,214 @@
+"""Generate the golden fixtures in this folder from the reference C++ engine.
+
+The reference engine (engine/ and mcts/ of the reference repository) is
+compiled from its own sources by ``oracle/Makefile`` into
+``oracle/_ref/libgkref.so`` and driven through ``oracle/ref_harness.cpp``.
+Run from the repository root, where the reference sources are mounted:
+
+    python tests/golden/make_golden.py
+
+Fixtures
+  rules_<scenario>.npz  board set-ups and action sequences of the reference's
+                        tests/gpu_rules_test.py (captures, suicide, territory,
+                        closed house, illegal moves, stock, two-pass
+                        threshold, seeded complete games); per step the
+                        expected wire records, accepted flags and encodings.
+  playouts.npz          uniform-random complete playouts (PCG32 per game).
+  positions.npz         generated mid-game positions with their encodings.
+  puct.npz              root visits / priors / best move / root value of the
+                        reference PUCT::search with the injected evaluator.
+  puct_uniform.npz      the reference PUCT with a uniform evaluator on the
+                        states of tests/gpu_puct_test.py:152-177.
+"""
+
+from __future__ import annotations
+
+import sys
+from pathlib import Path
+
+import numpy as np
+
+HERE = Path(__file__).resolve().parent
+ROOT = HERE.parent.parent
+sys.path.insert(0, str(ROOT))
+
+from oracle.oracle import Reference, RefState  # noqa: E402
+
+BLACK, WHITE = 1, 2
+
+
+def board(black=(), white=(), neutral=None):
+    cells = np.zeros(81, dtype=np.int32)
+    if neutral is not None:
+        cells[neutral[0] * 9 + neutral[1]] = 3
+    for points, colour in ((black, BLACK), (white, WHITE)):
+        for r, c in points:
+            assert cells[r * 9 + c] == 0
+            cells[r * 9 + c] = colour
+    return cells
+
+
+def last_liberty_cells():
+    cells = np.zeros(81, dtype=np.int32)
+    for r in range(9):
+        for c in range(9):
+            if c < 4 or (c == 4 and r < 4):
+                cells[r * 9 + c] = BLACK
+            elif c > 4 or (c == 4 and r > 4):
+                cells[r * 9 + c] = WHITE
+    return cells
+
+
+def square_enclosure(neutral=None, enemy=False):
+    points = []
+    for k in range(2, 7):
+        points += [(2, k), (6, k)]
+    for r in range(3, 6):
+        points += [(r, 2), (r, 6)]
+    return board(points, ((4, 4),) if enemy else (), neutral=neutral)
+
+
+def trajectory(ref, states, action_rows, encode_every=1):
+    """Apply rows of actions; record records/accepted/encodings per step."""
+    records = [np.stack([s.record() for s in states])]
+    accepted, features, masks, enc_steps = [], [], [], []
+
+    def encode(step):
+        f, m = zip(*(s.encode() for s in states))
+        features.append(np.stack(f).reshape(len(states), 810))
+        masks.append(np.stack(m))
+        enc_steps.append(step)
+
+    encode(0)
+    for step, row in enumerate(action_rows, start=1):
+        accepted.append([s.play(int(a)) for s, a in zip(states, row)])
+        records.append(np.stack([s.record() for s in states]))
+        if step % encode_every == 0 or step == len(action_rows):
+            encode(step)
+    return dict(records=np.stack(records).astype(np.int32), actions=np.asarray(action_rows, dtype=np.int64),
+                accepted=np.asarray(accepted, dtype=np.uint8), features=np.stack(features).astype(np.float32),
+                masks=np.stack(masks).astype(np.uint8), encode_steps=np.asarray(enc_steps, dtype=np.int32))
+
+
+def save(name, data):
+    np.savez_compressed(HERE / name, **data)
+    print(name, {k: v.shape for k, v in data.items()})
+
+
+def main():
+    ref = Reference()
+    from_board = lambda cells, to_play: RefState.from_board(ref, cells, to_play)  # noqa: E731
+
+    # tests/gpu_rules_test.py:137-148 (initial variants)
+    for name, neutral in (("initial_center", 40), ("initial_corner", 8), ("initial_none", -1)):
+        states = [RefState.initial(ref, neutral) for _ in range(3)]
+        save(f"rules_{name}.npz", trajectory(ref, states, [[0, 1, 2]]))
+
+    # tests/gpu_rules_test.py:150-169 (captures, simultaneous surround, neutral wall)
+    states = [
+        from_board(board(((1, 2), (2, 1), (3, 2)), ((2, 2),)), BLACK),
+        from_board(board(((1, 2), (1, 3), (2, 1), (3, 2), (3, 3)), ((2, 2), (2, 3))), BLACK),
+        from_board(board(((0, 6), (1, 6), (1, 8), (2, 7)), ((0, 7), (1, 7), (2, 8))), BLACK),
+        from_board(board(((3, 3), (4, 2)), ((4, 3),), (4, 4)), BLACK),
+        from_board(board(((2, 2),), ((1, 2), (2, 1), (3, 2))), WHITE),
+        from_board(last_liberty_cells(), BLACK),
+        from_board(last_liberty_cells(), WHITE),
+    ]
+    save("rules_captures.npz", trajectory(ref, states, [[21, 22, 8, 48, 21, 40, 40], [81] * 7]))
+
+    # :171-177 remaining liberty
+    states = [from_board(board(((1, 2), (2, 1), (3, 2), (3, 3)), ((2, 2), (2, 3))), BLACK)]
+    save("rules_liberty.npz", trajectory(ref, states, [[12]]))
+
+    # :179-191 suicide loses for both players
+    b, w = ((0, 1),), ((0, 0), (0, 2), (1, 0), (1, 2), (2, 1))
+    states = [from_board(board(b, w), BLACK), from_board(board(w, b), WHITE)]
+    save("rules_suicide.npz", trajectory(ref, states, [[10, 10]]))
+
+    # :193-215 territory edges, neutral walls, enemy exclusion
+    three_edges = board(tuple((r, 2) for r in range(9)), ((0, 3),))
+    boards = [
+        board(((1, 2), (2, 1), (2, 3), (3, 2))),
+        board(((0, 3), (1, 2), (1, 4), (2, 1), (2, 4), (3, 1), (3, 4), (4, 2), (4, 3), (4, 4))),
+        board(((0, 2), (0, 5), (1, 3), (1, 4))),
+        board(((0, 2), (1, 1), (2, 0))),
+        three_edges,
+        board(((4, 4),)),
+        square_enclosure(enemy=True),
+        square_enclosure((4, 4)),
+        board(((3, 5), (4, 6), (5, 5)), neutral=(4, 4)),
+    ]
+    states = [from_board(cells, BLACK) for cells in boards]
+    data = trajectory(ref, states, [[81] * 9, [81] * 9])
+    data["scores"] = np.asarray([s.score() for s in [from_board(c, BLACK) for c in boards]], dtype=np.int32)
+    save("rules_territory.npz", data)
+
+    # :217-226 closed house persists and forbids both players
+    states = [from_board(board(((1, 2), (2, 1), (2, 3))), BLACK)]
+    save("rules_house.npz", trajectory(ref, states, [[29], [80], [20], [81], [20]]))
+
+    # :228-238 illegal placements preserve actor, passes, stock and ownership
+    states = []
+    for _ in range(4):
+        s = RefState.initial(ref, 40)
+        assert s.play(0) and s.play(81)
+        states.append(s)
+    save("rules_illegal.npz", trajectory(ref, states, [[0, 40, -1, 82], [1, 2, 3, 4]]))
+
+    # :240-250 the 41-stone stock cannot be exceeded
+    states = [from_board(board(tuple(divmod(a, 9) for a in range(41))), BLACK)]
+    save("rules_stock.npz", trajectory(ref, states, [[80], [81]]))
+
+    # :252-264 two-pass threshold needs exactly three more house cells
+    boards = [board(((0, 2), (1, 1), (2, 0))), board(((0, 2), (0, 5), (1, 3), (1, 4))), board(neutral=(4, 4))]
+    states = [from_board(cells, BLACK) for cells in boards]
+    save("rules_threshold.npz", trajectory(ref, states, [[81] * 3, [81] * 3]))
+
+    # :277-292 seeded complete games from several neutral variants
+    variants = [40, -1, 8, 40, -1, 72, 40, -1]
+    states = [RefState.initial(ref, v) for v in variants]
+    rng = np.random.default_rng(6800)
+    probe = [RefState.initial(ref, v) for v in variants]
+    rows = []
+    for _ in range(170):
+        if all(p.record()[166] != 0 for p in probe):
+            break
+        row = []
+        for p in probe:
+            legal = p.legal()
+            a = 81 if not legal else int(legal[rng.integers(len(legal))])
+            row.append(a)
+            p.play(a)
+        rows.append(row)
+    save("rules_games.npz", trajectory(ref, states, rows, encode_every=7))
+
+    # Uniform-random playouts (PCG32 stream per game), reference legal_moves().
+    boards_out, infos = ref.random_playouts(2024, 256, neutral=40, fast=False, threads=8)
+    save("playouts.npz", dict(seed=np.asarray([2024]), boards=boards_out, infos=infos))
+
+    # Generated mid-game positions and their reference encodings.
+    recs = ref.gen_positions(11, 256, threads=8)
+    feats, masks = ref.encode_positions(11, 256, threads=8)
+    save("positions.npz", dict(seed=np.asarray([11]), records=recs, features=feats.reshape(256, 810),
+                               masks=masks.astype(np.uint8)))
+
+    # Reference PUCT with the injected evaluator.
+    n, sims = 48, 160
+    visits = np.zeros((n, 82), np.int32)
+    priors = np.zeros((n, 82), np.float64)
+    stats = np.zeros((n, 4), np.int32)
+    values = np.zeros((n, 2), np.float64)
+    roots = np.zeros((n, 170), np.int32)
+    for i in range(n):
+        s = RefState.generated(ref, 5, i)
+        roots[i] = s.record()
+        r = s.puct(sims)
+        visits[i], priors[i] = r["visits"], r["priors"]
+        stats[i] = (r["best"], r["simulations"], r["nodes"], r["evaluations"])
+        values[i] = (r["root_value"], r["best_value"])
+    save("puct.npz", dict(seed=np.asarray([5]), simulations=np.asarray([sims]), roots=roots, visits=visits,
+                          priors=priors, stats=stats, values=values))
+
+
+if __name__ == "__main__":
+    main()

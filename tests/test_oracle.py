@@ -1,0 +1,109 @@
+"""Pin the CPU oracle: golden vectors of the reference engine and its tests' known answers."""
+
+import numpy as np
+import pytest
+
+RULE_FIXTURES = ["initial_center", "initial_corner", "initial_none", "captures", "liberty", "suicide",
+                 "territory", "house", "illegal", "stock", "threshold", "games"]
+
+
+def replay_oracle(oracle, data):
+    """Replay a golden trajectory through the oracle; compare every step."""
+    recs = data["records"][0].copy()
+    enc = {int(s): i for i, s in enumerate(data["encode_steps"])}
+    f, m = oracle.encode(recs)
+    assert np.array_equal(f.reshape(len(recs), 810), data["features"][enc[0]])
+    assert np.array_equal(m, data["masks"][enc[0]].astype(bool))
+    for step, row in enumerate(data["actions"], start=1):
+        actions = np.where((row >= 0) & (row < 82), row, -1).astype(np.int32)
+        recs, accepted = oracle.play(recs, actions)
+        assert np.array_equal(accepted, data["accepted"][step - 1]), f"accepted differs at step {step}"
+        assert np.array_equal(recs, data["records"][step]), f"record differs at step {step}"
+        if step in enc:
+            f, m = oracle.encode(recs)
+            assert np.array_equal(f.reshape(len(recs), 810), data["features"][enc[step]])
+            assert np.array_equal(m, data["masks"][enc[step]].astype(bool))
+
+
+@pytest.mark.parametrize("name", RULE_FIXTURES)
+def test_oracle_rules_match_reference_fixtures(oracle, golden, name):
+    replay_oracle(oracle, golden(f"rules_{name}.npz"))
+
+
+def test_known_answers_of_reference_rule_tests(golden):
+    # tests/gpu_rules_test.py:166-167 - capture reasons and captured counts.
+    cap = golden("rules_captures.npz")
+    assert cap["records"][1][:, 166].tolist() == [1] * 7
+    assert cap["records"][1][:, 168].tolist() == [1, 2, 2, 1, 1, 40, 40]
+    assert cap["accepted"][1].tolist() == [0] * 7
+    # :206 - black territory of the nine fixture boards; :211-215 winners after two passes.
+    terr = golden("rules_territory.npz")
+    assert terr["scores"][:, 0].tolist() == [1, 5, 2, 3, 18, 0, 0, 8, 1]
+    assert terr["records"][2][:, 167].tolist() == [2, 1, 2, 1, 1, 2, 2, 1, 2]
+    # :263-264 - the 3-point black margin.
+    thr = golden("rules_threshold.npz")
+    assert thr["records"][2][:, 166].tolist() == [3, 3, 3]
+    assert thr["records"][2][:, 167].tolist() == [1, 2, 2]
+    # :179-191 - suicide is legal and loses for both colours.
+    sui = golden("rules_suicide.npz")
+    assert sui["accepted"][0].tolist() == [1, 1]
+    assert sui["records"][1][:, 166].tolist() == [2, 2]
+    # :217-226 - closed house forbids both players.
+    house = golden("rules_house.npz")
+    assert house["accepted"][:, 0].tolist() == [1, 1, 0, 1, 0]
+    assert house["records"][1][0, 81 + 20] == 1
+    # :240-250 - no stones left: only pass.
+    stock = golden("rules_stock.npz")
+    assert stock["masks"][0][0].sum() == 1 and stock["masks"][0][0][81] == 1
+
+
+def test_oracle_playouts_match_reference(oracle, golden):
+    g = golden("playouts.npz")
+    boards, infos = oracle.random_playouts(int(g["seed"][0]), len(g["boards"]))
+    assert np.array_equal(boards, g["boards"])
+    assert np.array_equal(infos, g["infos"])
+
+
+def test_oracle_positions_and_encoder_match_reference(oracle, golden):
+    g = golden("positions.npz")
+    recs = oracle.gen_positions(int(g["seed"][0]), len(g["records"]))
+    assert np.array_equal(recs, g["records"])
+    assert (recs[:, 166] == 0).all()
+    f, m = oracle.encode(recs)
+    assert np.array_equal(f.reshape(len(recs), 810), g["features"])
+    assert np.array_equal(m, g["masks"].astype(bool))
+
+
+def test_oracle_puct_matches_reference(oracle, golden):
+    g = golden("puct.npz")
+    sims = int(g["simulations"][0])
+    for i, root in enumerate(g["roots"]):
+        r = oracle.puct(root, sims)
+        assert np.array_equal(r["visits"], g["visits"][i])
+        assert np.array_equal(r["priors"], g["priors"][i])
+        assert (r["best"], r["simulations"], r["nodes"], r["evaluations"]) == tuple(g["stats"][i])
+        assert r["root_value"] == g["values"][i][0] and r["best_value"] == g["values"][i][1]
+
+
+def test_oracle_matches_reference_engine_directly(oracle, reference):
+    """Where the reference is built here, compare on fresh seeds as well."""
+    b1, i1 = oracle.random_playouts(99, 300)
+    b2, i2 = reference.random_playouts(99, 300, fast=True, threads=4)
+    assert np.array_equal(b1, b2) and np.array_equal(i1, i2)
+    assert np.array_equal(oracle.gen_positions(77, 200), reference.gen_positions(77, 200, threads=4))
+    recs = oracle.gen_positions(3, 8)
+    v, best, _ = oracle.puct_batch(recs, 120, threads=4)
+    v2, best2 = reference.puct_positions(3, 8, 120, threads=4)
+    assert np.array_equal(v, v2) and np.array_equal(best, best2)
+
+
+def test_injected_evaluator_is_a_pure_function(oracle, golden):
+    recs = golden("positions.npz")["records"][:4]
+    for rec in recs:
+        w1, v1 = oracle.evaluate(rec)
+        w2, v2 = oracle.evaluate(rec.copy())
+        assert np.array_equal(w1, w2) and v1 == v2
+        assert (w1 > 0).all() and np.isfinite(w1).all() and -1.0 <= v1 < 1.0
+    # Approximately standard-normal logits: log-weights have mean ~0, sd ~1.
+    logs = np.log(np.concatenate([oracle.evaluate(r)[0] for r in golden("positions.npz")["records"]]))
+    assert abs(logs.mean()) < 0.1 and abs(logs.std() - 1.0) < 0.1
