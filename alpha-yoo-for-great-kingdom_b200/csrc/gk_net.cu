@@ -1,0 +1,621 @@
+// gk_net.cu - policy/value network on sm_100a tensor cores (tcgen05 + TMEM).
+//
+// Semantics: the batch-norm PolicyValueNet (python/kingdom_ai/model.py:30-84
+// with BN folded into the convolutions and a 64-unit value hidden layer):
+//   stem 3x3 (10->C) + ReLU, R residual blocks of two 3x3 convs, then
+//   policy 1x1 (C->2) + ReLU -> FC 162->82, value 1x1 (C->1) + ReLU ->
+//   FC 81->64 -> ReLU -> FC 64->1 -> tanh.
+//
+// Tower kernel (persistent, one CTA per SM, 192 threads):
+//   * Images are processed in groups of G whole images, so a CTA never needs
+//     another CTA's halo. Each image is stored as 100 rows (a 10x10 grid,
+//     row r*10+c; column 9 and row 9 are zero padding shared by neighbours),
+//     each row holding C channels in bf16.
+//   * A 3x3 convolution is 9 shifted GEMMs: for tap (dr,dc) the A operand is
+//     the same activation buffer shifted by dr*10+dc rows. With the K-major
+//     no-swizzle layout ([C/8 chunks][rows][8 channels], 16-byte rows) a row
+//     shift is just a 16-byte move of the descriptor's start address.
+//   * D[128 x C] accumulates in TMEM (fp32), 9 taps x C/16 MMAs of
+//     128 x C x 16 per 128-row tile, issued by one thread.
+//   * Weights stream from L2 into a ring of tap slots with bulk (TMA) copies
+//     (no multicast) so the next layer's taps arrive while this one runs.
+//   * Four epilogue warps drain TMEM (tcgen05.ld), add the folded-BN bias
+//     and the residual, apply ReLU, zero the padding rows and write the next
+//     layer's bf16 rows back to shared memory. The last layer's epilogue
+//     also computes the two 1x1 head convolutions (3 channels) in fp32.
+// Heads kernel: the fully connected heads and, in search mode, the masked
+// softmax, written straight into the PUCT workspace.
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+
+#include <cstdint>
+
+#include "../../include/gk.h"
+#include "gk_device.cuh"
+#include "gk_launch.cuh"
+#include "gk_puct.cuh"
+#include "gk_tc.cuh"
+
+namespace gk {
+
+template <int C>
+struct NetCfg {
+    static_assert(C == 64 || C == 128, "channels must be 64 or 128");
+    static constexpr int G = C == 64 ? 5 : 2;    // images per group
+    static constexpr int T = C == 64 ? 4 : 2;    // 128-row tiles per group (>= 100*G rows)
+    static constexpr int HALO = 11;              // max |tap row shift| = 10 + 1
+    static constexpr int ROWS = T * 128 + 2 * HALO;
+    static constexpr int CHUNK = ROWS * 16;      // bytes between 8-channel chunks
+    static constexpr int ACT = (C / 8) * CHUNK;  // one activation buffer
+    static constexpr int SLOT = C * C * 2;       // one tap of weights (bf16)
+    static constexpr int NSLOT = C == 64 ? 11 : 2;
+    static constexpr bool TILE_OUTER = C == 64;  // all 9 taps resident: tile-major issue order
+    static constexpr int NBARS = 2 * NSLOT + 2 * T + 1;
+    static constexpr int SMEM = 2 * ACT + NSLOT * SLOT + NBARS * 8 + 16;
+    static constexpr uint32_t IDESC = tc::idesc_bf16(128, C);
+    static_assert(2 * T * C <= 512, "two layers of accumulators must fit in TMEM");
+};
+
+struct NetParams {
+    int channels, blocks;
+    const uint8_t* conv_w;  // per layer, per tap: [Cin/8][Cout][8] bf16 (stem Cin padded to 16)
+    const float* conv_b;    // [layers][C]
+    const float* head_w;    // [3][C]: policy 1x1 (2 rows) then value 1x1 (BN folded)
+    const float* head_b;    // [3]
+    const float* pol_w;     // [82][162]
+    const float* pol_b;     // [82]
+    const float* val_w1;    // [64][81]
+    const float* val_b1;    // [64]
+    const float* val_w2;    // [64]
+    const float* val_b2;    // [1]
+};
+
+struct NetInput {
+    const gk_bits* states;    // packed states, or null
+    const float* features;    // fp32 [N][10][81], or null
+    const int32_t* index;     // optional gather: image i reads slot index[i]
+    const int32_t* count_ptr; // optional device-side count (<= n)
+    int64_t n;
+};
+
+__device__ __forceinline__ uint32_t pack_bf16x2(float a, float b) {
+    const __nv_bfloat162 v = __floats2bfloat162_rn(a, b);
+    return *reinterpret_cast<const uint32_t*>(&v);
+}
+
+__device__ __forceinline__ float bf16_lo(uint32_t w) { return __uint_as_float(w << 16); }
+__device__ __forceinline__ float bf16_hi(uint32_t w) { return __uint_as_float(w & 0xffff0000u); }
+
+__device__ __forceinline__ int input_count(const NetInput& in) {
+    int64_t n = in.n;
+    if (in.count_ptr) {
+        const int64_t c = *in.count_ptr;
+        n = c < n ? c : n;
+    }
+    return (int)(n < 0 ? 0 : n);
+}
+
+// Stem input row m of a group: 10 planes as bf16 (channels 10-15 zero).
+template <int C>
+__device__ __forceinline__ void build_input_row(uint8_t* buf, int m, int base_img, int nimg, const NetInput& in) {
+    using K = NetCfg<C>;
+    const int img = m / 100, pos = m - img * 100, r = pos / 10, c = pos - r * 10;
+    uint4 lo = make_uint4(0, 0, 0, 0), hi = make_uint4(0, 0, 0, 0);
+    if (img < nimg && r < 9 && c < 9) {
+        const int idx = base_img + img;
+        const int src = in.index ? in.index[idx] : idx;
+        float v[10];
+        if (in.states) {
+            const gk_bits s = in.states[src];
+            const EncodePlanes e = encode_planes(s);
+            const int bit = r * 10 + c;
+            v[0] = (float)gk_test(e.own, bit);
+            v[1] = (float)gk_test(e.enemy, bit);
+            v[2] = (float)gk_test(e.neutral, bit);
+            v[3] = (float)gk_test(e.own_terr, bit);
+            v[4] = (float)gk_test(e.enemy_terr, bit);
+            v[5] = e.black_to_play;
+            v[6] = e.own_remaining;
+            v[7] = e.enemy_remaining;
+            v[8] = e.passes;
+            v[9] = (float)gk_test(e.legal, bit);
+        } else {
+            const float* f = in.features + (int64_t)src * GK_FEATURES + r * 9 + c;
+#pragma unroll
+            for (int k = 0; k < 10; ++k) v[k] = f[k * GK_CELLS];
+        }
+        lo = make_uint4(pack_bf16x2(v[0], v[1]), pack_bf16x2(v[2], v[3]), pack_bf16x2(v[4], v[5]),
+                        pack_bf16x2(v[6], v[7]));
+        hi = make_uint4(pack_bf16x2(v[8], v[9]), 0u, 0u, 0u);
+    }
+    *reinterpret_cast<uint4*>(buf + (K::HALO + m) * 16) = lo;
+    *reinterpret_cast<uint4*>(buf + K::CHUNK + (K::HALO + m) * 16) = hi;
+}
+
+template <int C>
+__global__ void __launch_bounds__(192, 1)
+    net_tower_kernel(NetParams p, NetInput in, float* headfeat, uint32_t* status) {
+    using K = NetCfg<C>;
+    extern __shared__ __align__(1024) uint8_t smem[];
+    uint8_t* const bufP = smem;
+    uint8_t* const bufQ = smem + K::ACT;
+    uint8_t* const slots = smem + 2 * K::ACT;
+    uint64_t* const bars = reinterpret_cast<uint64_t*>(slots + K::NSLOT * K::SLOT);
+    uint32_t* const tmem_holder = reinterpret_cast<uint32_t*>(bars + K::NBARS);
+    const uint32_t slot_full = tc::smem_u32(bars);
+    const uint32_t slot_free = slot_full + 8 * K::NSLOT;
+    const uint32_t acc_full = slot_free + 8 * K::NSLOT;
+    const uint32_t epi_done = acc_full + 8 * K::T;
+    const uint32_t mma_idle = epi_done + 8 * K::T;
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int NL = 1 + 2 * p.blocks;  // MMA layers per group
+    const int count = input_count(in);
+    const int groups = (count + K::G - 1) / K::G;
+
+    // Zero both activation buffers (halo and padding rows stay zero forever).
+    for (int i = threadIdx.x; i < 2 * K::ACT / 16; i += blockDim.x)
+        reinterpret_cast<uint4*>(smem)[i] = make_uint4(0, 0, 0, 0);
+    tc::fence_proxy_async_smem();
+    if (threadIdx.x == 0) {
+        // epi_done completes when all four epilogue warps have arrived.
+        for (int b = 0; b < K::NBARS; ++b) {
+            const uint32_t bar = slot_full + 8 * b;
+            tc::mbar_init(bar, bar >= epi_done && bar < mma_idle ? 4u : 1u);
+        }
+        tc::fence_mbar_init();
+    }
+    if (warp == 0) {
+        tc::tmem_alloc(tc::smem_u32(tmem_holder), 512);
+        tc::tmem_relinquish();
+    }
+    tc::tc_fence_before();
+    __syncthreads();
+    tc::tc_fence_after();
+    const uint32_t tmem = *tmem_holder;
+
+    if (warp == 0 && lane == 0) {
+        // ---------------- weight producer ----------------
+        int c = 0;
+        for (int g = blockIdx.x; g < groups; g += gridDim.x) {
+            for (int l = 0; l < NL; ++l) {
+                for (int tap = 0; tap < 9; ++tap, ++c) {
+                    const int slot = c % K::NSLOT, round = c / K::NSLOT;
+                    if (round > 0 && !tc::mbar_wait(slot_free + 8 * slot, (round - 1) & 1, status)) goto done;
+                    const uint32_t bytes = l == 0 ? 16u * C * 2u : (uint32_t)K::SLOT;
+                    const uint8_t* src = l == 0 ? p.conv_w + tap * bytes
+                                                : p.conv_w + 9 * 16 * C * 2 + ((size_t)(l - 1) * 9 + tap) * K::SLOT;
+                    tc::mbar_expect_tx(slot_full + 8 * slot, bytes);
+                    tc::bulk_g2s(tc::smem_u32(slots + slot * K::SLOT), src, bytes, slot_full + 8 * slot);
+                }
+            }
+        }
+    } else if (warp == 1 && lane == 0) {
+        // ---------------- MMA issuer ----------------
+        int c = 0, i = 0;
+        for (int g = blockIdx.x; g < groups; g += gridDim.x, ++i) {
+            for (int l = 0; l < NL; ++l) {
+                const int a = i * NL + l;                  // accumulator phase index
+                const uint32_t epi_parity = (uint32_t)(i * NL + l) & 1u;  // epilogue layer l of group i
+                const uint32_t colbase = (uint32_t)((a & 1) * K::T * C);
+                const uint32_t in_buf = tc::smem_u32(l % 2 == 0 ? bufQ : bufP);
+                const int ksteps = l == 0 ? 1 : C / 16;
+                if (K::TILE_OUTER) {
+                    for (int t = 0; t < K::T; ++t) {
+                        // Input rows of tile t come from tiles t-1..t+1 of the previous epilogue.
+                        for (int nb = (t == 0 ? 0 : t + 1); nb <= t + 1 && nb < K::T; ++nb)
+                            if (!tc::mbar_wait(epi_done + 8 * nb, epi_parity, status)) goto mma_done;
+                        tc::tc_fence_after();
+                        for (int tap = 0; tap < 9; ++tap) {
+                            const int cc = c + tap, slot = cc % K::NSLOT;
+                            if (t == 0) {
+                                if (!tc::mbar_wait(slot_full + 8 * slot, (uint32_t)(cc / K::NSLOT) & 1u, status))
+                                    goto mma_done;
+                                tc::tc_fence_after();
+                            }
+                            const int off = (tap / 3 - 1) * 10 + (tap % 3 - 1);
+                            const uint32_t a_addr = in_buf + (uint32_t)((K::HALO + t * 128 + off) * 16);
+                            const uint32_t b_addr = tc::smem_u32(slots + slot * K::SLOT);
+                            for (int s = 0; s < ksteps; ++s)
+                                tc::mma_bf16(tmem + colbase + t * C,
+                                             tc::smem_desc(a_addr + 2 * s * K::CHUNK, K::CHUNK, 128),
+                                             tc::smem_desc(b_addr + 2 * s * C * 16, C * 16, 128), K::IDESC,
+                                             (tap | s) != 0);
+                            if (t == K::T - 1) tc::mma_commit(slot_free + 8 * slot);
+                        }
+                        tc::mma_commit(acc_full + 8 * t);
+                    }
+                } else {
+                    for (int tap = 0; tap < 9; ++tap) {
+                        const int cc = c + tap, slot = cc % K::NSLOT;
+                        if (!tc::mbar_wait(slot_full + 8 * slot, (uint32_t)(cc / K::NSLOT) & 1u, status)) goto mma_done;
+                        tc::tc_fence_after();
+                        const int off = (tap / 3 - 1) * 10 + (tap % 3 - 1);
+                        const uint32_t b_addr = tc::smem_u32(slots + slot * K::SLOT);
+                        for (int t = 0; t < K::T; ++t) {
+                            if (tap == 0) {
+                                for (int nb = (t == 0 ? 0 : t + 1); nb <= t + 1 && nb < K::T; ++nb)
+                                    if (!tc::mbar_wait(epi_done + 8 * nb, epi_parity, status)) goto mma_done;
+                                tc::tc_fence_after();
+                            }
+                            const uint32_t a_addr = in_buf + (uint32_t)((K::HALO + t * 128 + off) * 16);
+                            for (int s = 0; s < ksteps; ++s)
+                                tc::mma_bf16(tmem + colbase + t * C,
+                                             tc::smem_desc(a_addr + 2 * s * K::CHUNK, K::CHUNK, 128),
+                                             tc::smem_desc(b_addr + 2 * s * C * 16, C * 16, 128), K::IDESC,
+                                             (tap | s) != 0);
+                            if (tap == 8) tc::mma_commit(acc_full + 8 * t);
+                        }
+                        tc::mma_commit(slot_free + 8 * slot);
+                    }
+                }
+                c += 9;
+            }
+        }
+    mma_done:
+        // Drain: every MMA issued above completes before TMEM is released.
+        tc::mma_commit(mma_idle);
+        tc::mbar_wait(mma_idle, 0, status);
+    } else if (warp >= 2) {
+        // ---------------- epilogue (4 warps, one TMEM lane quadrant each) ----------------
+        const int q = warp & 3;
+        const int etid = threadIdx.x - 64;
+        int i = 0;
+        for (int g = blockIdx.x; g < groups; g += gridDim.x, ++i) {
+            const int base_img = g * K::G;
+            const int nimg = count - base_img < K::G ? count - base_img : K::G;
+            // Epilogue layer 0: build the stem input (channels 0-15 of buffer Q).
+            for (int m = etid; m < K::T * 128; m += 128) build_input_row<C>(bufQ, m, base_img, nimg, in);
+            tc::fence_proxy_async_smem();
+            __syncwarp();
+            if (lane == 0)
+                for (int t = 0; t < K::T; ++t) tc::mbar_arrive(epi_done + 8 * t);
+            for (int l = 0; l < NL; ++l) {
+                const int a = i * NL + l;
+                const uint32_t colbase = (uint32_t)((a & 1) * K::T * C);
+                uint8_t* const out = l % 2 == 0 ? bufP : bufQ;
+                const bool residual = l >= 2 && l % 2 == 0;
+                const bool last = l == NL - 1;
+                const float* bias = p.conv_b + l * C;
+                for (int t = 0; t < K::T; ++t) {
+                    if (!tc::mbar_wait(acc_full + 8 * t, (uint32_t)a & 1u, status)) goto epi_done_label;
+                    tc::tc_fence_after();
+                    const int m = t * 128 + q * 32 + lane;
+                    const int img = m / 100, pos = m - img * 100, r = pos / 10, cc = pos - r * 10;
+                    const bool valid = img < nimg && r < 9 && cc < 9;
+                    uint8_t* const row = out + (K::HALO + m) * 16;
+                    float h0 = 0.f, h1 = 0.f, h2 = 0.f;
+#pragma unroll 1
+                    for (int cb = 0; cb < C / 32; ++cb) {
+                        float v[32];
+                        tc::tmem_ld32(tmem + ((uint32_t)(q * 32) << 16) + colbase + t * C + cb * 32, v);
+                        uint4 res[4];
+                        if (residual) {
+#pragma unroll
+                            for (int k = 0; k < 4; ++k)
+                                res[k] = *reinterpret_cast<const uint4*>(row + (cb * 4 + k) * K::CHUNK);
+                        }
+#pragma unroll
+                        for (int j = 0; j < 32; ++j) {
+                            float x = v[j] + __ldg(bias + cb * 32 + j);
+                            if (residual) {
+                                const uint4 rv = res[j >> 3];
+                                const uint32_t w = (j & 7) < 2 ? rv.x : (j & 7) < 4 ? rv.y : (j & 7) < 6 ? rv.z : rv.w;
+                                x += (j & 1) ? bf16_hi(w) : bf16_lo(w);
+                            }
+                            x = valid ? fmaxf(x, 0.0f) : 0.0f;
+                            v[j] = x;
+                        }
+                        if (last) {
+#pragma unroll
+                            for (int j = 0; j < 32; ++j) {
+                                const int ch = cb * 32 + j;
+                                h0 = fmaf(v[j], __ldg(p.head_w + ch), h0);
+                                h1 = fmaf(v[j], __ldg(p.head_w + C + ch), h1);
+                                h2 = fmaf(v[j], __ldg(p.head_w + 2 * C + ch), h2);
+                            }
+                        } else {
+#pragma unroll
+                            for (int k = 0; k < 4; ++k) {
+                                const uint4 o = make_uint4(pack_bf16x2(v[8 * k], v[8 * k + 1]),
+                                                           pack_bf16x2(v[8 * k + 2], v[8 * k + 3]),
+                                                           pack_bf16x2(v[8 * k + 4], v[8 * k + 5]),
+                                                           pack_bf16x2(v[8 * k + 6], v[8 * k + 7]));
+                                *reinterpret_cast<uint4*>(row + (cb * 4 + k) * K::CHUNK) = o;
+                            }
+                        }
+                    }
+                    if (last) {
+                        if (valid) {
+                            float* hf = headfeat + (int64_t)(base_img + img) * 243 + r * 9 + cc;
+                            hf[0] = fmaxf(h0 + __ldg(p.head_b + 0), 0.0f);
+                            hf[81] = fmaxf(h1 + __ldg(p.head_b + 1), 0.0f);
+                            hf[162] = fmaxf(h2 + __ldg(p.head_b + 2), 0.0f);
+                        }
+                        tc::tc_fence_before();
+                    } else {
+                        tc::fence_proxy_async_smem();
+                        tc::tc_fence_before();
+                        __syncwarp();
+                        if (lane == 0) tc::mbar_arrive(epi_done + 8 * t);
+                    }
+                }
+            }
+        }
+    epi_done_label:;
+    }
+done:
+    tc::tc_fence_before();
+    __syncthreads();
+    if (warp == 0) {
+        tc::tc_fence_after();
+        tc::tmem_dealloc(tmem, 512);
+    }
+}
+
+// ---- fully connected heads -------------------------------------------------------
+struct HeadOut {
+    float* logits;       // raw mode: [n][82]
+    float* values;       // raw mode: [n]
+    float* policy;       // search mode: [B][82] masked softmax, row index[i]
+    float* leaf_value;   // search mode: [B]
+    const gk_bits* states;  // search mode: leaf states for the legal mask
+};
+
+constexpr int kPolStride = 163;  // odd row stride: conflict-free lane-per-row reads
+constexpr int kValStride = 81;
+constexpr size_t kHeadSmem = (size_t)(82 * kPolStride + 64 * kValStride + 8 * 244) * sizeof(float);
+
+__global__ void __launch_bounds__(256) net_heads_kernel(NetParams p, const float* headfeat, NetInput in, HeadOut out) {
+    extern __shared__ float hs[];
+    float* wp = hs;
+    float* w1 = wp + 82 * kPolStride;
+    float* feat_all = w1 + 64 * kValStride;
+    for (int i = threadIdx.x; i < 82 * 162; i += blockDim.x) wp[(i / 162) * kPolStride + i % 162] = p.pol_w[i];
+    for (int i = threadIdx.x; i < 64 * 81; i += blockDim.x) w1[i] = p.val_w1[i];
+    __syncthreads();
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    float* feat = feat_all + warp * 244;
+    const int count = input_count(in);
+    for (int img = blockIdx.x * 8 + warp; img < count; img += gridDim.x * 8) {
+        const float* hf = headfeat + (int64_t)img * 243;
+        for (int k = lane; k < 243; k += 32) feat[k] = hf[k];
+        __syncwarp();
+        float logit[3];
+#pragma unroll
+        for (int k = 0; k < 3; ++k) {
+            const int a = lane + 32 * k;
+            float acc = 0.f;
+            if (a < GK_ACTIONS) {
+                const float* w = wp + a * kPolStride;
+                for (int j = 0; j < 162; ++j) acc = fmaf(w[j], feat[j], acc);
+                acc += __ldg(p.pol_b + a);
+            }
+            logit[k] = acc;
+        }
+        float vpart = 0.f;
+#pragma unroll
+        for (int k = 0; k < 2; ++k) {
+            const int u = lane + 32 * k;
+            const float* w = w1 + u * kValStride;
+            float acc = __ldg(p.val_b1 + u);
+            for (int j = 0; j < 81; ++j) acc = fmaf(w[j], feat[162 + j], acc);
+            vpart = fmaf(fmaxf(acc, 0.f), __ldg(p.val_w2 + u), vpart);
+        }
+#pragma unroll
+        for (int off = 16; off; off >>= 1) vpart += __shfl_xor_sync(0xffffffffu, vpart, off);
+        const float value = tanhf(vpart + __ldg(p.val_b2));
+        if (out.logits) {
+#pragma unroll
+            for (int k = 0; k < 3; ++k)
+                if (lane + 32 * k < GK_ACTIONS) out.logits[(int64_t)img * GK_ACTIONS + lane + 32 * k] = logit[k];
+            if (lane == 0) out.values[img] = value;
+        } else {
+            // Masked softmax over the leaf's legal actions (gpu_puct.py:500-501).
+            const int tree = in.index ? in.index[img] : img;
+            const gk_bits s = out.states[tree];
+            const gk_b96 placements = legal_placements(s);
+            bool legal[3];
+            float mx = -INFINITY;
+#pragma unroll
+            for (int k = 0; k < 3; ++k) {
+                const int a = lane + 32 * k;
+                legal[k] = a < GK_ACTIONS && (a == GK_PASS ? true : gk_test(placements, a + a / 9) != 0);
+                if (legal[k]) mx = fmaxf(mx, logit[k]);
+            }
+#pragma unroll
+            for (int off = 16; off; off >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
+            float e[3], sum = 0.f;
+#pragma unroll
+            for (int k = 0; k < 3; ++k) {
+                e[k] = legal[k] ? __expf(logit[k] - mx) : 0.f;
+                sum += e[k];
+            }
+#pragma unroll
+            for (int off = 16; off; off >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, off);
+#pragma unroll
+            for (int k = 0; k < 3; ++k)
+                if (lane + 32 * k < GK_ACTIONS) out.policy[(int64_t)tree * GK_ACTIONS + lane + 32 * k] = e[k] / sum;
+            if (lane == 0) out.leaf_value[tree] = value;
+        }
+        __syncwarp();
+    }
+}
+
+// ---- tensor-core self-test ---------------------------------------------------------
+// One 128x64x16 bf16 MMA from operands staged in the same K-major no-swizzle
+// layout the tower uses (A: chunk stride 2048 B, B: chunk stride 1024 B, 8-row
+// groups 128 B apart). The operands sit in a 64 KB buffer sized so that every
+// address stays inside it even if the two descriptor strides were read the
+// other way round; the result is compared on the host.
+constexpr int kSelfTestSmem = 65536;
+
+__global__ void __launch_bounds__(128, 1)
+    mma_selftest_kernel(const uint16_t* a, const uint16_t* b, float* d, uint32_t* status) {
+    extern __shared__ __align__(1024) uint8_t smem[];
+    __shared__ __align__(8) uint64_t bar;
+    __shared__ uint32_t tmem_holder;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    for (int i = threadIdx.x; i < kSelfTestSmem / 16; i += blockDim.x)
+        reinterpret_cast<uint4*>(smem)[i] = make_uint4(0, 0, 0, 0);
+    __syncthreads();
+    // A[m][k] (128 x 16) -> chunk (k/8) at 2048*(k/8) + 16*m; B[n][k] (64 x 16) at 32768 + 1024*(k/8) + 16*n.
+    for (int i = threadIdx.x; i < 128 * 16; i += blockDim.x) {
+        const int m = i / 16, k = i % 16;
+        reinterpret_cast<uint16_t*>(smem + 2048 * (k / 8) + 16 * m)[k % 8] = a[i];
+    }
+    for (int i = threadIdx.x; i < 64 * 16; i += blockDim.x) {
+        const int n = i / 16, k = i % 16;
+        reinterpret_cast<uint16_t*>(smem + 32768 + 1024 * (k / 8) + 16 * n)[k % 8] = b[i];
+    }
+    tc::fence_proxy_async_smem();
+    const uint32_t barp = tc::smem_u32(&bar);
+    if (threadIdx.x == 0) {
+        tc::mbar_init(barp, 1);
+        tc::fence_mbar_init();
+    }
+    if (warp == 0) {
+        tc::tmem_alloc(tc::smem_u32(&tmem_holder), 512);
+        tc::tmem_relinquish();
+    }
+    tc::tc_fence_before();
+    __syncthreads();
+    tc::tc_fence_after();
+    const uint32_t tmem = tmem_holder;
+    if (threadIdx.x == 0) {
+        const uint32_t base = tc::smem_u32(smem);
+        tc::mma_bf16(tmem, tc::smem_desc(base, 2048, 128), tc::smem_desc(base + 32768, 1024, 128),
+                     tc::idesc_bf16(128, 64), 0);
+        tc::mma_commit(barp);
+    }
+    __syncwarp();
+    const bool ok = tc::mbar_wait(barp, 0, status);
+    tc::tc_fence_after();
+    if (ok) {
+#pragma unroll 1
+        for (int cb = 0; cb < 2; ++cb) {
+            float v[32];
+            tc::tmem_ld32(tmem + ((uint32_t)(warp * 32) << 16) + cb * 32, v);
+            const int m = warp * 32 + lane;
+            for (int j = 0; j < 32; ++j) d[m * 64 + cb * 32 + j] = v[j];
+        }
+    }
+    tc::tc_fence_before();
+    __syncthreads();
+    if (warp == 0) {
+        tc::tc_fence_after();
+        tc::tmem_dealloc(tmem, 512);
+    }
+}
+
+inline NetParams make_params(const gk_net_t* net) {
+    NetParams p;
+    p.channels = net->channels;
+    p.blocks = net->blocks;
+    p.conv_w = static_cast<const uint8_t*>(net->conv_w);
+    p.conv_b = net->conv_b;
+    p.head_w = net->head_w;
+    p.head_b = net->head_b;
+    p.pol_w = net->pol_w;
+    p.pol_b = net->pol_b;
+    p.val_w1 = net->val_w1;
+    p.val_b1 = net->val_b1;
+    p.val_w2 = net->val_w2;
+    p.val_b2 = net->val_b2;
+    return p;
+}
+
+template <int C>
+int launch_tower(const NetParams& p, const NetInput& in, float* headfeat, uint32_t* status, cudaStream_t stream) {
+    using K = NetCfg<C>;
+    static bool done[64] = {};
+    if (!once_per_device(done, [] {
+            return cudaFuncSetAttribute(net_tower_kernel<C>, cudaFuncAttributeMaxDynamicSharedMemorySize, K::SMEM) ==
+                   cudaSuccess;
+        }))
+        return launch_status();
+    const int64_t groups = (in.n + K::G - 1) / K::G;
+    const int grid = (int)(groups < kSmCount ? groups : kSmCount);
+    net_tower_kernel<C><<<grid < 1 ? 1 : grid, 192, K::SMEM, stream>>>(p, in, headfeat, status);
+    return launch_status();
+}
+
+int launch_heads(const NetParams& p, const float* headfeat, const NetInput& in, const HeadOut& out,
+                 cudaStream_t stream) {
+    static bool done[64] = {};
+    if (!once_per_device(done, [] {
+            return cudaFuncSetAttribute(net_heads_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                        (int)kHeadSmem) == cudaSuccess;
+        }))
+        return launch_status();
+    int64_t blocks = (in.n + 7) / 8;
+    if (blocks > 2 * kSmCount) blocks = 2 * kSmCount;
+    net_heads_kernel<<<(int)(blocks < 1 ? 1 : blocks), 256, kHeadSmem, stream>>>(p, headfeat, in, out);
+    return launch_status();
+}
+
+inline bool valid_net(const gk_net_t* net) {
+    return net && (net->channels == 64 || net->channels == 128) && net->blocks >= 0 && net->blocks <= 64 &&
+           net->conv_w && net->conv_b && net->head_w && net->head_b && net->pol_w && net->pol_b && net->val_w1 &&
+           net->val_b1 && net->val_w2 && net->val_b2 && aligned16(net->conv_w);
+}
+
+int run_forward(const gk_net_t* net, const NetInput& in, float* headfeat, const HeadOut& out, uint32_t* status,
+                cudaStream_t stream) {
+    const NetParams p = make_params(net);
+    const int s = net->channels == 64 ? launch_tower<64>(p, in, headfeat, status, stream)
+                                      : launch_tower<128>(p, in, headfeat, status, stream);
+    if (s) return s;
+    return launch_heads(p, headfeat, in, out, stream);
+}
+
+}  // namespace gk
+
+using namespace gk;
+
+extern "C" {
+
+size_t gk_net_weight_bytes(int channels, int blocks) {
+    if ((channels != 64 && channels != 128) || blocks < 0) return 0;
+    return (size_t)9 * 16 * channels * 2 + (size_t)blocks * 2 * 9 * channels * channels * 2;
+}
+
+size_t gk_net_headfeat_bytes(int64_t n) { return n <= 0 ? 0 : (size_t)n * 243 * sizeof(float); }
+
+int gk_mma_selftest(const uint16_t* a, const uint16_t* b, float* d, uint32_t* status, void* stream) {
+    if (a == nullptr || b == nullptr || d == nullptr || status == nullptr) return GK_EINVAL;
+    static bool done[64] = {};
+    if (!once_per_device(done, [] {
+            return cudaFuncSetAttribute(mma_selftest_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                        kSelfTestSmem) == cudaSuccess;
+        }))
+        return launch_status();
+    mma_selftest_kernel<<<1, 128, kSelfTestSmem, as_stream(stream)>>>(a, b, d, status);
+    return launch_status();
+}
+
+int gk_net_forward(const gk_net_t* net, const uint32_t* states, const float* features, int64_t n, float* headfeat,
+                   float* logits, float* values, uint32_t* status, void* stream) {
+    if (!valid_net(net) || n < 0 || headfeat == nullptr || logits == nullptr || values == nullptr ||
+        status == nullptr || (states == nullptr) == (features == nullptr))
+        return GK_EINVAL;
+    if (n == 0) return 0;
+    NetInput in{reinterpret_cast<const gk_bits*>(states), features, nullptr, nullptr, n};
+    HeadOut out{logits, values, nullptr, nullptr, nullptr};
+    return run_forward(net, in, headfeat, out, status, as_stream(stream));
+}
+
+int gk_net_evaluate_puct(const gk_net_t* net, void* ws, int64_t batch, int capacity, float* headfeat,
+                         uint32_t* status, void* stream) {
+    if (!valid_net(net) || ws == nullptr || batch <= 0 || capacity < 1 || headfeat == nullptr || status == nullptr)
+        return GK_EINVAL;
+    int s = gk_puct_compact(ws, batch, capacity, stream);
+    if (s) return s;
+    PuctView v;
+    puct_layout(ws, batch, capacity, &v);
+    NetInput in{v.leaf_bits, nullptr, v.active, v.active_count, batch};
+    HeadOut out{nullptr, nullptr, v.policy, v.leaf_value, v.leaf_bits};
+    return run_forward(net, in, headfeat, out, status, as_stream(stream));
+}
+
+}  // extern "C"

@@ -43,6 +43,12 @@ class PuctResults(ctypes.Structure):
                 ("status", c_void_p)]
 
 
+class NetStruct(ctypes.Structure):
+    _fields_ = [("channels", c_int), ("blocks", c_int), ("conv_w", c_void_p), ("conv_b", c_void_p),
+                ("head_w", c_void_p), ("head_b", c_void_p), ("pol_w", c_void_p), ("pol_b", c_void_p),
+                ("val_w1", c_void_p), ("val_b1", c_void_p), ("val_w2", c_void_p), ("val_b2", c_void_p)]
+
+
 _SIGNATURES = {
     "gk_initial_records": [c_void_p, c_int64, c_int, c_void_p],
     "gk_initial_bits": [c_void_p, c_int64, c_int, c_void_p],
@@ -64,9 +70,15 @@ _SIGNATURES = {
     "gk_puct_finish": [c_void_p, c_int64, c_int, ctypes.POINTER(PuctResults), c_void_p],
     "gk_puct_search_hash": [c_void_p, c_int64, c_int, c_void_p, ctypes.POINTER(PuctOptions),
                             ctypes.POINTER(PuctResults), c_void_p],
+    "gk_mma_selftest": [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p],
+    "gk_net_forward": [ctypes.POINTER(NetStruct), c_void_p, c_void_p, c_int64, c_void_p, c_void_p, c_void_p,
+                       c_void_p, c_void_p],
+    "gk_net_evaluate_puct": [ctypes.POINTER(NetStruct), c_void_p, c_int64, c_int, c_void_p, c_void_p, c_void_p],
 }
 _SIZE_FUNCTIONS = {
     "gk_puct_workspace_bytes": [c_int64, c_int],
+    "gk_net_weight_bytes": [c_int, c_int],
+    "gk_net_headfeat_bytes": [c_int64],
 }
 
 _lock = threading.Lock()

@@ -159,6 +159,10 @@ class GpuPUCT:
         elif isinstance(model, nn.Module):
             self.model = copy.deepcopy(model).to(device=self.device, dtype=torch.float32).eval()
             self._kind = "module"
+            from .model import NativePolicyValueNet, PolicyValueNet
+            if type(self.model) is PolicyValueNet and self.model.channels in (64, 128):
+                self._native_net = NativePolicyValueNet(self.model.cpu(), device=self.device)
+                self._kind = "native"
         else:
             raise TypeError("model must be a torch.nn.Module or a HashEvaluator")
         native.library()
@@ -254,6 +258,8 @@ class GpuPUCT:
         out = _allocate_results(batch, device)
         native.call("gk_puct_finish", ws.pointer, batch, capacity, out.struct, stream)
         code = int(out.status.item())
+        if self._kind == "native":
+            self._native_net.check()
         if code:
             if code & 2:
                 raise ValueError("PUCT model must return finite logits and finite values in [-1, 1]")

@@ -101,3 +101,106 @@ def fold(conv: nn.Conv2d, bn: nn.BatchNorm2d):
     weight = conv.weight * scale.reshape(-1, *([1] * (conv.weight.dim() - 1)))
     bias = bn.bias - bn.running_mean * scale
     return weight.detach().float(), bias.detach().float()
+
+
+# ---------------------------------------------------------------------------
+# Native (sm_100a) network
+# ---------------------------------------------------------------------------
+
+def _pack_conv(weight: torch.Tensor, cin_pad: int) -> torch.Tensor:
+    """[Cout][Cin][3][3] fp32 -> per tap (row-major over (dr, dc)) bf16 [Cin/8][Cout][8]."""
+    cout, cin = weight.shape[:2]
+    w = torch.zeros((cout, cin_pad, 3, 3), dtype=torch.float32)
+    w[:, :cin] = weight
+    taps = w.permute(2, 3, 1, 0).reshape(9, cin_pad, cout)          # [tap][k][n]
+    taps = taps.reshape(9, cin_pad // 8, 8, cout).permute(0, 1, 3, 2)  # [tap][k/8][n][k%8]
+    return taps.contiguous().to(torch.bfloat16)
+
+
+class NativePolicyValueNet:
+    """A PolicyValueNet packed for the tcgen05 kernels (BN folded, bf16 convs).
+
+    ``forward_states`` / ``forward_features`` return raw logits [N,82] and
+    values [N] (fp32); ``evaluate_workspace`` is the in-search leaf evaluator.
+    Convolutions run in bf16 with fp32 accumulation; the 1x1 head convolutions
+    and the fully connected heads run in fp32.
+    """
+
+    def __init__(self, model: PolicyValueNet, device="cuda"):
+        from . import _native as native
+        self.native = native
+        self.device = torch.device(device)
+        if model.channels not in (64, 128):
+            raise ValueError("the native network supports 64 or 128 channels")
+        self.channels, self.blocks = model.channels, model.residual_blocks
+        model = model.eval()
+        with torch.no_grad():
+            convs = [fold(model.stem, model.stem_bn)]
+            for block in model.blocks:
+                convs.append(fold(block.conv1, block.bn1))
+                convs.append(fold(block.conv2, block.bn2))
+            packed = [_pack_conv(convs[0][0].cpu(), 16)] + [_pack_conv(w.cpu(), self.channels) for w, _ in convs[1:]]
+            conv_w = torch.cat([p.reshape(-1) for p in packed])
+            pw, pb = fold(model.policy_conv, model.policy_bn)
+            vw, vb = fold(model.value_conv, model.value_bn)
+            head_w = torch.cat([pw.reshape(2, -1), vw.reshape(1, -1)]).float()
+            head_b = torch.cat([pb, vb]).float()
+            tensors = {
+                "conv_w": conv_w,
+                "conv_b": torch.stack([b for _, b in convs]).float(),
+                "head_w": head_w, "head_b": head_b,
+                "pol_w": model.policy_fc.weight.detach().float(), "pol_b": model.policy_fc.bias.detach().float(),
+                "val_w1": model.value_fc1.weight.detach().float(), "val_b1": model.value_fc1.bias.detach().float(),
+                "val_w2": model.value_fc2.weight.detach().float().reshape(-1),
+                "val_b2": model.value_fc2.bias.detach().float().reshape(-1),
+            }
+        expected = native.library().gk_net_weight_bytes(self.channels, self.blocks)
+        if conv_w.numel() * 2 != expected:
+            raise RuntimeError("packed weight size mismatch")
+        self.tensors = {k: v.to(self.device).contiguous() for k, v in tensors.items()}
+        t = self.tensors
+        self.struct = native.NetStruct(
+            self.channels, self.blocks, t["conv_w"].data_ptr(), t["conv_b"].data_ptr(), t["head_w"].data_ptr(),
+            t["head_b"].data_ptr(), t["pol_w"].data_ptr(), t["pol_b"].data_ptr(), t["val_w1"].data_ptr(),
+            t["val_b1"].data_ptr(), t["val_w2"].data_ptr(), t["val_b2"].data_ptr())
+        self._headfeat = None
+        self.status = torch.zeros(1, dtype=torch.int32, device=self.device)
+
+    def _workspace(self, n):
+        if self._headfeat is None or self._headfeat.shape[0] < n:
+            self._headfeat = torch.empty((n, 243), dtype=torch.float32, device=self.device)
+        return self._headfeat
+
+    def _forward(self, states, features, n):
+        native = self.native
+        logits = torch.empty((n, ACTION_SIZE), dtype=torch.float32, device=self.device)
+        values = torch.empty((n,), dtype=torch.float32, device=self.device)
+        headfeat = self._workspace(n)
+        with torch.cuda.device(self.device):
+            stream = native.stream_of(self.device)
+            native.call("gk_net_forward", self.struct, native.ptr(states), native.ptr(features), n,
+                        native.ptr(headfeat), native.ptr(logits), native.ptr(values), native.ptr(self.status),
+                        stream)
+        return logits, values
+
+    def forward_states(self, bits: torch.Tensor):
+        """Packed states int32 [N,16] -> (logits [N,82], values [N])."""
+        bits = bits.to(self.device).contiguous()
+        return self._forward(bits, None, bits.shape[0])
+
+    def forward_features(self, features: torch.Tensor):
+        """Schema-1 features fp32 [N,10,9,9] -> (logits [N,82], values [N])."""
+        features = features.to(device=self.device, dtype=torch.float32).contiguous()
+        return self._forward(None, features, features.shape[0])
+
+    def evaluate_workspace(self, ws, stream):
+        """Fill the search workspace's policy/value for every leaf that needs it."""
+        headfeat = self._workspace(ws.batch)
+        self.native.call("gk_net_evaluate_puct", self.struct, ws.pointer, ws.batch, ws.capacity,
+                         self.native.ptr(headfeat), self.native.ptr(self.status), stream)
+
+    def check(self):
+        """Raise if any kernel reported a bounded wait that gave up."""
+        code = int(self.status.item())
+        if code:
+            raise RuntimeError(f"native network reported error bits {code:#x}")

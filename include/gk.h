@@ -174,6 +174,61 @@ GK_API int gk_puct_finish(void* ws, int64_t batch, int capacity, const gk_puct_r
 GK_API int gk_puct_search_hash(void* ws, int64_t batch, int simulations, const uint32_t* root_bits,
                         const gk_puct_options* options, const gk_puct_results_t* results, void* stream);
 
+/* -------------------------------------------------------------- network */
+
+/* Device pointers of a packed policy/value network (BN folded). Layout of
+ * conv_w: for each 3x3 layer (stem first, then two per residual block), for
+ * each of the 9 taps (row-major over (dr, dc)), bf16 [Cin/8][Cout][8]; the
+ * stem's Cin is padded from 10 to 16. conv_b: fp32 [layers][C]. head_w/head_b:
+ * the 1x1 policy (2 rows) and value (1 row) convolutions. The rest are the
+ * fully connected heads of python/kingdom_ai/model.py:51-69 (value hidden 64). */
+typedef struct {
+    int channels; /* 64 or 128 */
+    int blocks;   /* residual blocks */
+    const void* conv_w;
+    const float* conv_b;
+    const float* head_w; /* [3][C] */
+    const float* head_b; /* [3] */
+    const float* pol_w;  /* [82][162] */
+    const float* pol_b;  /* [82] */
+    const float* val_w1; /* [64][81] */
+    const float* val_b1; /* [64] */
+    const float* val_w2; /* [64] */
+    const float* val_b2; /* [1] */
+} gk_net_t;
+
+/* Tensor-core self-test: D[128,64] (fp32) = A[128,16] x B[64,16]^T (bf16 bit
+ * patterns, row-major) through one tcgen05.mma with the operand layout the
+ * network kernels use. No reference counterpart: a pre-flight check of the
+ * descriptor encodings, whose addresses stay in range by construction. */
+GK_API int gk_mma_selftest(const uint16_t* a, const uint16_t* b, float* d, uint32_t* status, void* stream);
+
+/* Bytes of packed bf16 convolution weights for this shape (0 if unsupported);
+ * the packed form of the reference model's conv parameters
+ * (python/kingdom_ai/model.py:43-50). */
+GK_API size_t gk_net_weight_bytes(int channels, int blocks);
+
+/* Bytes of the per-call head-feature workspace for n positions (the 1x1
+ * head convolution outputs of python/kingdom_ai/model.py:51-69). */
+GK_API size_t gk_net_headfeat_bytes(int64_t n);
+
+/* Network forward for n positions given either packed states (`states`,
+ * uint32[n,16]; the 10 observation planes are built on the fly) or schema-1
+ * features (fp32[n,10,9,9]); exactly one must be non-null. Writes raw policy
+ * logits fp32[n,82] and values fp32[n]. `headfeat` is workspace of
+ * gk_net_headfeat_bytes(n). Replaces the model forward of the reference's
+ * leaf evaluation (PolicyValueNet.forward, python/kingdom_ai/model.py:72-84,
+ * called from GpuPUCT._search, gpu_puct.py:485). */
+GK_API int gk_net_forward(const gk_net_t* net, const uint32_t* states, const float* features, int64_t n,
+                          float* headfeat, float* logits, float* values, uint32_t* status, void* stream);
+
+/* Leaf evaluation inside a search: compacts the trees whose leaf needs the
+ * network (device-side, no host synchronisation), runs the network on those
+ * leaves and writes the masked softmax policy and the value into the search
+ * workspace. Replaces GpuPUCT._search's evaluate() (gpu_puct.py:481-502). */
+GK_API int gk_net_evaluate_puct(const gk_net_t* net, void* ws, int64_t batch, int capacity, float* headfeat,
+                                uint32_t* status, void* stream);
+
 #ifdef __cplusplus
 }
 #endif
