@@ -95,6 +95,26 @@ def random_network(channels: int, blocks: int, seed: int) -> PolicyValueNet:
     return net.eval()
 
 
+def calibrate_batchnorm(model: PolicyValueNet, features: torch.Tensor) -> PolicyValueNet:
+    """Set every batch norm's running statistics from one pass over `features`.
+
+    A freshly initialised residual tower with arbitrary running statistics
+    grows its activations layer after layer; calibrated statistics normalise
+    each layer as a trained network's would, so the folded convolutions see
+    realistic value ranges.
+    """
+    bns = [m for m in model.modules() if isinstance(m, nn.BatchNorm2d)]
+    for bn in bns:
+        bn.reset_running_stats()
+        bn.momentum = None  # cumulative average over the calibration pass
+    model.train()
+    with torch.no_grad():
+        model(features)
+    for bn in bns:
+        bn.momentum = 0.1
+    return model.eval()
+
+
 def fold(conv: nn.Conv2d, bn: nn.BatchNorm2d):
     """Eval-mode BN folded into the preceding bias-free conv: (weight, bias) fp32."""
     scale = bn.weight / torch.sqrt(bn.running_var + bn.eps)
