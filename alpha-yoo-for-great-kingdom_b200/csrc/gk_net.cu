@@ -561,12 +561,27 @@ inline bool valid_net(const gk_net_t* net) {
 }
 
 int run_forward(const gk_net_t* net, const NetInput& in, float* headfeat, const HeadOut& out, uint32_t* status,
-                cudaStream_t stream) {
+                cudaStream_t stream, cudaEvent_t tower_start = nullptr, cudaEvent_t tower_stop = nullptr) {
     const NetParams p = make_params(net);
+    if (tower_start) cudaEventRecord(tower_start, stream);
     const int s = net->channels == 64 ? launch_tower<64>(p, in, headfeat, status, stream)
                                       : launch_tower<128>(p, in, headfeat, status, stream);
+    if (tower_stop) cudaEventRecord(tower_stop, stream);
     if (s) return s;
     return launch_heads(p, headfeat, in, out, stream);
+}
+
+int net_evaluate(const gk_net_t* net, void* ws, int64_t batch, int capacity, float* headfeat, uint32_t* status,
+                 cudaStream_t stream, cudaEvent_t tower_start, cudaEvent_t tower_stop) {
+    if (!valid_net(net) || ws == nullptr || batch <= 0 || capacity < 1 || headfeat == nullptr || status == nullptr)
+        return GK_EINVAL;
+    int s = gk_puct_compact(ws, batch, capacity, stream);
+    if (s) return s;
+    PuctView v;
+    puct_layout(ws, batch, capacity, &v);
+    NetInput in{v.leaf_bits, nullptr, v.active, v.active_count, batch};
+    HeadOut out{nullptr, nullptr, v.policy, v.leaf_value, v.leaf_bits};
+    return run_forward(net, in, headfeat, out, status, stream, tower_start, tower_stop);
 }
 
 }  // namespace gk
@@ -607,15 +622,7 @@ int gk_net_forward(const gk_net_t* net, const uint32_t* states, const float* fea
 
 int gk_net_evaluate_puct(const gk_net_t* net, void* ws, int64_t batch, int capacity, float* headfeat,
                          uint32_t* status, void* stream) {
-    if (!valid_net(net) || ws == nullptr || batch <= 0 || capacity < 1 || headfeat == nullptr || status == nullptr)
-        return GK_EINVAL;
-    int s = gk_puct_compact(ws, batch, capacity, stream);
-    if (s) return s;
-    PuctView v;
-    puct_layout(ws, batch, capacity, &v);
-    NetInput in{v.leaf_bits, nullptr, v.active, v.active_count, batch};
-    HeadOut out{nullptr, nullptr, v.policy, v.leaf_value, v.leaf_bits};
-    return run_forward(net, in, headfeat, out, status, as_stream(stream));
+    return net_evaluate(net, ws, batch, capacity, headfeat, status, as_stream(stream), nullptr, nullptr);
 }
 
 }  // extern "C"

@@ -23,6 +23,7 @@
 #include "gk_device.cuh"
 #include "gk_launch.cuh"
 #include "gk_puct.cuh"
+#include "gk_random.cuh"
 
 namespace gk {
 
@@ -405,54 +406,11 @@ __global__ void puct_hash_eval_kernel(PuctView v, int64_t B) {
 }
 
 // ---- root Dirichlet noise ---------------------------------------------------
-// Gamma(alpha) by Marsaglia & Tsang (2000), "A simple method for generating
-// gamma variables", with the alpha < 1 boost Gamma(alpha+1) * U^(1/alpha);
-// normals by Box-Muller. Stream per tree: PCG32 (seed, stream_base + tree).
-__device__ __forceinline__ double uniform01(gk_pcg32& r) {
-    const uint64_t hi = gk_pcg32_next(&r) >> 5, lo = gk_pcg32_next(&r) >> 6;  // 27 + 26 bits
-    return ((double)(hi * 67108864ull + lo) + 0.5) * (1.0 / 9007199254740992.0);
-}
-__device__ __forceinline__ double normal01(gk_pcg32& r) {
-    const double u1 = uniform01(r), u2 = uniform01(r);
-    return sqrt(-2.0 * log(u1)) * cospi(2.0 * u2);
-}
-__device__ double gamma_draw(double alpha, gk_pcg32& r) {
-    double boost = 1.0;
-    if (alpha < 1.0) {
-        boost = pow(uniform01(r), 1.0 / alpha);
-        alpha += 1.0;
-    }
-    const double d = alpha - 1.0 / 3.0, c = 1.0 / sqrt(9.0 * d);
-    for (int it = 0; it < 64; ++it) {
-        const double x = normal01(r);
-        double y = 1.0 + c * x;
-        if (y <= 0.0) continue;
-        y = y * y * y;
-        const double u = uniform01(r);
-        if (u < 1.0 - 0.0331 * x * x * x * x || log(u) < 0.5 * x * x + d * (1.0 - y + log(y))) return d * y * boost;
-    }
-    return d * boost;
-}
-
+// Stream per tree: PCG32 (seed, stream_base + tree); draws in gk_random.cuh.
 __global__ void puct_noise_kernel(PuctView v, int64_t B, int C, uint64_t seed, uint64_t stream_base, double alpha) {
     for (int64_t t = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; t < B; t += (int64_t)gridDim.x * blockDim.x) {
-        const gk_bits root = v.node_state[t * C];
-        const gk_b96 placements = legal_placements(root);
-        const bool live = gk_reason(&root) == GK_NONE;
         gk_pcg32 r = gk_pcg32_seed(seed, stream_base + (uint64_t)t);
-        double g[GK_ACTIONS];
-        double largest = 0.0;
-        for (int a = 0; a < GK_ACTIONS; ++a) {
-            g[a] = 0.0;
-            if (live && action_legal(placements, true, a)) {
-                double x = gamma_draw(alpha, r);
-                if (!isfinite(x) || x < 0.0) x = 0.0;
-                g[a] = x;
-                largest = fmax(largest, x);
-            }
-        }
-        const double scale = largest > 2.2250738585072014e-308 ? largest : 2.2250738585072014e-308;
-        for (int a = 0; a < GK_ACTIONS; ++a) v.noise[t * GK_ACTIONS + a] = (float)(g[a] / scale);
+        root_noise(v.node_state[t * C], alpha, r, v.noise + t * GK_ACTIONS);
     }
 }
 

@@ -2,10 +2,12 @@
 // evaluator and self-play translation units.
 #pragma once
 
+#include <cuda_runtime.h>
+
 #include <cstddef>
 #include <cstdint>
 
-#include "../../include/gk_common.h"
+#include "../../include/gk.h"
 
 namespace gk {
 
@@ -86,6 +88,11 @@ inline size_t puct_layout(void* base, int64_t B, int C, PuctView* v) {
     if (v) *v = t;
     return off;
 }
+
+// Native-network leaf evaluation of a search workspace (gk_net.cu); events,
+// when given, are recorded around the tower kernel on `stream`.
+int net_evaluate(const gk_net_t* net, void* ws, int64_t batch, int capacity, float* headfeat, uint32_t* status,
+                 cudaStream_t stream, cudaEvent_t tower_start, cudaEvent_t tower_stop);
 
 struct PuctOptions {
     double c_puct;

@@ -1,0 +1,183 @@
+"""Continuous batched self-play on one GPU (native network, no host syncs per ply).
+
+``SelfPlayEngine`` keeps `lanes` games in flight; ``step()`` plays one ply in
+every lane through a single ``gk_selfplay_ply`` call: a full PUCT search per
+lane with the tcgen05 network as leaf evaluator, then one move per lane.
+Finished games write their samples to a device FIFO ``ReplayRing`` in the row
+schema of the reference ReplayBuffer (python/kingdom_ai/replay.py:106-125)
+and their lanes start the next game.
+
+Randomness is keyed by (seed, game id, ply), so the games played are the same
+however lanes are split across GPUs: rank r of W plays game ids
+r*lanes + i, then + W*lanes per finished game.
+"""
+
+from __future__ import annotations
+
+import ctypes
+
+import torch
+
+from . import _native as native
+from .gpu_puct import GpuPUCTOptions, SearchWorkspace
+from .gpu_rules import _launch_scope
+from .model import NativePolicyValueNet, PolicyValueNet
+
+COUNTER_NAMES = ("moves", "games", "rows", "errors", "black_wins", "white_wins", "capture_endings",
+                 "evaluations")
+
+
+class SelfPlayParams(ctypes.Structure):
+    _fields_ = [("simulations", ctypes.c_int), ("c_puct", ctypes.c_double), ("dirichlet_alpha", ctypes.c_double),
+                ("dirichlet_epsilon", ctypes.c_double), ("fpu_enabled", ctypes.c_int),
+                ("fpu_reduction", ctypes.c_double), ("temperature_moves", ctypes.c_int),
+                ("temperature", ctypes.c_double), ("final_temperature", ctypes.c_double),
+                ("seed", ctypes.c_uint64), ("game_stride", ctypes.c_uint64), ("neutral_cell", ctypes.c_int)]
+
+
+class ReplayStruct(ctypes.Structure):
+    _fields_ = [("features", ctypes.c_void_p), ("masks", ctypes.c_void_p), ("policy", ctypes.c_void_p),
+                ("value", ctypes.c_void_p), ("to_play", ctypes.c_void_p), ("capacity", ctypes.c_int64)]
+
+
+class SelfPlayBuffers(ctypes.Structure):
+    _fields_ = [("states", ctypes.c_void_p), ("lane_ply", ctypes.c_void_p), ("game_id", ctypes.c_void_p),
+                ("counters", ctypes.c_void_p)]
+
+
+def _bind():
+    lib = native.library()
+    if getattr(lib, "_selfplay_bound", False):
+        return lib
+    native.register("gk_selfplay_workspace_bytes", [ctypes.c_int64], ctypes.c_size_t)
+    native.register("gk_selfplay_reset", [ctypes.c_void_p, ctypes.c_int64, ctypes.c_int, ctypes.c_uint64,
+                                          ctypes.c_void_p])
+    native.register("gk_selfplay_buffers", [ctypes.c_void_p, ctypes.c_int64, ctypes.POINTER(SelfPlayBuffers)])
+    native.register("gk_selfplay_ply", [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int64,
+                                        ctypes.POINTER(native.NetStruct), ctypes.POINTER(SelfPlayParams),
+                                        ctypes.POINTER(ReplayStruct), ctypes.c_void_p, ctypes.c_void_p,
+                                        ctypes.c_void_p, ctypes.c_void_p])
+    native.register("gk_timer_create", [ctypes.c_int], ctypes.c_void_p)
+    native.register("gk_timer_destroy", [ctypes.c_void_p], None)
+    native.register("gk_timer_reset", [ctypes.c_void_p], None)
+    native.register("gk_timer_read", [ctypes.c_void_p, ctypes.POINTER(ctypes.c_double),
+                                      ctypes.POINTER(ctypes.c_int)])
+    lib._selfplay_bound = True
+    return lib
+
+
+class ReplayRing:
+    """Device FIFO of training rows (features, legal mask, policy, value, to_play)."""
+
+    ROW_BYTES = 810 * 4 + 82 + 82 * 4 + 4 + 1  # 3655, as replay.py:109
+
+    def __init__(self, capacity: int, device):
+        self.capacity = int(capacity)
+        self.device = torch.device(device)
+        c = max(self.capacity, 1)
+        self.features = torch.zeros((c, 10, 9, 9), dtype=torch.float32, device=self.device)
+        self.masks = torch.zeros((c, 82), dtype=torch.bool, device=self.device)
+        self.policy = torch.zeros((c, 82), dtype=torch.float32, device=self.device)
+        self.value = torch.zeros((c,), dtype=torch.float32, device=self.device)
+        self.to_play = torch.zeros((c,), dtype=torch.int8, device=self.device)
+        self.struct = ReplayStruct(self.features.data_ptr(), self.masks.data_ptr(), self.policy.data_ptr(),
+                                   self.value.data_ptr(), self.to_play.data_ptr(), self.capacity)
+
+    def rows(self, start: int, count: int):
+        """Row indices [start, start + count) of the ring (modulo capacity)."""
+        idx = (torch.arange(count, device=self.device, dtype=torch.int64) + start) % self.capacity
+        return (self.features[idx], self.masks[idx], self.policy[idx], self.value[idx], self.to_play[idx])
+
+
+class Timer:
+    """CUDA-event pairs recorded around the network tower inside a ply."""
+
+    def __init__(self, pairs: int):
+        lib = _bind()
+        self.handle = lib.gk_timer_create(pairs)
+        if not self.handle:
+            raise RuntimeError("could not create CUDA events")
+
+    def reset(self):
+        native.library().gk_timer_reset(self.handle)
+
+    def read(self):
+        total, pairs = ctypes.c_double(), ctypes.c_int()
+        native.call("gk_timer_read", self.handle, ctypes.byref(total), ctypes.byref(pairs))
+        return total.value, pairs.value
+
+    def __del__(self):
+        try:
+            native.library().gk_timer_destroy(self.handle)
+        except Exception:
+            pass
+
+
+class SelfPlayEngine:
+    """`lanes` concurrent games on one GPU, advanced one ply per ``step()``."""
+
+    def __init__(self, model: PolicyValueNet, lanes: int, options: GpuPUCTOptions | None = None, *,
+                 temperature: float = 1.0, temperature_moves: int | None = 10, final_temperature: float = 0.0,
+                 replay_capacity: int = 1 << 20, seed: int | None = None, rank: int = 0, world_size: int = 1,
+                 device="cuda", neutral=(4, 4)):
+        lib = _bind()
+        self.device = native.require_cuda(device)
+        self.options = options or GpuPUCTOptions()
+        if self.options.tactical_checks:
+            raise NotImplementedError("tactical_checks is not available in this engine yet")
+        self.lanes = int(lanes)
+        self.net = model if isinstance(model, NativePolicyValueNet) else NativePolicyValueNet(model, self.device)
+        seed = self.options.seed if seed is None else seed
+        neutral_cell = -1 if neutral is None else neutral[0] * 9 + neutral[1]
+        self.params = SelfPlayParams(
+            self.options.simulations, float(self.options.c_puct), float(self.options.dirichlet_alpha),
+            float(self.options.dirichlet_epsilon), 1 if self.options.fpu_reduction is not None else 0,
+            float(self.options.fpu_reduction or 0.0),
+            self.options.simulations + 10**9 if temperature_moves is None else int(temperature_moves),
+            float(temperature), float(final_temperature), seed & (2**64 - 1), world_size * self.lanes, neutral_cell)
+        self.first_game = rank * self.lanes
+        self.neutral_cell = neutral_cell
+        nbytes = lib.gk_selfplay_workspace_bytes(self.lanes)
+        self.storage = torch.empty(nbytes, dtype=torch.uint8, device=self.device)
+        self.search = SearchWorkspace(self.lanes, self.options.simulations + 1, self.device)
+        self.headfeat = torch.empty((self.lanes, 243), dtype=torch.float32, device=self.device)
+        self.status = torch.zeros(1, dtype=torch.int32, device=self.device)
+        self.replay = ReplayRing(replay_capacity, self.device) if replay_capacity > 0 else None
+        bufs = SelfPlayBuffers()
+        native.call("gk_selfplay_buffers", native.ptr(self.storage), self.lanes, bufs)
+        base = self.storage.data_ptr()
+        self.counters = self.storage[bufs.counters - base:bufs.counters - base + 64].view(torch.int64)
+        self.states = self.storage[bufs.states - base:bufs.states - base + self.lanes * 64].view(torch.int32).view(
+            self.lanes, 16)
+        self.timer = None
+        self.reset()
+
+    def reset(self):
+        with torch.cuda.device(self.device):
+            stream = _launch_scope(self.device, self.storage)
+            native.call("gk_selfplay_reset", native.ptr(self.storage), self.lanes, self.neutral_cell,
+                        self.first_game, stream)
+
+    def enable_timer(self, plies: int):
+        """Record the network tower of the next `plies` plies with CUDA events."""
+        self.timer = Timer(plies * (self.options.simulations + 1))
+        return self.timer
+
+    def step(self, plies: int = 1):
+        with torch.cuda.device(self.device):
+            stream = _launch_scope(self.device, self.storage, self.search.storage, self.headfeat)
+            replay = self.replay.struct if self.replay is not None else None
+            for _ in range(plies):
+                native.call("gk_selfplay_ply", native.ptr(self.storage), self.search.pointer, self.lanes,
+                            self.net.struct, self.params, replay, native.ptr(self.headfeat),
+                            native.ptr(self.status), self.timer.handle if self.timer else None, stream)
+
+    def stats(self) -> dict:
+        values = self.counters.cpu().tolist()
+        return dict(zip(COUNTER_NAMES, values))
+
+    def check(self):
+        code = int(self.status.item())
+        stats = self.stats()
+        if code or stats["errors"]:
+            raise RuntimeError(f"self-play reported status {code:#x}, {stats['errors']} rejected moves")

@@ -229,6 +229,88 @@ GK_API int gk_net_forward(const gk_net_t* net, const uint32_t* states, const flo
 GK_API int gk_net_evaluate_puct(const gk_net_t* net, void* ws, int64_t batch, int capacity, float* headfeat,
                                 uint32_t* status, void* stream);
 
+/* ------------------------------------------------------------ self-play */
+
+/* Per-ply self-play parameters (GpuPUCTOptions plus the temperature schedule
+ * of collect_gpu_puct_games, python/kingdom_ai/gpu_training.py:124-175). */
+typedef struct {
+    int simulations;
+    double c_puct;
+    double dirichlet_alpha;
+    double dirichlet_epsilon;
+    int fpu_enabled;
+    double fpu_reduction;
+    int temperature_moves;    /* plies per game that use `temperature` */
+    double temperature;       /* before temperature_moves (0 = best action) */
+    double final_temperature; /* afterwards */
+    uint64_t seed;            /* root noise and move sampling */
+    uint64_t game_stride;     /* game-id step when a lane starts its next game */
+    int neutral_cell;         /* start position's neutral stone, -1 for none */
+} gk_selfplay_params_t;
+
+/* FIFO replay ring in the CPU ReplayBuffer's row schema
+ * (python/kingdom_ai/replay.py:106-125): features f32[cap,10,9,9],
+ * masks bool[cap,82], policy f32[cap,82], value f32[cap], to_play i8[cap]. */
+typedef struct {
+    float* features;
+    uint8_t* masks;
+    float* policy;
+    float* value;
+    int8_t* to_play;
+    int64_t capacity;
+} gk_replay_t;
+
+/* Device pointers into a self-play workspace. counters (uint64[8]): moves,
+ * finished games, replay rows written (monotone; ring index = rows % cap),
+ * errors, black wins, white wins, capture endings, network evaluations. */
+typedef struct {
+    uint32_t* states;   /* [lanes,16] packed current positions */
+    int32_t* lane_ply;  /* [lanes] */
+    uint64_t* game_id;  /* [lanes] */
+    uint64_t* counters; /* [8] */
+} gk_selfplay_buffers_t;
+
+/* Bytes of self-play workspace for `lanes` concurrent games (positions,
+ * per-game history of states and visit policies, counters). The device-side
+ * equivalent of the history tensors of gpu_training.py:44-55. */
+GK_API size_t gk_selfplay_workspace_bytes(int64_t lanes);
+
+/* Start every lane at the initial position; lane i plays game first_game + i,
+ * then first_game + i + game_stride, ... Zeroes the counters. Replaces the
+ * GpuStateBatch.initial call of collect_gpu_puct_games (gpu_training.py:171). */
+GK_API int gk_selfplay_reset(void* ws, int64_t lanes, int neutral_cell, uint64_t first_game, void* stream);
+
+/* Fill `out` (host struct) with device pointers into the workspace. Same
+ * role as the reference's history tensors (gpu_training.py:44-55). */
+GK_API int gk_selfplay_buffers(void* ws, int64_t lanes, gk_selfplay_buffers_t* out);
+
+/* One ply of batched self-play: a full search per lane with the native
+ * network (no host synchronisation), then one move per lane; finished games
+ * are written to `replay` (may be NULL) and their lanes restart. `puct_ws`
+ * is a search workspace for (lanes, simulations + 1); `headfeat` holds
+ * gk_net_headfeat_bytes(lanes); `timer` (may be NULL, see gk_timer_create)
+ * records the network tower's launches. Replaces one iteration of the
+ * reference's per-ply loop (gpu_training.py:59-87). */
+GK_API int gk_selfplay_ply(void* sp_ws, void* puct_ws, int64_t lanes, const gk_net_t* net,
+                           const gk_selfplay_params_t* params, const gk_replay_t* replay, float* headfeat,
+                           uint32_t* status, void* timer, void* stream);
+
+/* CUDA-event timer for kernel launches inside gk_selfplay_ply: a host object
+ * holding `pairs` start/stop event pairs (NULL on failure). No reference
+ * counterpart: the reference times phases with perf_counter (loop.py:563-621). */
+GK_API void* gk_timer_create(int pairs);
+
+/* Destroy a timer and its events. No reference counterpart (see gk_timer_create). */
+GK_API void gk_timer_destroy(void* timer);
+
+/* Forget recorded pairs so the next plies start from the first pair. No
+ * reference counterpart (see gk_timer_create). */
+GK_API void gk_timer_reset(void* timer);
+
+/* Sum of the recorded pairs' elapsed times; the stream must be synchronised.
+ * No reference counterpart (see gk_timer_create). */
+GK_API int gk_timer_read(void* timer, double* total_ms, int* pairs);
+
 #ifdef __cplusplus
 }
 #endif

@@ -14,14 +14,24 @@ LIBRARY = ROOT / "alpha-yoo-for-great-kingdom_b200" / "kingdom_ai" / "libgk.so"
 def declared_symbols():
     names = []
     for header in HEADERS:
-        names += re.findall(r"^GK_API\s+\w+\s+(gk_\w+)\s*\(", header.read_text(), flags=re.M)
+        names += re.findall(r"^GK_API\s+[\w\s\*]*?\b(gk_\w+)\s*\(", header.read_text(), flags=re.M)
     return names
 
 
 def test_header_declares_entry_points():
     names = declared_symbols()
-    assert len(names) >= 20
+    assert len(names) >= 30
     assert len(names) == len(set(names))
+    assert "gk_timer_create" in names and "gk_selfplay_ply" in names
+
+
+def test_every_declaration_has_its_own_comment():
+    for header in HEADERS:
+        lines = header.read_text().splitlines()
+        for i, line in enumerate(lines):
+            if line.startswith("GK_API"):
+                above = lines[i - 1].strip()
+                assert above.endswith("*/"), f"{header.name}:{i + 1} {line}"
 
 
 def test_library_exports_every_declared_symbol():

@@ -1,0 +1,80 @@
+"""Device-resident self-play engine: legality, replay rows, determinism, shard invariance."""
+
+import numpy as np
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+
+def small_net(seed=3):
+    from kingdom_ai.model import random_network
+    return random_network(64, 2, seed)
+
+
+def run_engine(lanes, plies, rank=0, world=1, seed=11, sims=16, replay=4096, temperature_moves=4):
+    from kingdom_ai.gpu_puct import GpuPUCTOptions
+    from kingdom_ai.selfplay import SelfPlayEngine
+
+    opts = GpuPUCTOptions(simulations=sims, c_puct=1.5, dirichlet_alpha=0.3, dirichlet_epsilon=0.25, seed=seed)
+    engine = SelfPlayEngine(small_net(), lanes, opts, temperature_moves=temperature_moves, replay_capacity=replay,
+                            rank=rank, world_size=world)
+    engine.step(plies)
+    torch.cuda.synchronize()
+    engine.check()
+    return engine
+
+
+def rows_of(engine):
+    n = engine.stats()["rows"]
+    r = engine.replay
+    n = min(n, r.capacity)
+    return (r.features[:n].cpu().numpy(), r.masks[:n].cpu().numpy(), r.policy[:n].cpu().numpy(),
+            r.value[:n].cpu().numpy(), r.to_play[:n].cpu().numpy())
+
+
+def test_counters_and_replay_rows_are_consistent(oracle):
+    lanes, plies = 96, 70
+    engine = run_engine(lanes, plies)
+    s = engine.stats()
+    assert s["moves"] == lanes * plies and s["errors"] == 0
+    assert s["games"] > 0 and s["black_wins"] + s["white_wins"] == s["games"]
+    assert s["evaluations"] >= lanes * plies  # at least the root of every search
+    feats, masks, policy, value, to_play = rows_of(engine)
+    assert len(value) == s["rows"] > 0
+    assert set(np.unique(value).tolist()) <= {-1.0, 1.0}
+    assert set(np.unique(to_play).tolist()) <= {1, 2}
+    # Observation planes are one-hot where they must be and agree with the mask.
+    cells = feats[:, :3].reshape(len(feats), 3, 81)
+    assert (cells.sum(axis=1) <= 1).all()
+    assert np.array_equal(feats[:, 9].reshape(len(feats), 81) > 0, masks[:, :81])
+    assert np.array_equal(feats[:, 5, 0, 0] == 1.0, to_play == 1)
+    # Visit policies are distributions over legal actions only.
+    assert np.allclose(policy.sum(axis=1), 1.0, atol=1e-5)
+    assert (policy[~masks] == 0).all()
+
+
+def test_same_seed_same_games():
+    a = run_engine(48, 40, seed=5)
+    b = run_engine(48, 40, seed=5)
+    for x, y in zip(rows_of(a), rows_of(b)):
+        assert np.array_equal(x, y)
+    c = run_engine(48, 40, seed=6)
+    assert not np.array_equal(rows_of(a)[2], rows_of(c)[2])
+
+
+def test_games_do_not_depend_on_sharding():
+    """One engine with 64 lanes = two ranks of 32 lanes: the same games, the same rows."""
+    plies = 60
+    whole = run_engine(64, plies, seed=9, temperature_moves=8)
+    half0 = run_engine(32, plies, rank=0, world=2, seed=9, temperature_moves=8)
+    half1 = run_engine(32, plies, rank=1, world=2, seed=9, temperature_moves=8)
+    # Completed games are written in completion order, which differs between
+    # layouts; compare the multisets of rows.
+    def keyset(rows):
+        feats, masks, policy, value, to_play = rows
+        return sorted(hash((f.tobytes(), p.tobytes(), float(v))) for f, p, v in zip(feats, policy, value))
+    w = rows_of(whole)
+    h = [np.concatenate(parts) for parts in zip(rows_of(half0), rows_of(half1))]
+    assert whole.stats()["games"] == half0.stats()["games"] + half1.stats()["games"]
+    assert keyset(w) == keyset(h)
