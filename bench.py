@@ -255,9 +255,17 @@ def main():
     parser.add_argument("--impl", choices=["ours", "reference"], default="ours")
     parser.add_argument("--e2e-steps", type=int, default=3)
     parser.add_argument("--no-cpu-baseline", action="store_true")
+    parser.add_argument("--workload", choices=["selfplay", "network", "rules", "encode", "puct"], default="selfplay",
+                        help="selfplay is the headline; the others time one kernel family each")
+    parser.add_argument("--net", default="128x10", help="network workload: CHANNELSxBLOCKS")
+    parser.add_argument("--batch", type=int, default=8192, help="network workload batch")
     args = parser.parse_args()
     if args.impl == "reference":
         reference_arm(args)
+        return
+    if args.workload != "selfplay":
+        import bench_components
+        getattr(bench_components, f"bench_{args.workload}")(args, peaks())
         return
 
     import torch

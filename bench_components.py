@@ -1,0 +1,166 @@
+"""Per-kernel benchmarks behind `bench.py --workload ...` (one JSON line each).
+
+    network  leaf evaluation: `--net CxR --batch B` (default 10 x 128ch, 8192 positions)
+    rules    4096 uniform-random complete playouts, and one transition of 2^22 packed states
+    encode   observation planes + legal masks for 65,536 and 2^20 generated positions
+    puct     1024 trees x 800 simulations with the injected evaluator
+
+Every timed launch is bracketed by CUDA events on the launching stream; an L2
+flush (a 256 MB write) separates timed launches so each one reads its inputs
+from HBM.
+"""
+
+from __future__ import annotations
+
+import json
+
+import torch
+
+from kingdom_ai import _native as native
+
+L2_FLUSH_BYTES = 256 << 20
+
+
+class Flusher:
+    def __init__(self, device):
+        self.buf = torch.empty(L2_FLUSH_BYTES // 4, dtype=torch.int32, device=device)
+
+    def __call__(self):
+        self.buf.fill_(1)
+
+
+def timed(fn, steps, warmup, flush):
+    """Average milliseconds of `fn` over `steps` launches (events per launch)."""
+    for _ in range(warmup):
+        fn()
+    total = 0.0
+    for _ in range(steps):
+        flush()
+        start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        start.record()
+        fn()
+        stop.record()
+        stop.synchronize()
+        total += start.elapsed_time(stop)
+    return total / steps
+
+
+def positions(n, seed, device):
+    bits = torch.empty((n, 16), dtype=torch.int32, device=device)
+    native.call("gk_gen_positions", seed, 0, n, native.ptr(bits), native.stream_of(device))
+    return bits
+
+
+def emit(line):
+    print(json.dumps(line), flush=True)
+
+
+def bench_network(args, peaks):
+    from kingdom_ai.gpu_puct import encode_packed
+    from kingdom_ai.model import NativePolicyValueNet, calibrate_batchnorm, random_network
+
+    device = torch.device("cuda", 0)
+    channels, blocks = (int(x) for x in args.net.split("x"))
+    n = args.batch
+    model = random_network(channels, blocks, 1234).to(device)
+    bits = positions(n, 4321, device)
+    features, _ = encode_packed(bits)
+    calibrate_batchnorm(model, features)
+    net = NativePolicyValueNet(model.cpu(), device)
+    flush = Flusher(device)
+    ms = timed(lambda: net.forward_states(bits), args.steps, args.warmup, flush)
+    net.check()
+    flops = 2 * 81 * 9 * 10 * channels + 2 * blocks * 2 * 81 * 9 * channels * channels + 2 * 81 * (
+        channels * 3 + 162 * 82 + 81 * 64 + 64)
+    tflops = n * flops / (ms / 1e3) / 1e12
+    with torch.no_grad():
+        t_ref = timed(lambda: model.to(device)(features), max(1, args.steps // 2), 1, flush)
+        with torch.autocast("cuda", dtype=torch.bfloat16):
+            t_amp = timed(lambda: model(features), max(1, args.steps // 2), 1, flush)
+    emit({"workload": f"network forward {channels}ch x {blocks} blocks, batch {n}", "metric": "positions/s",
+          "value": n / (ms / 1e3), "unit": "positions/s", "ms_per_batch": ms, "dtype": "bf16",
+          "roofline": {"bound": "tensor", "achieved": tflops, "peak": peaks[0], "unit": "TFLOP/s",
+                       "frac": tflops / peaks[0], "flops_per_position": flops},
+          "pytorch_fp32_ms": t_ref, "pytorch_bf16_autocast_ms": t_amp})
+
+
+def bench_rules(args, peaks):
+    device = torch.device("cuda", 0)
+    flush = Flusher(device)
+    n = 4096
+    boards = torch.empty((n, 81), dtype=torch.int8, device=device)
+    infos = torch.empty((n, 5), dtype=torch.int32, device=device)
+    stream = native.stream_of(device)
+    ms = timed(lambda: native.call("gk_random_playouts", 2024, 0, n, 40, native.ptr(boards), native.ptr(infos),
+                                   stream), args.steps, args.warmup, flush)
+    plies = int(infos[:, 4].sum().item())
+    big = 1 << 22
+    bits = positions(big, 99, device)
+    work = bits.clone()
+    actions = torch.randint(0, 82, (big,), dtype=torch.int32, device=device)
+    accepted = torch.empty(big, dtype=torch.bool, device=device)
+    # A copy restores the inputs before each launch; the transition alone is timed.
+    total = 0.0
+    for i in range(args.warmup + args.steps):
+        work.copy_(bits)
+        flush()
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s.record()
+        native.call("gk_play_bits", native.ptr(work), native.ptr(actions), 4, native.ptr(accepted), big, stream)
+        e.record()
+        e.synchronize()
+        if i >= args.warmup:
+            total += s.elapsed_time(e)
+    play_ms = total / args.steps
+    bytes_per_state = 64 + 4 + 64 + 1
+    gbs = big * bytes_per_state / (play_ms / 1e3) / 1e9
+    emit({"workload": "rules: 4096 uniform-random complete playouts; one transition of 2^22 packed states",
+          "metric": "playout moves/s", "value": plies / (ms / 1e3), "unit": "moves/s",
+          "games_per_s": n / (ms / 1e3), "playout_ms": ms, "mean_plies": plies / n,
+          "play_kernel": {"states": big, "ms": play_ms, "states_per_s": big / (play_ms / 1e3)},
+          "roofline": {"bound": "hbm", "kernel": "play_bits_kernel", "achieved": gbs, "peak": peaks[1],
+                       "unit": "GB/s", "frac": gbs / peaks[1], "bytes_per_state": bytes_per_state}})
+
+
+def bench_encode(args, peaks):
+    device = torch.device("cuda", 0)
+    flush = Flusher(device)
+    stream = native.stream_of(device)
+    out = {}
+    for n in (65536, 1 << 20):
+        bits = positions(n, 11, device)
+        feats = torch.empty((n, 10, 9, 9), dtype=torch.float32, device=device)
+        masks = torch.empty((n, 82), dtype=torch.bool, device=device)
+        ms = timed(lambda: native.call("gk_encode_bits", native.ptr(bits), native.ptr(feats), native.ptr(masks), n,
+                                       stream), args.steps, args.warmup, flush)
+        out[n] = ms
+    bytes_per_pos = 64 + 3240 + 82
+    n = 65536
+    gbs = n * bytes_per_pos / (out[n] / 1e3) / 1e9
+    big = 1 << 20
+    gbs_big = big * bytes_per_pos / (out[big] / 1e3) / 1e9
+    emit({"workload": "encode 65,536 generated positions (and 2^20)", "metric": "positions/s",
+          "value": n / (out[n] / 1e3), "unit": "positions/s", "ms": out[n], "ms_2pow20": out[big],
+          "roofline": {"bound": "hbm", "kernel": "encode_bits_kernel", "achieved": gbs, "peak": peaks[1],
+                       "unit": "GB/s", "frac": gbs / peaks[1], "bytes_per_position": bytes_per_pos,
+                       "achieved_2pow20": gbs_big, "frac_2pow20": gbs_big / peaks[1]}})
+
+
+def bench_puct(args, peaks):
+    from kingdom_ai.gpu_puct import search_hash
+
+    device = torch.device("cuda", 0)
+    flush = Flusher(device)
+    n, sims = 1024, 800
+    bits = positions(n, 4242, device)
+    holder = {}
+
+    def run():
+        holder["r"] = search_hash(bits, sims)
+
+    ms = timed(run, max(1, args.steps // 3), 1, flush)
+    r = holder["r"]
+    assert int(r.simulations.sum().item()) == n * sims
+    emit({"workload": "PUCT 1024 trees x 800 simulations, injected evaluator, c_puct 1.5", "metric": "simulations/s",
+          "value": n * sims / (ms / 1e3), "unit": "simulations/s", "ms_per_search": ms,
+          "nodes_mean": float(r.nodes.float().mean().item())})
