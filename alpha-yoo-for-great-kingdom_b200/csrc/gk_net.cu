@@ -19,10 +19,12 @@
 //     128 x C x 16 per 128-row tile, issued by one thread.
 //   * Weights stream from L2 into a ring of tap slots with bulk (TMA) copies
 //     (no multicast) so the next layer's taps arrive while this one runs.
-//   * Four epilogue warps drain TMEM (tcgen05.ld), add the folded-BN bias
-//     and the residual, apply ReLU, zero the padding rows and write the next
-//     layer's bf16 rows back to shared memory. The last layer's epilogue
-//     also computes the two 1x1 head convolutions (3 channels) in fp32.
+//   * Eight epilogue warps (two per TMEM lane quadrant, each owning half of
+//     the channels, biases held in registers) drain TMEM (tcgen05.ld), add
+//     the folded-BN bias and the residual, apply ReLU, zero the padding rows
+//     and write the next layer's bf16 rows back to shared memory. After the
+//     last layer a head pass computes the two 1x1 head convolutions
+//     (3 channels, fp32 weights staged in shared memory).
 // Heads kernel: the fully connected heads and, in search mode, the masked
 // softmax, written straight into the PUCT workspace.
 #include <cuda_bf16.h>
@@ -50,8 +52,11 @@ struct NetCfg {
     static constexpr int SLOT = C * C * 2;       // one tap of weights (bf16)
     static constexpr int NSLOT = C == 64 ? 11 : 2;
     static constexpr bool TILE_OUTER = C == 64;  // all 9 taps resident: tile-major issue order
-    static constexpr int NBARS = 2 * NSLOT + 2 * T + 1;
-    static constexpr int SMEM = 2 * ACT + NSLOT * SLOT + NBARS * 8 + 16;
+    static constexpr int EPI_WARPS = 8;          // two per TMEM lane quadrant, each half the channels
+    static constexpr int THREADS = 64 + 32 * EPI_WARPS;
+    static constexpr int NBARS = 2 * NSLOT + 2 * T + 2;  // + mma_idle, heads_ready
+    static constexpr int HEADW = (3 * C + 3 + 3) / 4 * 4;  // head 1x1 weights + biases (floats)
+    static constexpr int SMEM = 2 * ACT + NSLOT * SLOT + NBARS * 8 + 16 + HEADW * 4;
     static constexpr uint32_t IDESC = tc::idesc_bf16(128, C);
     static_assert(2 * T * C <= 512, "two layers of accumulators must fit in TMEM");
 };
@@ -133,7 +138,7 @@ __device__ __forceinline__ void build_input_row(uint8_t* buf, int m, int base_im
 }
 
 template <int C>
-__global__ void __launch_bounds__(192, 1)
+__global__ void __launch_bounds__(NetCfg<C>::THREADS, 1)
     net_tower_kernel(NetParams p, NetInput in, float* headfeat, uint32_t* status) {
     using K = NetCfg<C>;
     extern __shared__ __align__(1024) uint8_t smem[];
@@ -142,11 +147,13 @@ __global__ void __launch_bounds__(192, 1)
     uint8_t* const slots = smem + 2 * K::ACT;
     uint64_t* const bars = reinterpret_cast<uint64_t*>(slots + K::NSLOT * K::SLOT);
     uint32_t* const tmem_holder = reinterpret_cast<uint32_t*>(bars + K::NBARS);
+    float* const headw = reinterpret_cast<float*>(tmem_holder + 4);  // [3][C] then [3] biases
     const uint32_t slot_full = tc::smem_u32(bars);
     const uint32_t slot_free = slot_full + 8 * K::NSLOT;
     const uint32_t acc_full = slot_free + 8 * K::NSLOT;
     const uint32_t epi_done = acc_full + 8 * K::T;
     const uint32_t mma_idle = epi_done + 8 * K::T;
+    const uint32_t heads_ready = mma_idle + 8;
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int NL = 1 + 2 * p.blocks;  // MMA layers per group
@@ -156,12 +163,15 @@ __global__ void __launch_bounds__(192, 1)
     // Zero both activation buffers (halo and padding rows stay zero forever).
     for (int i = threadIdx.x; i < 2 * K::ACT / 16; i += blockDim.x)
         reinterpret_cast<uint4*>(smem)[i] = make_uint4(0, 0, 0, 0);
+    for (int i = threadIdx.x; i < 3 * C; i += blockDim.x) headw[i] = p.head_w[i];
+    if (threadIdx.x < 3) headw[3 * C + threadIdx.x] = p.head_b[threadIdx.x];
     tc::fence_proxy_async_smem();
     if (threadIdx.x == 0) {
-        // epi_done completes when all four epilogue warps have arrived.
+        // epi_done and heads_ready complete when every epilogue warp has arrived.
         for (int b = 0; b < K::NBARS; ++b) {
             const uint32_t bar = slot_full + 8 * b;
-            tc::mbar_init(bar, bar >= epi_done && bar < mma_idle ? 4u : 1u);
+            const bool per_warp = (bar >= epi_done && bar < mma_idle) || bar == heads_ready;
+            tc::mbar_init(bar, per_warp ? (uint32_t)K::EPI_WARPS : 1u);
         }
         tc::fence_mbar_init();
     }
@@ -257,15 +267,18 @@ __global__ void __launch_bounds__(192, 1)
         tc::mma_commit(mma_idle);
         tc::mbar_wait(mma_idle, 0, status);
     } else if (warp >= 2) {
-        // ---------------- epilogue (4 warps, one TMEM lane quadrant each) ----------------
-        const int q = warp & 3;
+        // ------- epilogue: 8 warps; warp -> (TMEM lane quadrant, half of the channels) -------
+        constexpr int HALF = C / 2;
+        const int e = warp - 2;
+        const int q = warp & 3;          // TMEM lanes 32q..32q+31 = tile rows
+        const int col0 = (e >> 2) * HALF; // this warp's channels [col0, col0 + C/2)
         const int etid = threadIdx.x - 64;
         int i = 0;
         for (int g = blockIdx.x; g < groups; g += gridDim.x, ++i) {
             const int base_img = g * K::G;
             const int nimg = count - base_img < K::G ? count - base_img : K::G;
             // Epilogue layer 0: build the stem input (channels 0-15 of buffer Q).
-            for (int m = etid; m < K::T * 128; m += 128) build_input_row<C>(bufQ, m, base_img, nimg, in);
+            for (int m = etid; m < K::T * 128; m += 32 * K::EPI_WARPS) build_input_row<C>(bufQ, m, base_img, nimg, in);
             tc::fence_proxy_async_smem();
             __syncwarp();
             if (lane == 0)
@@ -276,7 +289,9 @@ __global__ void __launch_bounds__(192, 1)
                 uint8_t* const out = l % 2 == 0 ? bufP : bufQ;
                 const bool residual = l >= 2 && l % 2 == 0;
                 const bool last = l == NL - 1;
-                const float* bias = p.conv_b + l * C;
+                float bias[HALF];
+#pragma unroll
+                for (int j = 0; j < HALF; ++j) bias[j] = __ldg(p.conv_b + l * C + col0 + j);
                 for (int t = 0; t < K::T; ++t) {
                     if (!tc::mbar_wait(acc_full + 8 * t, (uint32_t)a & 1u, status)) goto epi_done_label;
                     tc::tc_fence_after();
@@ -284,62 +299,71 @@ __global__ void __launch_bounds__(192, 1)
                     const int img = m / 100, pos = m - img * 100, r = pos / 10, cc = pos - r * 10;
                     const bool valid = img < nimg && r < 9 && cc < 9;
                     uint8_t* const row = out + (K::HALO + m) * 16;
-                    float h0 = 0.f, h1 = 0.f, h2 = 0.f;
-#pragma unroll 1
-                    for (int cb = 0; cb < C / 32; ++cb) {
+#pragma unroll
+                    for (int cb = 0; cb < HALF / 32; ++cb) {
+                        const int ch0 = col0 + cb * 32;
                         float v[32];
-                        tc::tmem_ld32(tmem + ((uint32_t)(q * 32) << 16) + colbase + t * C + cb * 32, v);
+                        tc::tmem_ld32(tmem + ((uint32_t)(q * 32) << 16) + colbase + t * C + ch0, v);
                         uint4 res[4];
                         if (residual) {
 #pragma unroll
                             for (int k = 0; k < 4; ++k)
-                                res[k] = *reinterpret_cast<const uint4*>(row + (cb * 4 + k) * K::CHUNK);
+                                res[k] = *reinterpret_cast<const uint4*>(row + (ch0 / 8 + k) * K::CHUNK);
                         }
 #pragma unroll
                         for (int j = 0; j < 32; ++j) {
-                            float x = v[j] + __ldg(bias + cb * 32 + j);
+                            float x = v[j] + bias[cb * 32 + j];
                             if (residual) {
                                 const uint4 rv = res[j >> 3];
                                 const uint32_t w = (j & 7) < 2 ? rv.x : (j & 7) < 4 ? rv.y : (j & 7) < 6 ? rv.z : rv.w;
                                 x += (j & 1) ? bf16_hi(w) : bf16_lo(w);
                             }
-                            x = valid ? fmaxf(x, 0.0f) : 0.0f;
-                            v[j] = x;
+                            v[j] = valid ? fmaxf(x, 0.0f) : 0.0f;
                         }
-                        if (last) {
 #pragma unroll
-                            for (int j = 0; j < 32; ++j) {
-                                const int ch = cb * 32 + j;
-                                h0 = fmaf(v[j], __ldg(p.head_w + ch), h0);
-                                h1 = fmaf(v[j], __ldg(p.head_w + C + ch), h1);
-                                h2 = fmaf(v[j], __ldg(p.head_w + 2 * C + ch), h2);
-                            }
-                        } else {
-#pragma unroll
-                            for (int k = 0; k < 4; ++k) {
-                                const uint4 o = make_uint4(pack_bf16x2(v[8 * k], v[8 * k + 1]),
-                                                           pack_bf16x2(v[8 * k + 2], v[8 * k + 3]),
-                                                           pack_bf16x2(v[8 * k + 4], v[8 * k + 5]),
-                                                           pack_bf16x2(v[8 * k + 6], v[8 * k + 7]));
-                                *reinterpret_cast<uint4*>(row + (cb * 4 + k) * K::CHUNK) = o;
-                            }
+                        for (int k = 0; k < 4; ++k) {
+                            const uint4 o = make_uint4(pack_bf16x2(v[8 * k], v[8 * k + 1]),
+                                                       pack_bf16x2(v[8 * k + 2], v[8 * k + 3]),
+                                                       pack_bf16x2(v[8 * k + 4], v[8 * k + 5]),
+                                                       pack_bf16x2(v[8 * k + 6], v[8 * k + 7]));
+                            *reinterpret_cast<uint4*>(row + (ch0 / 8 + k) * K::CHUNK) = o;
                         }
                     }
-                    if (last) {
-                        if (valid) {
-                            float* hf = headfeat + (int64_t)(base_img + img) * 243 + r * 9 + cc;
-                            hf[0] = fmaxf(h0 + __ldg(p.head_b + 0), 0.0f);
-                            hf[81] = fmaxf(h1 + __ldg(p.head_b + 1), 0.0f);
-                            hf[162] = fmaxf(h2 + __ldg(p.head_b + 2), 0.0f);
-                        }
-                        tc::tc_fence_before();
-                    } else {
+                    tc::tc_fence_before();
+                    if (!last) {
                         tc::fence_proxy_async_smem();
-                        tc::tc_fence_before();
                         __syncwarp();
                         if (lane == 0) tc::mbar_arrive(epi_done + 8 * t);
                     }
                 }
+            }
+            // Head pass: the 1x1 policy (2) and value (1) convolutions over the
+            // final rows, once all eight warps have written them.
+            __syncwarp();
+            if (lane == 0) tc::mbar_arrive(heads_ready);
+            if (!tc::mbar_wait(heads_ready, (uint32_t)i & 1u, status)) goto epi_done_label;
+            for (int m = etid; m < K::T * 128; m += 32 * K::EPI_WARPS) {
+                const int img = m / 100, pos = m - img * 100, r = pos / 10, cc = pos - r * 10;
+                if (!(img < nimg && r < 9 && cc < 9)) continue;
+                const uint8_t* row = bufP + (K::HALO + m) * 16;
+                float h0 = headw[3 * C], h1 = headw[3 * C + 1], h2 = headw[3 * C + 2];
+#pragma unroll 4
+                for (int k = 0; k < C / 8; ++k) {
+                    const uint4 rv = *reinterpret_cast<const uint4*>(row + k * K::CHUNK);
+                    const uint32_t w[4] = {rv.x, rv.y, rv.z, rv.w};
+#pragma unroll
+                    for (int j = 0; j < 8; ++j) {
+                        const float x = (j & 1) ? bf16_hi(w[j >> 1]) : bf16_lo(w[j >> 1]);
+                        const int ch = k * 8 + j;
+                        h0 = fmaf(x, headw[ch], h0);
+                        h1 = fmaf(x, headw[C + ch], h1);
+                        h2 = fmaf(x, headw[2 * C + ch], h2);
+                    }
+                }
+                float* hf = headfeat + (int64_t)(base_img + img) * 243 + r * 9 + cc;
+                hf[0] = fmaxf(h0, 0.0f);
+                hf[81] = fmaxf(h1, 0.0f);
+                hf[162] = fmaxf(h2, 0.0f);
             }
         }
     epi_done_label:;
@@ -536,7 +560,7 @@ int launch_tower(const NetParams& p, const NetInput& in, float* headfeat, uint32
         return launch_status();
     const int64_t groups = (in.n + K::G - 1) / K::G;
     const int grid = (int)(groups < kSmCount ? groups : kSmCount);
-    net_tower_kernel<C><<<grid < 1 ? 1 : grid, 192, K::SMEM, stream>>>(p, in, headfeat, status);
+    net_tower_kernel<C><<<grid < 1 ? 1 : grid, K::THREADS, K::SMEM, stream>>>(p, in, headfeat, status);
     return launch_status();
 }
 
