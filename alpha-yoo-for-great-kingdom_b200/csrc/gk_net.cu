@@ -6,7 +6,8 @@
 //   policy 1x1 (C->2) + ReLU -> FC 162->82, value 1x1 (C->1) + ReLU ->
 //   FC 81->64 -> ReLU -> FC 64->1 -> tanh.
 //
-// Tower kernel (persistent, one CTA per SM, 192 threads):
+// Tower kernel (persistent, one CTA per SM, 320 threads: a weight producer,
+// an MMA warp and eight epilogue warps):
 //   * Images are processed in groups of G whole images, so a CTA never needs
 //     another CTA's halo. Each image is stored as 100 rows (a 10x10 grid,
 //     row r*10+c; column 9 and row 9 are zero padding shared by neighbours),
@@ -16,9 +17,12 @@
 //     no-swizzle layout ([C/8 chunks][rows][8 channels], 16-byte rows) a row
 //     shift is just a 16-byte move of the descriptor's start address.
 //   * D[128 x C] accumulates in TMEM (fp32), 9 taps x C/16 MMAs of
-//     128 x C x 16 per 128-row tile, issued by one thread.
+//     128 x C x 16 per 128-row tile. The MMA warp runs a fully unrolled
+//     issue loop on warp-uniform descriptors and one elected lane issues
+//     each instruction, so an MMA costs a couple of uniform adds.
 //   * Weights stream from L2 into a ring of tap slots with bulk (TMA) copies
-//     (no multicast) so the next layer's taps arrive while this one runs.
+//     (no multicast) so the next taps arrive while this one runs: 11 slots
+//     for C=64 (all 9 taps resident, tiles issued tile-major), 3 for C=128.
 //   * Eight epilogue warps (two per TMEM lane quadrant, each owning half of
 //     the channels, biases held in registers) drain TMEM (tcgen05.ld), add
 //     the folded-BN bias and the residual, apply ReLU, zero the padding rows
@@ -46,11 +50,16 @@ struct NetCfg {
     static constexpr int G = C == 64 ? 5 : 2;    // images per group
     static constexpr int T = C == 64 ? 4 : 2;    // 128-row tiles per group (>= 100*G rows)
     static constexpr int HALO = 11;              // max |tap row shift| = 10 + 1
-    static constexpr int ROWS = T * 128 + 2 * HALO;
+    // Rows a kept output reads: the group's G*100 rows and a zero halo either
+    // side. The tail of the last tile (rows G*100 .. T*128-1) is computed but
+    // never stored; its MMAs read up to TAIL rows past a chunk, i.e. into the
+    // next chunk or buffer, or into the weight slots after the last buffer.
+    static constexpr int ROWS = G * 100 + 2 * HALO;
+    static constexpr int TAIL = T * 128 - G * 100;
     static constexpr int CHUNK = ROWS * 16;      // bytes between 8-channel chunks
     static constexpr int ACT = (C / 8) * CHUNK;  // one activation buffer
     static constexpr int SLOT = C * C * 2;       // one tap of weights (bf16)
-    static constexpr int NSLOT = C == 64 ? 11 : 2;
+    static constexpr int NSLOT = C == 64 ? 11 : 3;
     static constexpr bool TILE_OUTER = C == 64;  // all 9 taps resident: tile-major issue order
     static constexpr int EPI_WARPS = 8;          // two per TMEM lane quadrant, each half the channels
     static constexpr int THREADS = 64 + 32 * EPI_WARPS;
@@ -59,6 +68,8 @@ struct NetCfg {
     static constexpr int SMEM = 2 * ACT + NSLOT * SLOT + NBARS * 8 + 16 + HEADW * 4;
     static constexpr uint32_t IDESC = tc::idesc_bf16(128, C);
     static_assert(2 * T * C <= 512, "two layers of accumulators must fit in TMEM");
+    static_assert(TAIL >= 0 && TAIL * 16 <= NSLOT * SLOT, "tail reads stay inside the shared-memory allocation");
+    static_assert(SMEM <= 232448, "shared memory per CTA");
 };
 
 struct NetParams {
@@ -137,6 +148,105 @@ __device__ __forceinline__ void build_input_row(uint8_t* buf, int m, int base_im
     *reinterpret_cast<uint4*>(buf + K::CHUNK + (K::HALO + m) * 16) = hi;
 }
 
+struct MmaBarriers {
+    uint32_t slot_full, slot_free, acc_full, epi_done;
+    uint32_t* status;
+};
+
+// Lane 0 waits; the outcome is broadcast so the warp's control flow stays uniform.
+__device__ __forceinline__ bool warp_wait(uint32_t bar, uint32_t parity, uint32_t* status, bool leader) {
+    int ok = 1;
+    if (leader) ok = tc::mbar_wait(bar, parity, status) ? 1 : 0;
+    ok = __shfl_sync(0xffffffffu, ok, 0);
+    tc::tc_fence_after();
+    return ok != 0;
+}
+
+// All MMAs of one 3x3 layer for the T tiles of a group, issued by the whole
+// (converged) MMA warp with one elected lane per instruction. KS = K steps of
+// 16 input channels per tap (1 for the stem). `a_lo`/`a_hi` are the halves of
+// the descriptor of row 0 of the input buffer, `b_lo`/`b_hi` of weight slot 0;
+// `c` is the running tap count that selects weight slots. A row shift or K
+// step is an add to a descriptor's low half (the 14-bit start-address field
+// holds addresses below 2^18 and never carries into the stride fields);
+// where the loops are unrolled the added offsets are compile-time constants.
+// Returns false if a bounded wait gave up.
+template <int C, int KS>
+__device__ __forceinline__ bool issue_layer(uint32_t tmem_d, uint32_t a_lo, uint32_t a_hi, uint32_t b_lo,
+                                            uint32_t b_hi, int c, uint32_t epi_parity, const MmaBarriers& mb,
+                                            bool leader) {
+    using K = NetCfg<C>;
+    constexpr uint32_t kChunk16 = K::CHUNK / 16;  // A K-chunk stride in 16-byte units
+    constexpr uint32_t kBChunk16 = C;             // B K-chunk stride (C rows x 16 B) in 16-byte units
+    constexpr uint32_t kSlot16 = K::SLOT / 16;
+    int sl = c % K::NSLOT;                         // weight slot of the layer's first tap
+    uint32_t par = (uint32_t)(c / K::NSLOT) & 1u;  // and the parity of its fill
+    if (K::TILE_OUTER) {
+        // Weight slot and fill parity of each tap of this layer.
+        int slot[9];
+        uint32_t parity[9];
+#pragma unroll
+        for (int tap = 0; tap < 9; ++tap) {
+            slot[tap] = sl;
+            parity[tap] = par;
+            if (++sl == K::NSLOT) {
+                sl = 0;
+                par ^= 1u;
+            }
+        }
+#pragma unroll
+        for (int t = 0; t < K::T; ++t) {
+            // Input rows of tile t come from tiles t-1..t+1 of the previous epilogue.
+#pragma unroll
+            for (int nb = (t == 0 ? 0 : t + 1); nb <= t + 1 && nb < K::T; ++nb)
+                if (!warp_wait(mb.epi_done + 8 * nb, epi_parity, mb.status, leader)) return false;
+#pragma unroll
+            for (int tap = 0; tap < 9; ++tap) {
+                if (t == 0 && !warp_wait(mb.slot_full + 8 * slot[tap], parity[tap], mb.status, leader)) return false;
+                const int off = (tap / 3 - 1) * 10 + (tap % 3 - 1);
+                const uint32_t a = a_lo + (uint32_t)(t * 128 + off);
+                const uint32_t b = b_lo + (uint32_t)slot[tap] * kSlot16;
+#pragma unroll
+                for (int s = 0; s < KS; ++s)
+                    tc::mma_bf16_warp(tmem_d + t * C, a + 2 * s * kChunk16, a_hi, b + 2 * s * kBChunk16, b_hi,
+                                      K::IDESC, (tap | s) != 0);
+                if (t == K::T - 1) tc::mma_commit_warp(mb.slot_free + 8 * slot[tap]);
+            }
+            tc::mma_commit_warp(mb.acc_full + 8 * t);
+        }
+    } else {
+        // The tap loop stays rolled here: unrolled over 9 taps x T tiles x KS
+        // steps the issue code no longer stays in the instruction cache next
+        // to the epilogue's, and the tower ran twice as long.
+#pragma unroll 1
+        for (int tap = 0; tap < 9; ++tap) {
+            if (!warp_wait(mb.slot_full + 8 * sl, par, mb.status, leader)) return false;
+            const int off = (tap / 3 - 1) * 10 + (tap % 3 - 1);
+            const uint32_t b = b_lo + (uint32_t)sl * kSlot16;
+#pragma unroll
+            for (int t = 0; t < K::T; ++t) {
+                if (tap == 0) {
+#pragma unroll
+                    for (int nb = (t == 0 ? 0 : t + 1); nb <= t + 1 && nb < K::T; ++nb)
+                        if (!warp_wait(mb.epi_done + 8 * nb, epi_parity, mb.status, leader)) return false;
+                }
+                const uint32_t a = a_lo + (uint32_t)(t * 128 + off);
+#pragma unroll
+                for (int s = 0; s < KS; ++s)
+                    tc::mma_bf16_warp(tmem_d + t * C, a + 2 * s * kChunk16, a_hi, b + 2 * s * kBChunk16, b_hi,
+                                      K::IDESC, (tap | s) != 0);
+                if (tap == 8) tc::mma_commit_warp(mb.acc_full + 8 * t);
+            }
+            tc::mma_commit_warp(mb.slot_free + 8 * sl);
+            if (++sl == K::NSLOT) {
+                sl = 0;
+                par ^= 1u;
+            }
+        }
+    }
+    return true;
+}
+
 template <int C>
 __global__ void __launch_bounds__(NetCfg<C>::THREADS, 1)
     net_tower_kernel(NetParams p, NetInput in, float* headfeat, uint32_t* status) {
@@ -200,72 +310,31 @@ __global__ void __launch_bounds__(NetCfg<C>::THREADS, 1)
                 }
             }
         }
-    } else if (warp == 1 && lane == 0) {
-        // ---------------- MMA issuer ----------------
+    } else if (warp == 1) {
+        // ---------------- MMA issuer: the whole warp runs the loop, one lane issues ----------------
+        const MmaBarriers mb{slot_full, slot_free, acc_full, epi_done, status};
+        const uint64_t bdesc = tc::smem_desc(tc::smem_u32(slots), C * 16, 128);
+        const uint64_t adescP = tc::smem_desc(tc::smem_u32(bufP) + K::HALO * 16, K::CHUNK, 128);
+        const uint64_t adescQ = tc::smem_desc(tc::smem_u32(bufQ) + K::HALO * 16, K::CHUNK, 128);
+        const uint32_t a_hi = (uint32_t)(adescP >> 32), b_lo = (uint32_t)bdesc, b_hi = (uint32_t)(bdesc >> 32);
+        const bool leader = lane == 0;
+        bool ok = true;
         int c = 0, i = 0;
-        for (int g = blockIdx.x; g < groups; g += gridDim.x, ++i) {
-            for (int l = 0; l < NL; ++l) {
-                const int a = i * NL + l;                  // accumulator phase index
+        for (int g = blockIdx.x; ok && g < groups; g += gridDim.x, ++i) {
+            for (int l = 0; ok && l < NL; ++l, c += 9) {
+                const int a = i * NL + l;  // accumulator phase index
                 const uint32_t epi_parity = (uint32_t)(i * NL + l) & 1u;  // epilogue layer l of group i
-                const uint32_t colbase = (uint32_t)((a & 1) * K::T * C);
-                const uint32_t in_buf = tc::smem_u32(l % 2 == 0 ? bufQ : bufP);
-                const int ksteps = l == 0 ? 1 : C / 16;
-                if (K::TILE_OUTER) {
-                    for (int t = 0; t < K::T; ++t) {
-                        // Input rows of tile t come from tiles t-1..t+1 of the previous epilogue.
-                        for (int nb = (t == 0 ? 0 : t + 1); nb <= t + 1 && nb < K::T; ++nb)
-                            if (!tc::mbar_wait(epi_done + 8 * nb, epi_parity, status)) goto mma_done;
-                        tc::tc_fence_after();
-                        for (int tap = 0; tap < 9; ++tap) {
-                            const int cc = c + tap, slot = cc % K::NSLOT;
-                            if (t == 0) {
-                                if (!tc::mbar_wait(slot_full + 8 * slot, (uint32_t)(cc / K::NSLOT) & 1u, status))
-                                    goto mma_done;
-                                tc::tc_fence_after();
-                            }
-                            const int off = (tap / 3 - 1) * 10 + (tap % 3 - 1);
-                            const uint32_t a_addr = in_buf + (uint32_t)((K::HALO + t * 128 + off) * 16);
-                            const uint32_t b_addr = tc::smem_u32(slots + slot * K::SLOT);
-                            for (int s = 0; s < ksteps; ++s)
-                                tc::mma_bf16(tmem + colbase + t * C,
-                                             tc::smem_desc(a_addr + 2 * s * K::CHUNK, K::CHUNK, 128),
-                                             tc::smem_desc(b_addr + 2 * s * C * 16, C * 16, 128), K::IDESC,
-                                             (tap | s) != 0);
-                            if (t == K::T - 1) tc::mma_commit(slot_free + 8 * slot);
-                        }
-                        tc::mma_commit(acc_full + 8 * t);
-                    }
-                } else {
-                    for (int tap = 0; tap < 9; ++tap) {
-                        const int cc = c + tap, slot = cc % K::NSLOT;
-                        if (!tc::mbar_wait(slot_full + 8 * slot, (uint32_t)(cc / K::NSLOT) & 1u, status)) goto mma_done;
-                        tc::tc_fence_after();
-                        const int off = (tap / 3 - 1) * 10 + (tap % 3 - 1);
-                        const uint32_t b_addr = tc::smem_u32(slots + slot * K::SLOT);
-                        for (int t = 0; t < K::T; ++t) {
-                            if (tap == 0) {
-                                for (int nb = (t == 0 ? 0 : t + 1); nb <= t + 1 && nb < K::T; ++nb)
-                                    if (!tc::mbar_wait(epi_done + 8 * nb, epi_parity, status)) goto mma_done;
-                                tc::tc_fence_after();
-                            }
-                            const uint32_t a_addr = in_buf + (uint32_t)((K::HALO + t * 128 + off) * 16);
-                            for (int s = 0; s < ksteps; ++s)
-                                tc::mma_bf16(tmem + colbase + t * C,
-                                             tc::smem_desc(a_addr + 2 * s * K::CHUNK, K::CHUNK, 128),
-                                             tc::smem_desc(b_addr + 2 * s * C * 16, C * 16, 128), K::IDESC,
-                                             (tap | s) != 0);
-                            if (tap == 8) tc::mma_commit(acc_full + 8 * t);
-                        }
-                        tc::mma_commit(slot_free + 8 * slot);
-                    }
-                }
-                c += 9;
+                const uint32_t tmem_d = tmem + (uint32_t)((a & 1) * K::T * C);
+                const uint32_t a_lo = (uint32_t)(l % 2 == 0 ? adescQ : adescP);
+                ok = l == 0 ? issue_layer<C, 1>(tmem_d, a_lo, a_hi, b_lo, b_hi, c, epi_parity, mb, leader)
+                            : issue_layer<C, C / 16>(tmem_d, a_lo, a_hi, b_lo, b_hi, c, epi_parity, mb, leader);
             }
         }
-    mma_done:
         // Drain: every MMA issued above completes before TMEM is released.
-        tc::mma_commit(mma_idle);
-        tc::mbar_wait(mma_idle, 0, status);
+        __syncwarp();
+        tc::mma_commit_warp(mma_idle);
+        if (leader) tc::mbar_wait(mma_idle, 0, status);
+        __syncwarp();
     } else if (warp >= 2) {
         // ------- epilogue: 8 warps; warp -> (TMEM lane quadrant, half of the channels) -------
         constexpr int HALF = C / 2;
@@ -278,7 +347,7 @@ __global__ void __launch_bounds__(NetCfg<C>::THREADS, 1)
             const int base_img = g * K::G;
             const int nimg = count - base_img < K::G ? count - base_img : K::G;
             // Epilogue layer 0: build the stem input (channels 0-15 of buffer Q).
-            for (int m = etid; m < K::T * 128; m += 32 * K::EPI_WARPS) build_input_row<C>(bufQ, m, base_img, nimg, in);
+            for (int m = etid; m < K::G * 100; m += 32 * K::EPI_WARPS) build_input_row<C>(bufQ, m, base_img, nimg, in);
             tc::fence_proxy_async_smem();
             __syncwarp();
             if (lane == 0)
@@ -298,6 +367,7 @@ __global__ void __launch_bounds__(NetCfg<C>::THREADS, 1)
                     const int m = t * 128 + q * 32 + lane;
                     const int img = m / 100, pos = m - img * 100, r = pos / 10, cc = pos - r * 10;
                     const bool valid = img < nimg && r < 9 && cc < 9;
+                    const bool stored = m < K::G * 100;  // tail rows of the last tile are dropped
                     uint8_t* const row = out + (K::HALO + m) * 16;
 #pragma unroll
                     for (int cb = 0; cb < HALF / 32; ++cb) {
@@ -305,7 +375,7 @@ __global__ void __launch_bounds__(NetCfg<C>::THREADS, 1)
                         float v[32];
                         tc::tmem_ld32(tmem + ((uint32_t)(q * 32) << 16) + colbase + t * C + ch0, v);
                         uint4 res[4];
-                        if (residual) {
+                        if (residual && stored) {
 #pragma unroll
                             for (int k = 0; k < 4; ++k)
                                 res[k] = *reinterpret_cast<const uint4*>(row + (ch0 / 8 + k) * K::CHUNK);
@@ -321,7 +391,7 @@ __global__ void __launch_bounds__(NetCfg<C>::THREADS, 1)
                             v[j] = valid ? fmaxf(x, 0.0f) : 0.0f;
                         }
 #pragma unroll
-                        for (int k = 0; k < 4; ++k) {
+                        for (int k = 0; k < 4 && stored; ++k) {
                             const uint4 o = make_uint4(pack_bf16x2(v[8 * k], v[8 * k + 1]),
                                                        pack_bf16x2(v[8 * k + 2], v[8 * k + 3]),
                                                        pack_bf16x2(v[8 * k + 4], v[8 * k + 5]),

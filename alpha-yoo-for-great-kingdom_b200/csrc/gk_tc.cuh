@@ -52,13 +52,15 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
     return done != 0;
 }
 
-// Bounded wait for the phase with the given parity; false on timeout.
+// Bounded wait for the phase with the given parity; false on timeout. The
+// first timeout also records (barrier shared address | parity << 31) in
+// status[1], so a stalled pipeline can be located from the host.
 __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, uint32_t* status) {
     if (mbar_try_wait(bar, parity)) return true;
     const long long start = clock64();
     while (!mbar_try_wait(bar, parity)) {
         if (clock64() - start > kSpinCycles) {
-            atomicOr(status, 4u);  // GK_ERR_TIMEOUT
+            if ((atomicOr(status, 4u) & 4u) == 0u) status[1] = bar | (parity << 31);  // GK_ERR_TIMEOUT
             return false;
         }
     }
@@ -130,6 +132,32 @@ __device__ __forceinline__ void mma_bf16(uint32_t tmem_d, uint64_t adesc, uint64
 __device__ __forceinline__ void mma_commit(uint32_t bar) {
     asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar)
                  : "memory");
+}
+
+// Warp-collective forms: every lane of a converged warp executes them and
+// elect.sync lets exactly one lane (the lowest, the same one every time, so
+// commits track that lane's MMAs) issue. Descriptors come as 32-bit halves so
+// that warp-uniform address arithmetic stays on the uniform datapath and a
+// row shift or K step costs one 32-bit add of the low half.
+__device__ __forceinline__ void mma_bf16_warp(uint32_t tmem_d, uint32_t a_lo, uint32_t a_hi, uint32_t b_lo,
+                                              uint32_t b_hi, uint32_t idesc, uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p, e;\n\t.reg .b64 ad, bd;\n\t"
+        "mov.b64 ad, {%1, %2};\n\t"
+        "mov.b64 bd, {%3, %4};\n\t"
+        "setp.ne.b32 p, %6, 0;\n\t"
+        "elect.sync _|e, 0xffffffff;\n\t"
+        "@e tcgen05.mma.cta_group::1.kind::f16 [%0], ad, bd, %5, p;\n\t}" ::"r"(tmem_d),
+        "r"(a_lo), "r"(a_hi), "r"(b_lo), "r"(b_hi), "r"(idesc), "r"(accumulate)
+        : "memory");
+}
+
+__device__ __forceinline__ void mma_commit_warp(uint32_t bar) {
+    asm volatile(
+        "{\n\t.reg .pred e;\n\t"
+        "elect.sync _|e, 0xffffffff;\n\t"
+        "@e tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];\n\t}" ::"r"(bar)
+        : "memory");
 }
 
 // 32 lanes x 32 consecutive fp32 columns -> 32 registers per thread.

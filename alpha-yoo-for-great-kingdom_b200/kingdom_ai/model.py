@@ -184,7 +184,7 @@ class NativePolicyValueNet:
             t["head_b"].data_ptr(), t["pol_w"].data_ptr(), t["pol_b"].data_ptr(), t["val_w1"].data_ptr(),
             t["val_b1"].data_ptr(), t["val_w2"].data_ptr(), t["val_b2"].data_ptr())
         self._headfeat = None
-        self.status = torch.zeros(1, dtype=torch.int32, device=self.device)
+        self.status = torch.zeros(2, dtype=torch.int32, device=self.device)
 
     def _workspace(self, n):
         if self._headfeat is None or self._headfeat.shape[0] < n:
@@ -221,6 +221,7 @@ class NativePolicyValueNet:
 
     def check(self):
         """Raise if any kernel reported a bounded wait that gave up."""
-        code = int(self.status.item())
+        code, where = (int(v) for v in self.status.tolist())
         if code:
-            raise RuntimeError(f"native network reported error bits {code:#x}")
+            raise RuntimeError(f"native network reported error bits {code:#x} (wait at {where & 0x7fffffff:#x}, "
+                               f"parity {(where >> 31) & 1})")

@@ -141,7 +141,7 @@ class SelfPlayEngine:
         self.storage = torch.empty(nbytes, dtype=torch.uint8, device=self.device)
         self.search = SearchWorkspace(self.lanes, self.options.simulations + 1, self.device)
         self.headfeat = torch.empty((self.lanes, 243), dtype=torch.float32, device=self.device)
-        self.status = torch.zeros(1, dtype=torch.int32, device=self.device)
+        self.status = torch.zeros(2, dtype=torch.int32, device=self.device)
         self.replay = ReplayRing(replay_capacity, self.device) if replay_capacity > 0 else None
         bufs = SelfPlayBuffers()
         native.call("gk_selfplay_buffers", native.ptr(self.storage), self.lanes, bufs)
@@ -177,7 +177,7 @@ class SelfPlayEngine:
         return dict(zip(COUNTER_NAMES, values))
 
     def check(self):
-        code = int(self.status.item())
+        code = int(self.status[0].item())
         stats = self.stats()
         if code or stats["errors"]:
             raise RuntimeError(f"self-play reported status {code:#x}, {stats['errors']} rejected moves")

@@ -11,6 +11,10 @@
  *     by the matching *_workspace_bytes function.
  *   - Device-side failures never trap: they set bits (GK_ERR_* in
  *     gk_common.h) in a caller-supplied uint32 status word or per-lane word.
+ *     Entry points whose kernels wait on barriers (gk_net_*, gk_mma_selftest,
+ *     gk_selfplay_ply) take uint32 status[2]: every wait is bounded, and the
+ *     first wait that gives up sets GK_ERR_TIMEOUT in status[0] and records
+ *     its barrier's shared address | parity << 31 in status[1].
  *
  * Each declaration names the reference interface it replaces. The reference
  * launches NVRTC kernels through ctypes (python/kingdom_ai/gpu_runtime.py:179-221,

@@ -2,7 +2,7 @@
 
 Two references:
   * the fp32 PyTorch model - the accuracy statement for bf16 arithmetic:
-    max |logit - logit_fp32| <= rtol * max |logit_fp32| and
+    max |logit - logit_fp32| <= rtol * max |logit_fp32| + 5e-3 and
     max |value - value_fp32| <= vtol, with (rtol, vtol) = (1e-2, 5e-2) for one
     block, (2e-2, 0.1) for 6 x 64 and (4e-2, 0.15) for 10 x 128 (Kaiming
     initialisation, batch norms calibrated on generated positions; rounding
@@ -23,6 +23,7 @@ import torch.nn.functional as F
 pytestmark = pytest.mark.gpu
 
 LOGIT_RTOL = 1e-2   # vs fp32, relative to the largest |logit|
+LOGIT_ATOL = 5e-3   # vs fp32, absolute floor for networks with tiny logits
 VALUE_ATOL = 5e-2   # vs fp32
 EMU_RTOL = 2e-3     # vs the bf16-rounding emulation, relative to the largest |logit|
 EMU_VALUE_ATOL = 5e-3
@@ -42,13 +43,11 @@ def bf16_emulation(model, features):
         y = F.conv2d(x, r(w.to(features.device)), b.to(features.device), padding=1)
         if i >= 2 and i % 2 == 0:
             y = y + skip
-        y = torch.relu(y)
-        if i == len(layers) - 1:
-            x = y
-        else:
-            x = r(y)
-            if i % 2 == 0:
-                skip = x
+        # Every layer's output is stored in bf16, including the last, which
+        # the head pass reads back.
+        x = r(torch.relu(y))
+        if i % 2 == 0:
+            skip = x
     pw, pb = fold(model.policy_conv, model.policy_bn)
     vw, vb = fold(model.value_conv, model.value_bn)
     p = torch.relu(F.conv2d(x, pw.to(x.device), pb.to(x.device))).flatten(1)
@@ -67,13 +66,13 @@ def selftest():
     a = torch.randn(128, 16, generator=g).bfloat16()
     b = torch.randn(64, 16, generator=g).bfloat16()
     d = torch.zeros(128, 64, device="cuda")
-    status = torch.zeros(1, dtype=torch.int32, device="cuda")
+    status = torch.zeros(2, dtype=torch.int32, device="cuda")
     ac, bc = a.view(torch.int16).cuda(), b.view(torch.int16).cuda()
     native.call("gk_mma_selftest", native.ptr(ac), native.ptr(bc), native.ptr(d), native.ptr(status),
                 native.stream_of(d.device))
     torch.cuda.synchronize()
     expected = a.float() @ b.float().T
-    return d.cpu(), expected, int(status.item())
+    return d.cpu(), expected, int(status[0].item())
 
 
 def test_tensor_core_selftest(selftest):
@@ -127,7 +126,7 @@ def compare(channels, blocks, n, seed, selftest, calibrate=False, emu_rtol=EMU_R
         with open(out, "a") as f:
             f.write(json.dumps(stats) + "\n")
     assert stats["emu_max_abs_logit"] <= emu_rtol * scale and stats["emu_max_abs_value"] <= emu_vtol
-    assert stats["fp32_max_abs_logit"] <= rtol * scale and stats["fp32_max_abs_value"] <= vtol
+    assert stats["fp32_max_abs_logit"] <= rtol * scale + LOGIT_ATOL and stats["fp32_max_abs_value"] <= vtol
     # The state-fed and feature-fed stems see identical bf16 inputs.
     assert torch.equal(logits, logits2) and torch.equal(values, values2)
     return stats
