@@ -39,6 +39,11 @@ CHANNELS, BLOCKS = 64, 6
 # padding): stem 3x3 10->C, 2R convs 3x3 C->C, the 1x1 head convs C->3.
 TOWER_FLOPS_PER_EVAL = (2 * 81 * 9 * 10 * CHANNELS + 2 * BLOCKS * 2 * 81 * 9 * CHANNELS * CHANNELS
                         + 2 * 81 * CHANNELS * 3)  # 72.63 MFLOP
+# DRAM bytes of one tower launch (dram__bytes_read.sum + dram__bytes_write.sum)
+# from an ncu capture of net_tower_kernel<64> on 4096 positions: the bf16
+# weights streamed once per image group plus the packed input states;
+# activations never leave shared memory and the head features stay in L2.
+TOWER_DRAM_BYTES_PER_LAUNCH = 1_286_912
 # Kernel launches per ply: begin, noise, finish, advance; (compact, tower,
 # heads, expand/backup) per evaluation; select per simulation.
 LAUNCHES_PER_PLY = 4 + 4 * (SIMULATIONS + 1) + SIMULATIONS
@@ -104,11 +109,17 @@ class ClockSampler:
 
 
 def peaks():
+    """(bf16 sustained TFLOP/s, HBM GB/s, source, bf16 burst TFLOP/s).
+
+    The sustained GEMM figure is the denominator for the tower timed inside a
+    seconds-long self-play step; the burst figure is for a kernel timed alone.
+    """
     path = ROOT / "MEASURED_PEAKS.json"
     if path.exists():
         data = json.loads(path.read_text())
-        return data.get("bf16_tflops_sustained", 1378.6), data.get("hbm_gbs", 6543.4), "measured"
-    return 1400.0, 6650.0, "fallback"
+        return (data.get("bf16_tflops_sustained", 1378.6), data.get("hbm_gbs", 6543.4), "measured",
+                data.get("bf16_tflops", 1619.6))
+    return 1400.0, 6650.0, "fallback", 1590.0
 
 
 def cpu_baseline_sample(seconds: float = 15.0):
@@ -272,6 +283,7 @@ def main():
     import torch.distributed as dist
 
     from kingdom_ai.gpu_puct import GpuPUCTOptions
+    from kingdom_ai.distributed import ReplayGather
     from kingdom_ai.selfplay import ReplayRing, SelfPlayEngine
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -290,12 +302,12 @@ def main():
                             replay_capacity=fifo_capacity if world == 1 else 1 << 18, rank=rank, world_size=world,
                             device=device)
     fifo = engine.replay if world == 1 else (ReplayRing(fifo_capacity, device) if rank == 0 else None)
-    gather = RowGather(engine, fifo, world, rank, device) if world > 1 else None
+    gather = ReplayGather(engine.replay, fifo) if world > 1 else None
 
     def step():
         engine.step(1)
         if gather is not None:
-            gather.run()
+            gather.run(int(engine.counters[2].item()))
 
     for _ in range(args.warmup):
         step()
@@ -332,7 +344,7 @@ def main():
     my_evals = after["evaluations"] - before["evaluations"]
     tower_s = tower_ms / 1000.0
     tflops = my_evals * TOWER_FLOPS_PER_EVAL / tower_s / 1e12 if tower_s > 0 else None
-    peak_tf, hbm, peak_kind = peaks()
+    peak_tf, hbm, peak_kind, _ = peaks()
 
     e2e = None
     if args.e2e_steps > 0:
@@ -363,7 +375,7 @@ def main():
                        "l2": "working set (search trees 3.2 GB/GPU) far larger than L2"},
             "roofline": {"bound": "tensor", "kernel": "net_tower_kernel<64>",
                          "achieved": tflops, "peak": peak_tf, "unit": "TFLOP/s",
-                         "frac": (tflops / peak_tf) if tflops else None, "traffic": None,
+                         "frac": (tflops / peak_tf) if tflops else None, "traffic": TOWER_DRAM_BYTES_PER_LAUNCH,
                          "peak_kind": f"{peak_kind} bf16 sustained",
                          "flops_per_eval": TOWER_FLOPS_PER_EVAL, "launches": tower_launches,
                          "avg_launch_ms": tower_ms / max(tower_launches, 1)},
@@ -375,52 +387,6 @@ def main():
         print(json.dumps(line), flush=True)
     if world > 1:
         dist.destroy_process_group()
-
-
-class RowGather:
-    """Gather each rank's new replay rows into rank 0's FIFO over NCCL."""
-
-    def __init__(self, engine, fifo, world, rank, device):
-        self.engine, self.fifo, self.world, self.rank, self.device = engine, fifo, world, rank, device
-        self.sent = 0
-        self.fifo_head = 0
-
-    def run(self):
-        import torch
-        import torch.distributed as dist
-
-        total = int(self.engine.counters[2].item())
-        count = total - self.sent
-        counts = torch.tensor([count], dtype=torch.int64, device=self.device)
-        all_counts = torch.empty(self.world, dtype=torch.int64, device=self.device)
-        dist.all_gather_into_tensor(all_counts, counts)
-        sizes = all_counts.tolist()
-        width = max(sizes)
-        if width == 0:
-            return
-        ring = self.engine.replay
-        feats, masks, pol, val, tp = ring.rows(self.sent % ring.capacity, count)
-        pad = width - count
-        parts = []
-        for t in (feats.reshape(count, -1), masks.to(torch.uint8), pol, val.reshape(count, 1),
-                  tp.reshape(count, 1).to(torch.float32)):
-            t = t.to(torch.float32) if t.dtype != torch.float32 else t
-            parts.append(torch.nn.functional.pad(t, (0, 0, 0, pad)))
-        packed = torch.cat(parts, dim=1).contiguous()
-        out = torch.empty((self.world * width, packed.shape[1]), dtype=torch.float32, device=self.device)
-        dist.all_gather_into_tensor(out, packed)
-        self.sent = total
-        if self.rank == 0 and self.fifo is not None:
-            pieces = [out[r * width:r * width + sizes[r]] for r in range(self.world)]
-            rows = torch.cat(pieces)
-            n = rows.shape[0]
-            idx = (torch.arange(n, device=self.device) + self.fifo_head) % self.fifo.capacity
-            self.fifo.features.view(self.fifo.capacity, -1)[idx] = rows[:, :810]
-            self.fifo.masks[idx] = rows[:, 810:892] != 0
-            self.fifo.policy[idx] = rows[:, 892:974]
-            self.fifo.value[idx] = rows[:, 974]
-            self.fifo.to_play[idx] = rows[:, 975].to(torch.int8)
-            self.fifo_head += n
 
 
 if __name__ == "__main__":

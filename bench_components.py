@@ -79,8 +79,9 @@ def bench_network(args, peaks):
             t_amp = timed(lambda: model(features), max(1, args.steps // 2), 1, flush)
     emit({"workload": f"network forward {channels}ch x {blocks} blocks, batch {n}", "metric": "positions/s",
           "value": n / (ms / 1e3), "unit": "positions/s", "ms_per_batch": ms, "dtype": "bf16",
-          "roofline": {"bound": "tensor", "achieved": tflops, "peak": peaks[0], "unit": "TFLOP/s",
-                       "frac": tflops / peaks[0], "flops_per_position": flops},
+          "roofline": {"bound": "tensor", "achieved": tflops, "peak": peaks[3], "unit": "TFLOP/s",
+                       "frac": tflops / peaks[3], "peak_kind": f"{peaks[2]} bf16 burst (kernel timed alone)",
+                       "flops_per_position": flops},
           "pytorch_fp32_ms": t_ref, "pytorch_bf16_autocast_ms": t_amp})
 
 
