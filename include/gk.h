@@ -178,6 +178,29 @@ GK_API int gk_puct_finish(void* ws, int64_t batch, int capacity, const gk_puct_r
 GK_API int gk_puct_search_hash(void* ws, int64_t batch, int simulations, const uint32_t* root_bits,
                         const gk_puct_options* options, const gk_puct_results_t* results, void* stream);
 
+/* Scratch limit of gk_puct_search_hash_noalloc per device: 16 MiB, e.g. 20
+ * trees of 400 simulations, 125 of 64 or 471 of 16. */
+#define GK_NOALLOC_SCRATCH_BYTES (16u * 1024u * 1024u)
+/* Returned when a request needs more scratch than GK_NOALLOC_SCRATCH_BYTES. */
+#define GK_ENOSPC (-28)
+
+/* gk_puct_search_hash without a caller workspace; it has no reference
+ * counterpart. For callers that can pass device buffers but cannot allocate
+ * device memory on the call path: a host-language binding with no CUDA
+ * allocator of its own (a cgo, JNI or ctypes stub holding only pointers it
+ * was given), or a service whose device memory is fixed at start-up. The
+ * trees live in a file-scope device array of GK_NOALLOC_SCRATCH_BYTES; a
+ * request whose gk_puct_workspace_bytes(batch, simulations + 1) exceeds it
+ * returns GK_ENOSPC and launches nothing. The first call on a device
+ * resolves the array's address with that device current (set-up): make it
+ * before any stream capture. Each call clears the root-noise rows to zero
+ * (this search draws no noise). All calls on a device share the array, so
+ * calls that overlap in time (other streams, other host threads) race: the
+ * caller serialises them. Calls no allocator. */
+GK_API int gk_puct_search_hash_noalloc(int64_t batch, int simulations, const uint32_t* root_bits,
+                                       const gk_puct_options* options, const gk_puct_results_t* results,
+                                       void* stream);
+
 /* -------------------------------------------------------------- network */
 
 /* Device pointers of a packed policy/value network (BN folded). Layout of
