@@ -5,9 +5,10 @@
 //   State::play            engine/src/State.cpp:92-167  (gpu_play, gpu_rules.py:185-252)
 //   Board::territory       engine/src/Board.cpp:149-198 (gpu_claim_territory, gpu_rules.py:124-172)
 //   legal placements       gpu_legal, gpu_rules.py:174-183
-// Flood fills are iterated 4-neighbour dilations masked by the passable set;
-// the padding column (bit r*10+9) is outside every mask, so horizontal shifts
-// need no column masks.
+// Flood fills are iterated 4-neighbour dilations masked by the passable set
+// (small regions: stone groups), or run-filling floods (large regions: the
+// territory passes); the padding column (bit r*10+9) is outside every mask,
+// so horizontal shifts need no column masks and row runs never join.
 #pragma once
 
 #include <cstdint>
@@ -56,6 +57,67 @@ __device__ __forceinline__ int select_bit(gk_b96 a, int j) {
     return word * 32 + base;
 }
 
+// ---- run-filling flood for large regions -------------------------------------
+// Within one row a region is a union of runs of set bits, and runs of
+// different rows are separated by the zero padding column. Adding the seeds
+// to the mask carries from each seed to the top of its run, so
+// ((m + x) ^ m) & m | x is every cell from a seed up to the end of its run;
+// the same on bit-reversed words covers the cells below the seed. A flood
+// then alternates a full horizontal closure with one vertical step, and
+// needs one iteration per vertical turn of the region instead of one per
+// cell of its radius.
+
+__device__ __forceinline__ gk_b96 add96(gk_b96 a, gk_b96 b) {
+    gk_b96 r;
+    asm("add.cc.u32 %0, %3, %6;\n\t"
+        "addc.cc.u32 %1, %4, %7;\n\t"
+        "addc.u32 %2, %5, %8;"
+        : "=r"(r.w[0]), "=r"(r.w[1]), "=r"(r.w[2])
+        : "r"(a.w[0]), "r"(a.w[1]), "r"(a.w[2]), "r"(b.w[0]), "r"(b.w[1]), "r"(b.w[2]));
+    return r;
+}
+
+// Bit i -> bit 95 - i.
+__device__ __forceinline__ gk_b96 rev96(gk_b96 a) { return gk_b(__brev(a.w[2]), __brev(a.w[1]), __brev(a.w[0])); }
+
+__device__ __forceinline__ gk_b96 xor96(gk_b96 a, gk_b96 b) {
+    return gk_b(a.w[0] ^ b.w[0], a.w[1] ^ b.w[1], a.w[2] ^ b.w[2]);
+}
+
+// Cells of mask m (mr = rev96(m)) in a horizontal run that holds a cell of x (x within m).
+__device__ __forceinline__ gk_b96 run_fill(gk_b96 m, gk_b96 mr, gk_b96 x) {
+    const gk_b96 up = gk_or(gk_and(xor96(add96(m, x), m), m), x);
+    const gk_b96 xr = rev96(x);
+    const gk_b96 down = rev96(gk_or(gk_and(xor96(add96(mr, xr), mr), mr), xr));
+    return gk_or(up, down);
+}
+
+// Same result as gk_flood(m, seed) for any region, fastest for large ones.
+__device__ __forceinline__ gk_b96 flood_runs(gk_b96 m, gk_b96 seed) {
+    const gk_b96 mr = rev96(m);
+    gk_b96 x = run_fill(m, mr, gk_and(seed, m));
+    for (;;) {
+        const gk_b96 fresh = gk_andnot(gk_and(gk_or(gk_shl(x, 10), gk_shr(x, 10)), m), x);
+        if (!gk_any(fresh)) return x;
+        x = gk_or(x, run_fill(m, mr, fresh));
+    }
+}
+
+// Two floods of one mask from two seed sets, advanced in the same loop.
+__device__ __forceinline__ void flood_runs2(gk_b96 m, gk_b96 sa, gk_b96 sb, gk_b96& ra, gk_b96& rb) {
+    const gk_b96 mr = rev96(m);
+    gk_b96 a = run_fill(m, mr, gk_and(sa, m)), b = run_fill(m, mr, gk_and(sb, m));
+    for (;;) {
+        const gk_b96 fa = gk_andnot(gk_and(gk_or(gk_shl(a, 10), gk_shr(a, 10)), m), a);
+        const gk_b96 fb = gk_andnot(gk_and(gk_or(gk_shl(b, 10), gk_shr(b, 10)), m), b);
+        if (!gk_any(gk_or(fa, fb))) break;
+        a = gk_or(a, run_fill(m, mr, fa));
+        b = gk_or(b, run_fill(m, mr, fb));
+    }
+    ra = a;
+    rb = b;
+}
+
 __device__ __forceinline__ gk_b96 empty_cells(const gk_bits& s) {
     gk_b96 occ = gk_or(gk_or(gk_get(&s, GK_PLANE_BLACK), gk_get(&s, GK_PLANE_WHITE)), gk_get(&s, GK_PLANE_NEUTRAL));
     return gk_andnot(gk_valid(), occ);
@@ -77,17 +139,17 @@ __device__ __forceinline__ gk_b96 legal_placements(const gk_bits& s) {
 __device__ __forceinline__ void claim_territory(gk_bits& s) {
     const gk_b96 black = gk_get(&s, GK_PLANE_BLACK), white = gk_get(&s, GK_PLANE_WHITE);
     const gk_b96 E = empty_cells(s);
-    const gk_b96 near_black = gk_flood(E, gk_and(E, gk_neighbours(black)));
-    const gk_b96 near_white = gk_flood(E, gk_and(E, gk_neighbours(white)));
+    gk_b96 near_black, near_white;
+    flood_runs2(E, gk_and(E, gk_neighbours(black)), gk_and(E, gk_neighbours(white)), near_black, near_white);
     gk_b96 pb = gk_andnot(near_black, near_white);
     gk_b96 pw = gk_andnot(near_white, near_black);
     const gk_b96 C = gk_or(pb, pw);
     if (!gk_any(C)) return;
     // Components touching all four edges: nested floods by edge.
-    gk_b96 t = gk_flood(C, gk_and(C, gk_b(GK_ROW0_0, 0u, 0u)));
-    if (gk_any(t)) t = gk_flood(t, gk_and(t, gk_b(0u, 0u, GK_ROW8_2)));
-    if (gk_any(t)) t = gk_flood(t, gk_and(t, gk_b(GK_COL0_0, GK_COL0_1, GK_COL0_2)));
-    if (gk_any(t)) t = gk_flood(t, gk_and(t, gk_b(GK_COL8_0, GK_COL8_1, GK_COL8_2)));
+    gk_b96 t = flood_runs(C, gk_and(C, gk_b(GK_ROW0_0, 0u, 0u)));
+    if (gk_any(t)) t = flood_runs(t, gk_and(t, gk_b(0u, 0u, GK_ROW8_2)));
+    if (gk_any(t)) t = flood_runs(t, gk_and(t, gk_b(GK_COL0_0, GK_COL0_1, GK_COL0_2)));
+    if (gk_any(t)) t = flood_runs(t, gk_and(t, gk_b(GK_COL8_0, GK_COL8_1, GK_COL8_2)));
     pb = gk_andnot(pb, t);
     pw = gk_andnot(pw, t);
     const gk_b96 ob = gk_get(&s, GK_PLANE_OWN_BLACK), ow = gk_get(&s, GK_PLANE_OWN_WHITE);

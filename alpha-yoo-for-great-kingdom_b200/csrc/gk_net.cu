@@ -460,42 +460,78 @@ constexpr int kPolStride = 163;  // odd row stride: conflict-free lane-per-row r
 constexpr int kValStride = 81;
 constexpr size_t kHeadSmem = (size_t)(82 * kPolStride + 64 * kValStride + 8 * 244) * sizeof(float);
 
+// Copies an N-float row-major matrix of COLS columns into shared memory with
+// row stride STRIDE. Each thread issues a batch of independent read-only
+// loads before its shared stores; a load-store pair per iteration would
+// serialise on global latency (a generic source pointer may alias shared
+// memory, so the compiler cannot move loads ahead of the stores).
+template <int N, int COLS, int STRIDE>
+__device__ __forceinline__ void stage_matrix(float* dst, const float* src) {
+    constexpr int kBatch = 8;
+    for (int base = threadIdx.x; base < N; base += blockDim.x * kBatch) {
+        float v[kBatch];
+#pragma unroll
+        for (int u = 0; u < kBatch; ++u) {
+            const int i = base + u * (int)blockDim.x;
+            v[u] = i < N ? __ldg(src + i) : 0.f;
+        }
+#pragma unroll
+        for (int u = 0; u < kBatch; ++u) {
+            const int i = base + u * (int)blockDim.x;
+            if (i < N) dst[(i / COLS) * STRIDE + i % COLS] = v[u];
+        }
+    }
+}
+
 __global__ void __launch_bounds__(256) net_heads_kernel(NetParams p, const float* headfeat, NetInput in, HeadOut out) {
     extern __shared__ float hs[];
     float* wp = hs;
     float* w1 = wp + 82 * kPolStride;
     float* feat_all = w1 + 64 * kValStride;
-    for (int i = threadIdx.x; i < 82 * 162; i += blockDim.x) wp[(i / 162) * kPolStride + i % 162] = p.pol_w[i];
-    for (int i = threadIdx.x; i < 64 * 81; i += blockDim.x) w1[i] = p.val_w1[i];
+    stage_matrix<82 * 162, 162, kPolStride>(wp, p.pol_w);
+    stage_matrix<64 * 81, 81, kValStride>(w1, p.val_w1);
     __syncthreads();
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     float* feat = feat_all + warp * 244;
     const int count = input_count(in);
+    // Lane l owns actions l, l+32, l+64 (the last only for l < 18) and hidden
+    // units l, l+32 of the value head.
+    const float* wa = wp + lane * kPolStride;
+    const float* wb = wp + (lane + 32) * kPolStride;
+    const float* wc = wp + (lane + 64 < GK_ACTIONS ? lane + 64 : GK_ACTIONS - 1) * kPolStride;
+    const float* va = w1 + lane * kValStride;
+    const float* vb = w1 + (lane + 32) * kValStride;
     for (int img = blockIdx.x * 8 + warp; img < count; img += gridDim.x * 8) {
         const float* hf = headfeat + (int64_t)img * 243;
-        for (int k = lane; k < 243; k += 32) feat[k] = hf[k];
+        float fv[8];
+#pragma unroll
+        for (int u = 0; u < 8; ++u) fv[u] = lane + 32 * u < 243 ? __ldg(hf + lane + 32 * u) : 0.f;
+#pragma unroll
+        for (int u = 0; u < 8; ++u)
+            if (lane + 32 * u < 243) feat[lane + 32 * u] = fv[u];
         __syncwarp();
+        // Three independent accumulation chains, each summed in feature order.
+        float la = 0.f, lb = 0.f, lc = 0.f;
+#pragma unroll 6
+        for (int j = 0; j < 162; ++j) {
+            const float f = feat[j];
+            la = fmaf(wa[j], f, la);
+            lb = fmaf(wb[j], f, lb);
+            lc = fmaf(wc[j], f, lc);
+        }
         float logit[3];
-#pragma unroll
-        for (int k = 0; k < 3; ++k) {
-            const int a = lane + 32 * k;
-            float acc = 0.f;
-            if (a < GK_ACTIONS) {
-                const float* w = wp + a * kPolStride;
-                for (int j = 0; j < 162; ++j) acc = fmaf(w[j], feat[j], acc);
-                acc += __ldg(p.pol_b + a);
-            }
-            logit[k] = acc;
+        logit[0] = la + __ldg(p.pol_b + lane);
+        logit[1] = lb + __ldg(p.pol_b + lane + 32);
+        logit[2] = lane + 64 < GK_ACTIONS ? lc + __ldg(p.pol_b + lane + 64) : 0.f;
+        float ha = __ldg(p.val_b1 + lane), hb = __ldg(p.val_b1 + lane + 32);
+#pragma unroll 9
+        for (int j = 0; j < 81; ++j) {
+            const float f = feat[162 + j];
+            ha = fmaf(va[j], f, ha);
+            hb = fmaf(vb[j], f, hb);
         }
-        float vpart = 0.f;
-#pragma unroll
-        for (int k = 0; k < 2; ++k) {
-            const int u = lane + 32 * k;
-            const float* w = w1 + u * kValStride;
-            float acc = __ldg(p.val_b1 + u);
-            for (int j = 0; j < 81; ++j) acc = fmaf(w[j], feat[162 + j], acc);
-            vpart = fmaf(fmaxf(acc, 0.f), __ldg(p.val_w2 + u), vpart);
-        }
+        float vpart = fmaf(fmaxf(ha, 0.f), __ldg(p.val_w2 + lane), 0.f);
+        vpart = fmaf(fmaxf(hb, 0.f), __ldg(p.val_w2 + lane + 32), vpart);
 #pragma unroll
         for (int off = 16; off; off >>= 1) vpart += __shfl_xor_sync(0xffffffffu, vpart, off);
         const float value = tanhf(vpart + __ldg(p.val_b2));

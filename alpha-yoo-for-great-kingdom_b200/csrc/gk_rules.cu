@@ -5,9 +5,11 @@
 //   wire records  int32 [N,170]  (python/kingdom_ai/gpu_rules.py:16-33)
 //   packed states uint32[N,16]   (gk_bits, 64 B; include/gk_common.h)
 //   features      fp32  [N,10,9,9], masks bool [N,82]
-// Streaming kernels stage whole blocks of records/states through shared
-// memory with coalesced 16-byte loads and stores; one thread then owns one
-// state in registers.
+// Wire-record kernels stage whole blocks of records through shared memory
+// with coalesced 16-byte loads and stores; one thread then owns one state in
+// registers. The packed-state transition reads and writes each 64-byte state
+// directly, and the packed-state encoder builds its output rows in shared
+// memory and writes them with bulk (TMA) stores.
 #include <cuda_runtime.h>
 
 #include <cstdint>
@@ -15,6 +17,7 @@
 #include "../../include/gk.h"
 #include "gk_device.cuh"
 #include "gk_launch.cuh"
+#include "gk_tc.cuh"
 
 namespace gk {
 
@@ -203,16 +206,89 @@ __global__ void __launch_bounds__(kRecBlock) encode_records_kernel(const int32_t
     }
 }
 
-__global__ void __launch_bounds__(kRecBlock) encode_bits_kernel(const gk_bits* bits, float* features,
-                                                                 uint8_t* masks, int64_t n) {
-    __shared__ PlaneSmem planes;
-    for (int64_t base = (int64_t)blockIdx.x * kRecBlock; base < n; base += (int64_t)gridDim.x * kRecBlock) {
-        const int count = (int)(n - base < kRecBlock ? n - base : kRecBlock);
-        if ((int)threadIdx.x < count) store_planes(planes, threadIdx.x, encode_planes(bits[base + threadIdx.x]));
+// Encoder from packed states, in chunks of kEncChunk positions per block:
+//   1. one thread per position computes its planes (registers -> shared);
+//   2. one thread per (position, cell) writes the cell's 10 plane values and
+//      its mask byte into a shared-memory image of the chunk's output rows,
+//      which are contiguous in HBM (kEncChunk * 3,240 + kEncChunk * 82 bytes);
+//   3. one thread hands the image to the TMA engine as two bulk stores.
+// Two images alternate, so a chunk is computed while the previous one drains.
+// Outputs that are not 16-byte aligned, and a final partial chunk, are
+// copied out with ordinary stores instead.
+constexpr int kEncChunk = 16;
+constexpr int kEncThreads = 256;
+
+struct EncodeStage {
+    float feat[2][kEncChunk * GK_FEATURES];   // 2 x 51,840 B (16-byte aligned)
+    uint8_t mask[2][kEncChunk * GK_ACTIONS];  // 2 x 1,312 B
+    uint32_t bits[kEncChunk][18];              // own, enemy, neutral, own_terr, enemy_terr, legal
+    float consts[kEncChunk][4];
+    uint32_t pass_legal[kEncChunk];
+};
+constexpr size_t kEncSmem = sizeof(EncodeStage);
+
+template <bool kBulk>
+__global__ void __launch_bounds__(kEncThreads) encode_bits_kernel(const gk_bits* bits, float* features,
+                                                                   uint8_t* masks, int64_t n) {
+    extern __shared__ __align__(128) uint8_t enc_smem[];
+    EncodeStage& st = *reinterpret_cast<EncodeStage*>(enc_smem);
+    const int64_t chunks = (n + kEncChunk - 1) / kEncChunk;
+    int buf = 0;
+    for (int64_t c = blockIdx.x; c < chunks; c += gridDim.x, buf ^= 1) {
+        const int64_t base = c * kEncChunk;
+        const int count = (int)(n - base < kEncChunk ? n - base : kEncChunk);
+        if ((int)threadIdx.x < count) {
+            const EncodePlanes e = encode_planes(bits[base + threadIdx.x]);
+            const gk_b96 v[6] = {e.own, e.enemy, e.neutral, e.own_terr, e.enemy_terr, e.legal};
+#pragma unroll
+            for (int k = 0; k < 6; ++k) {
+                st.bits[threadIdx.x][3 * k] = v[k].w[0];
+                st.bits[threadIdx.x][3 * k + 1] = v[k].w[1];
+                st.bits[threadIdx.x][3 * k + 2] = v[k].w[2];
+            }
+            st.consts[threadIdx.x][0] = e.black_to_play;
+            st.consts[threadIdx.x][1] = e.own_remaining;
+            st.consts[threadIdx.x][2] = e.enemy_remaining;
+            st.consts[threadIdx.x][3] = e.passes;
+            st.pass_legal[threadIdx.x] = e.pass_legal ? 1u : 0u;
+        }
+        // The image in `buf` went to a bulk store two chunks ago; it must have
+        // been read out before it is overwritten.
+        if (kBulk && threadIdx.x == 0) tc::bulk_wait_read<1>();
         __syncthreads();
-        write_encoded(planes, count, features + base * GK_FEATURES, masks + base * GK_ACTIONS);
+        float* out = st.feat[buf];
+        uint8_t* mout = st.mask[buf];
+        for (int i = threadIdx.x; i < count * GK_CELLS; i += blockDim.x) {
+            const int pos = i / GK_CELLS, cell = i - pos * GK_CELLS;
+            const int bit = cell + cell / 9;
+            const int w = bit >> 5, sh = bit & 31;
+            const uint32_t* b = st.bits[pos];
+            float* o = out + pos * GK_FEATURES + cell;
+#pragma unroll
+            for (int k = 0; k < 5; ++k) o[k * GK_CELLS] = ((b[3 * k + w] >> sh) & 1u) ? 1.0f : 0.0f;
+#pragma unroll
+            for (int k = 0; k < 4; ++k) o[(5 + k) * GK_CELLS] = st.consts[pos][k];
+            const uint32_t legal = (b[15 + w] >> sh) & 1u;
+            o[9 * GK_CELLS] = legal ? 1.0f : 0.0f;
+            mout[pos * GK_ACTIONS + cell] = (uint8_t)legal;
+        }
+        if ((int)threadIdx.x < count) mout[threadIdx.x * GK_ACTIONS + GK_PASS] = (uint8_t)st.pass_legal[threadIdx.x];
+        if (kBulk) tc::fence_proxy_async_smem();  // generic-proxy writes -> visible to the bulk copy
         __syncthreads();
+        if (kBulk && count == kEncChunk) {
+            if (threadIdx.x == 0) {
+                tc::bulk_s2g(features + base * GK_FEATURES, tc::smem_u32(out), kEncChunk * GK_FEATURES * 4);
+                tc::bulk_s2g(masks + base * GK_ACTIONS, tc::smem_u32(mout), kEncChunk * GK_ACTIONS);
+                tc::bulk_commit();
+            }
+        } else {
+            float* fdst = features + base * GK_FEATURES;
+            for (int i = threadIdx.x; i < count * GK_FEATURES; i += blockDim.x) fdst[i] = out[i];
+            uint8_t* mdst = masks + base * GK_ACTIONS;
+            for (int i = threadIdx.x; i < count * GK_ACTIONS; i += blockDim.x) mdst[i] = mout[i];
+        }
     }
+    if (kBulk && threadIdx.x == 0) tc::bulk_wait<0>();
 }
 
 __global__ void __launch_bounds__(kRecBlock) records_to_bits_kernel(const int32_t* recs, gk_bits* bits,
@@ -246,25 +322,40 @@ __global__ void __launch_bounds__(kRecBlock) bits_to_records_kernel(const gk_bit
     }
 }
 
+// One state per thread, grid-stride. Each thread reads and writes its own
+// 64-byte state directly (four 16-byte accesses when the array is 16-byte
+// aligned); with no block-wide staging a state whose transition runs long
+// (big flood fills) delays only its own warp. Rejected states are not
+// written back.
+template <bool kVector>
 __global__ void __launch_bounds__(kBitsBlock) play_bits_kernel(gk_bits* bits, const void* actions, int action_bytes,
                                                                 uint8_t* accepted, int64_t n) {
-    __shared__ __align__(16) gk_bits tile[kBitsBlock];
-    for (int64_t base = (int64_t)blockIdx.x * kBitsBlock; base < n; base += (int64_t)gridDim.x * kBitsBlock) {
-        const int count = (int)(n - base < kBitsBlock ? n - base : kBitsBlock);
-        block_copy_in(reinterpret_cast<uint32_t*>(tile), reinterpret_cast<const uint32_t*>(bits + base),
-                      (int64_t)count * 16);
-        __syncthreads();
-        const int t = threadIdx.x;
-        if (t < count) {
-            gk_bits s = tile[t];
-            const bool ok = play(s, read_action(actions, action_bytes, base + t));
-            accepted[base + t] = ok ? 1 : 0;
-            if (ok) tile[t] = s;
+    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
+        gk_bits s;
+        if (kVector) {
+            const uint4* src = reinterpret_cast<const uint4*>(bits + i);
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+                const uint4 v = __ldcs(src + q);
+                s.w[4 * q] = v.x;
+                s.w[4 * q + 1] = v.y;
+                s.w[4 * q + 2] = v.z;
+                s.w[4 * q + 3] = v.w;
+            }
+        } else {
+            s = bits[i];
         }
-        __syncthreads();
-        block_copy_out(reinterpret_cast<uint32_t*>(bits + base), reinterpret_cast<const uint32_t*>(tile),
-                       (int64_t)count * 16);
-        __syncthreads();
+        const bool ok = play(s, read_action(actions, action_bytes, i));
+        accepted[i] = ok ? 1 : 0;
+        if (!ok) continue;
+        if (kVector) {
+            uint4* dst = reinterpret_cast<uint4*>(bits + i);
+#pragma unroll
+            for (int q = 0; q < 4; ++q)
+                __stcs(dst + q, make_uint4(s.w[4 * q], s.w[4 * q + 1], s.w[4 * q + 2], s.w[4 * q + 3]));
+        } else {
+            bits[i] = s;
+        }
     }
 }
 
@@ -346,7 +437,11 @@ bool configure_rules_kernels() {
                cudaFuncSetAttribute(records_to_bits_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                     (int)kRecSmem) == cudaSuccess &&
                cudaFuncSetAttribute(bits_to_records_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                    (int)kRecSmem) == cudaSuccess;
+                                    (int)kRecSmem) == cudaSuccess &&
+               cudaFuncSetAttribute(encode_bits_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                    (int)kEncSmem) == cudaSuccess &&
+               cudaFuncSetAttribute(encode_bits_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                    (int)kEncSmem) == cudaSuccess;
     });
 }
 
@@ -412,16 +507,26 @@ int gk_play_bits(uint32_t* bits, const void* actions, int action_bytes, uint8_t*
     if (bits == nullptr || actions == nullptr || accepted == nullptr || n < 0) return GK_EINVAL;
     if (action_bytes != 4 && action_bytes != 8) return GK_EINVAL;
     if (n == 0) return 0;
-    play_bits_kernel<<<blocks_for(n, kBitsBlock, kSmCount * 8), kBitsBlock, 0, as_stream(stream)>>>(
-        reinterpret_cast<gk_bits*>(bits), actions, action_bytes, accepted, n);
+    const int grid = blocks_for(n, kBitsBlock, kSmCount * 8);
+    if (aligned16(bits))
+        play_bits_kernel<true><<<grid, kBitsBlock, 0, as_stream(stream)>>>(reinterpret_cast<gk_bits*>(bits), actions,
+                                                                          action_bytes, accepted, n);
+    else
+        play_bits_kernel<false><<<grid, kBitsBlock, 0, as_stream(stream)>>>(reinterpret_cast<gk_bits*>(bits), actions,
+                                                                           action_bytes, accepted, n);
     return launch_status();
 }
 
 int gk_encode_bits(const uint32_t* bits, float* features, uint8_t* masks, int64_t n, void* stream) {
     if (bits == nullptr || features == nullptr || masks == nullptr || n < 0) return GK_EINVAL;
     if (n == 0) return 0;
-    encode_bits_kernel<<<rec_grid(n), kRecBlock, 0, as_stream(stream)>>>(reinterpret_cast<const gk_bits*>(bits),
-                                                                           features, masks, n);
+    if (!configure_rules_kernels()) return launch_status();
+    const int grid = blocks_for(n, kEncChunk, kSmCount * 2);
+    const gk_bits* states = reinterpret_cast<const gk_bits*>(bits);
+    if (aligned16(features) && aligned16(masks))
+        encode_bits_kernel<true><<<grid, kEncThreads, kEncSmem, as_stream(stream)>>>(states, features, masks, n);
+    else
+        encode_bits_kernel<false><<<grid, kEncThreads, kEncSmem, as_stream(stream)>>>(states, features, masks, n);
     return launch_status();
 }
 

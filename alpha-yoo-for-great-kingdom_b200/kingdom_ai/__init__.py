@@ -11,3 +11,4 @@ from .gpu_rules import (  # noqa: F401
     GPU_WINNER, GpuStateBatch,
 )
 from .gpu_puct import GpuPUCT, GpuPUCTOptions, GpuSearchResult, HashEvaluator  # noqa: F401
+from .training import Cell, EndReason, GameData, TrainingSample, collect_gpu_puct_games  # noqa: F401

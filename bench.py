@@ -270,6 +270,10 @@ def main():
                         help="selfplay is the headline; the others time one kernel family each")
     parser.add_argument("--net", default="128x10", help="network workload: CHANNELSxBLOCKS")
     parser.add_argument("--batch", type=int, default=8192, help="network workload batch")
+    parser.add_argument("--states", type=int, default=1 << 22, help="rules workload: states per play launch")
+    parser.add_argument("--positions", type=int, default=65536, help="encode workload: positions")
+    parser.add_argument("--trees", type=int, default=1024, help="puct workload: trees")
+    parser.add_argument("--sims", type=int, default=800, help="puct workload: simulations per tree")
     args = parser.parse_args()
     if args.impl == "reference":
         reference_arm(args)

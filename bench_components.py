@@ -95,7 +95,7 @@ def bench_rules(args, peaks):
     ms = timed(lambda: native.call("gk_random_playouts", 2024, 0, n, 40, native.ptr(boards), native.ptr(infos),
                                    stream), args.steps, args.warmup, flush)
     plies = int(infos[:, 4].sum().item())
-    big = 1 << 22
+    big = args.states
     bits = positions(big, 99, device)
     work = bits.clone()
     actions = torch.randint(0, 82, (big,), dtype=torch.int32, device=device)
@@ -115,7 +115,7 @@ def bench_rules(args, peaks):
     play_ms = total / args.steps
     bytes_per_state = 64 + 4 + 64 + 1
     gbs = big * bytes_per_state / (play_ms / 1e3) / 1e9
-    emit({"workload": "rules: 4096 uniform-random complete playouts; one transition of 2^22 packed states",
+    emit({"workload": f"rules: 4096 uniform-random complete playouts; one transition of {big} packed states",
           "metric": "playout moves/s", "value": plies / (ms / 1e3), "unit": "moves/s",
           "games_per_s": n / (ms / 1e3), "playout_ms": ms, "mean_plies": plies / n,
           "play_kernel": {"states": big, "ms": play_ms, "states_per_s": big / (play_ms / 1e3)},
@@ -128,7 +128,8 @@ def bench_encode(args, peaks):
     flush = Flusher(device)
     stream = native.stream_of(device)
     out = {}
-    for n in (65536, 1 << 20):
+    small, big = args.positions, 1 << 20
+    for n in (small, big):
         bits = positions(n, 11, device)
         feats = torch.empty((n, 10, 9, 9), dtype=torch.float32, device=device)
         masks = torch.empty((n, 82), dtype=torch.bool, device=device)
@@ -136,11 +137,10 @@ def bench_encode(args, peaks):
                                        stream), args.steps, args.warmup, flush)
         out[n] = ms
     bytes_per_pos = 64 + 3240 + 82
-    n = 65536
+    n = small
     gbs = n * bytes_per_pos / (out[n] / 1e3) / 1e9
-    big = 1 << 20
     gbs_big = big * bytes_per_pos / (out[big] / 1e3) / 1e9
-    emit({"workload": "encode 65,536 generated positions (and 2^20)", "metric": "positions/s",
+    emit({"workload": f"encode {n} generated positions (and 2^20)", "metric": "positions/s",
           "value": n / (out[n] / 1e3), "unit": "positions/s", "ms": out[n], "ms_2pow20": out[big],
           "roofline": {"bound": "hbm", "kernel": "encode_bits_kernel", "achieved": gbs, "peak": peaks[1],
                        "unit": "GB/s", "frac": gbs / peaks[1], "bytes_per_position": bytes_per_pos,
@@ -152,7 +152,7 @@ def bench_puct(args, peaks):
 
     device = torch.device("cuda", 0)
     flush = Flusher(device)
-    n, sims = 1024, 800
+    n, sims = args.trees, args.sims
     bits = positions(n, 4242, device)
     holder = {}
 
@@ -162,6 +162,6 @@ def bench_puct(args, peaks):
     ms = timed(run, max(1, args.steps // 3), 1, flush)
     r = holder["r"]
     assert int(r.simulations.sum().item()) == n * sims
-    emit({"workload": "PUCT 1024 trees x 800 simulations, injected evaluator, c_puct 1.5", "metric": "simulations/s",
+    emit({"workload": f"PUCT {n} trees x {sims} simulations, injected evaluator, c_puct 1.5", "metric": "simulations/s",
           "value": n * sims / (ms / 1e3), "unit": "simulations/s", "ms_per_search": ms,
           "nodes_mean": float(r.nodes.float().mean().item())})

@@ -91,3 +91,19 @@ def test_product_never_imports_the_oracle():
     for path in list(package.rglob("*.py")) + list(package.rglob("*.cu")) + list(package.rglob("*.cuh")):
         text = path.read_text()
         assert "oracle" not in text.replace("the oracle", ""), path
+
+
+def test_collect_gpu_puct_games_validates_like_the_reference():
+    """python/kingdom_ai/gpu_training.py:150-168; all checks run before any device work."""
+    from kingdom_ai.gpu_puct import HashEvaluator
+    from kingdom_ai.training import collect_gpu_puct_games
+
+    assert collect_gpu_puct_games(HashEvaluator(), 0) == []
+    for kw, exc in (({"games": -1}, ValueError), ({"batch_size": 0}, ValueError), ({"seed": -1}, ValueError),
+                    ({"temperature": float("nan")}, ValueError), ({"temperature": True}, TypeError),
+                    ({"temperature_moves": -2}, ValueError), ({"record_history": 1}, TypeError),
+                    ({"options": object()}, TypeError)):
+        args = {"games": 1, **kw}
+        games = args.pop("games")
+        with pytest.raises(exc):
+            collect_gpu_puct_games(HashEvaluator(), games, **args)
