@@ -72,7 +72,7 @@ __global__ void puct_begin_kernel(PuctView v, int64_t B, int C, const gk_bits* r
     }
 }
 
-__global__ void __launch_bounds__(32 * kWarpsPerBlock) puct_select_kernel(PuctView v, int64_t B, int C, PuctOptions o) {
+__global__ void __launch_bounds__(32 * kWarpsPerBlock, 6) puct_select_kernel(PuctView v, int64_t B, int C, PuctOptions o) {
     const int lane = threadIdx.x & 31;
     const int64_t t = (blockIdx.x * (int64_t)blockDim.x + threadIdx.x) >> 5;
     if (t >= B) return;
@@ -84,10 +84,16 @@ __global__ void __launch_bounds__(32 * kWarpsPerBlock) puct_select_kernel(PuctVi
     }
     const int64_t tbase = t * C;
     int node = 0, depth = 0;
-    // The current node's state stays in registers; a child created during this
-    // pass is known to be unexpanded, so no lane reads memory another lane of
-    // this warp has just written.
+    // The current node's state and statistics stay in registers. All loads a
+    // tree level needs are issued together - the node's statistics with its
+    // state, and this lane's three edges (visits, prior, W, child) in one go -
+    // so a level costs two dependent global round trips. A child created
+    // during this pass is known to be unexpanded, so no lane reads memory
+    // another lane of this warp has just written.
     gk_bits st = v.node_state[tbase];
+    bool expanded = v.expanded[tbase] != 0;
+    int node_n = v.node_visits[tbase];
+    float node_q = v.node_value[tbase];
     bool fresh = false;
     for (;;) {
         const int64_t vtx = tbase + node;
@@ -95,25 +101,38 @@ __global__ void __launch_bounds__(32 * kWarpsPerBlock) puct_select_kernel(PuctVi
             if (lane == 0) v.leaf_value[t] = terminal_value(st);
             break;
         }
-        if (fresh || !v.expanded[vtx]) {
+        if (fresh || !expanded) {
             if (lane == 0) {
                 v.needs_eval[t] = 1;
                 v.leaf_bits[t] = st;
             }
             break;
         }
-        const double scale = sqrt((double)v.node_visits[vtx]);
-        const gk_b96 placements = legal_placements(st);
         const int64_t ebase = vtx * GK_ACTIONS;
+        int en[3], ech[3];
+        double ep[3], ew[3];
+#pragma unroll
+        for (int k = 0; k < 3; ++k) {
+            const int a = lane + 32 * k;
+            const bool in_row = a < GK_ACTIONS;
+            en[k] = in_row ? v.visits[ebase + a] : 0;
+            ep[k] = in_row ? v.prior[ebase + a] : 0.0;
+            ew[k] = in_row ? v.wsum[ebase + a] : 0.0;
+            ech[k] = in_row ? v.child[ebase + a] : -1;
+        }
+        const double scale = sqrt((double)node_n);
+        const gk_b96 placements = legal_placements(st);
         int best = -1;
         double best_score = 0.0, best_prior = 0.0;
-        for (int a = lane; a < GK_ACTIONS; a += 32) {
-            if (!action_legal(placements, true, a)) continue;
-            const int n = v.visits[ebase + a];
-            const double p = v.prior[ebase + a];
+#pragma unroll
+        for (int k = 0; k < 3; ++k) {
+            const int a = lane + 32 * k;
+            if (a >= GK_ACTIONS || !action_legal(placements, true, a)) continue;
+            const int n = en[k];
+            const double p = ep[k];
             double q;
-            if (n == 0) q = o.fpu_enabled != 0.0 ? GK_DSUB((double)v.node_value[vtx], o.fpu_reduction) : 0.0;
-            else q = v.wsum[ebase + a] / (double)n;
+            if (n == 0) q = o.fpu_enabled != 0.0 ? GK_DSUB((double)node_q, o.fpu_reduction) : 0.0;
+            else q = ew[k] / (double)n;
             const double expl = GK_DMUL(p, scale) / GK_DADD(1.0, (double)n);
             const double score = o.c_puct >= 1.0 ? GK_DADD(q / o.c_puct, expl) : GK_DADD(q, GK_DMUL(o.c_puct, expl));
             if (best < 0 || score > best_score || (score == best_score && p > best_prior)) {
@@ -143,7 +162,9 @@ __global__ void __launch_bounds__(32 * kWarpsPerBlock) puct_select_kernel(PuctVi
             }
             break;
         }
-        int ch = v.child[ebase + best];
+        // The chosen edge's child index is already in the lane that owns it.
+        const int slot = best >> 5;
+        int ch = __shfl_sync(kFull, slot == 0 ? ech[0] : slot == 1 ? ech[1] : ech[2], best & 31);
         if (ch < 0) {
             gk_bits next = st;
             const bool ok = play(next, best);
@@ -167,6 +188,9 @@ __global__ void __launch_bounds__(32 * kWarpsPerBlock) puct_select_kernel(PuctVi
             fresh = true;
         } else {
             st = v.node_state[tbase + ch];
+            expanded = v.expanded[tbase + ch] != 0;
+            node_n = v.node_visits[tbase + ch];
+            node_q = v.node_value[tbase + ch];
             fresh = false;
         }
         if (lane == 0) {
