@@ -172,9 +172,11 @@ GK_API int gk_puct_expand_backup(void* ws, int64_t batch, int capacity, const gk
 GK_API int gk_puct_finish(void* ws, int64_t batch, int capacity, const gk_puct_results_t* results, void* stream);
 
 /* A complete search with the injected evaluator, no host synchronisation:
- * begin, root evaluation, `simulations` x (select, evaluate, expand/backup),
- * finish. The workspace must be sized for capacity = simulations + 1.
- * Equivalent of PUCT::search (mcts/src/PUCT.cpp:177-268) per tree. */
+ * begin, then one kernel in which each tree's warp runs the root evaluation
+ * and `simulations` x (select, evaluate, expand/backup), then finish. Results
+ * equal those of the separate gk_puct_* steps. The workspace must be sized
+ * for capacity = simulations + 1. Equivalent of PUCT::search
+ * (mcts/src/PUCT.cpp:177-268) per tree. */
 GK_API int gk_puct_search_hash(void* ws, int64_t batch, int simulations, const uint32_t* root_bits,
                         const gk_puct_options* options, const gk_puct_results_t* results, void* stream);
 

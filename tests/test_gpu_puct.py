@@ -55,6 +55,27 @@ def test_hash_search_full_size_bit_exact(kai, oracle):
     assert np.array_equal(result.root_values.cpu().numpy(), roots)
 
 
+
+def test_fused_hash_search_equals_the_step_by_step_search(kai):
+    """gk_puct_search_hash (one kernel, a warp per tree) against GpuPUCT's
+    per-simulation select / evaluate / expand launches, c_puct 1.25, FPU 0.2."""
+    from kingdom_ai import _native as native
+    from kingdom_ai.gpu_puct import SearchWorkspace, _allocate_results
+
+    n, sims = 300, 96
+    bits = torch.empty((n, 16), dtype=torch.int32, device="cuda")
+    native.call("gk_gen_positions", 99, 0, n, native.ptr(bits), native.stream_of(bits.device))
+    options = kai.GpuPUCTOptions(simulations=sims, c_puct=1.25, dirichlet_epsilon=0.0, fpu_reduction=0.2, seed=1)
+    step = kai.GpuPUCT(kai.HashEvaluator(), options).search_packed(bits)
+    ws = SearchWorkspace(n, sims + 1, bits.device)
+    out = _allocate_results(n, bits.device)
+    native.call("gk_puct_search_hash", ws.pointer, n, sims, native.ptr(bits), native.PuctOptions(1.25, 0.0, 1, 0.2),
+                out.struct, native.stream_of(bits.device))
+    fused = out.result()
+    for name in ("actions", "visits", "policy", "values", "simulations", "network_evaluations", "priors",
+                 "best_values", "nodes", "root_values"):
+        assert torch.equal(getattr(fused, name), getattr(step, name)), name
+
 def zero_model(kai):
     from kingdom_ai.model import PolicyValueNet
     torch.manual_seed(829)
