@@ -362,7 +362,7 @@ __global__ void __launch_bounds__(NetCfg<C>::THREADS, 1)
 #pragma unroll
                 for (int j = 0; j < HALF; ++j) bias[j] = __ldg(p.conv_b + l * C + col0 + j);
                 for (int t = 0; t < K::T; ++t) {
-                    if (!tc::mbar_wait(acc_full + 8 * t, (uint32_t)a & 1u, status)) goto epi_done_label;
+                    if (!warp_wait(acc_full + 8 * t, (uint32_t)a & 1u, status, lane == 0)) goto epi_done_label;
                     tc::tc_fence_after();
                     const int m = t * 128 + q * 32 + lane;
                     const int img = m / 100, pos = m - img * 100, r = pos / 10, cc = pos - r * 10;
@@ -411,7 +411,7 @@ __global__ void __launch_bounds__(NetCfg<C>::THREADS, 1)
             // final rows, once all eight warps have written them.
             __syncwarp();
             if (lane == 0) tc::mbar_arrive(heads_ready);
-            if (!tc::mbar_wait(heads_ready, (uint32_t)i & 1u, status)) goto epi_done_label;
+            if (!warp_wait(heads_ready, (uint32_t)i & 1u, status, lane == 0)) goto epi_done_label;
             for (int m = etid; m < K::T * 128; m += 32 * K::EPI_WARPS) {
                 const int img = m / 100, pos = m - img * 100, r = pos / 10, cc = pos - r * 10;
                 if (!(img < nimg && r < 9 && cc < 9)) continue;
@@ -445,6 +445,363 @@ done:
         tc::tc_fence_after();
         tc::tmem_dealloc(tmem, 512);
     }
+}
+
+// ---- 64-channel tower with column-fused taps ----------------------------------
+// For C = 64 an MMA of N = 64 output channels is bound by shared-memory operand
+// traffic (A 4 KB + B 2 KB per 128x64x16 step): the nine-tap issue pattern
+// measured 2,078 cycles per 128-row tile on B200, against 1,410 for the
+// pattern used here. The column taps dc = 0 and dc = +1 of each row offset dr
+// share one MMA of N = 128: B = [W(dr,0) | W(dr,+1)] on A shifted by 10 dr
+// rows, so the accumulator holds P0[m] (dc = 0) and P1[m] = sum_dr x[m + 10 dr]
+// W(dr,+1). The tap dc = -1 is an N = 64 MMA on A shifted by 10 dr - 1 rows
+// that accumulates straight into P0. The output row is then
+//     y[m] = P0[m] + P1[m+1],
+// a one-row shift the epilogue applies with a warp shuffle and, at TMEM
+// lane-quadrant boundaries, a shared-memory exchange. Tiles start every 127
+// rows: a tile's 128th row only supplies P1 to its 127th, so tiles need no
+// data from one another and two sets of eight epilogue warps finish
+// alternate tiles concurrently (the epilogue, not the MMA, limits a tile).
+// Accumulators take 128 TMEM columns, four in a ring; tile c (a running count
+// over groups, layers and tiles) waits for the epilogue of tile c-3, which
+// drains its buffer (c-4) and finishes every input row it reads. Weight slot
+// dr holds one row offset's [Cin/8][3][64][8] block, which gk_net_t.conv_w
+// stores contiguously for 64 channels (one bulk copy); the N = 128 operand is
+// its rows 64..191 (dc = 0, +1), the N = 64 operand rows 0..63 (dc = -1).
+struct Cols64 {
+    static constexpr int C = 64, G = 5, T = 4, HALO = 11;
+    static constexpr int STRIDE = 127;            // rows between tile starts (T * 127 >= G * 100)
+    static constexpr int ROWS = G * 100 + 2 * HALO;
+    static constexpr int TAIL = (T - 1) * STRIDE + 128 - G * 100;
+    static constexpr int CHUNK = ROWS * 16;
+    static constexpr int ACT = (C / 8) * CHUNK;
+    static constexpr int NACC = 2 * C;            // 128 accumulator columns per tile
+    static constexpr int NBUF = 4;                // accumulators in the TMEM ring
+    static constexpr int BCHUNK = 3 * C * 16;     // 3072 B per 8-channel chunk of a slot
+    static constexpr int SLOT = (C / 8) * BCHUNK; // 24,576 B: one row offset's weights
+    static constexpr int NSLOT = 3;
+    static constexpr int SETS = 2;                // epilogue warp sets and MMA warps, alternate tiles
+    static constexpr int EPI_WARPS = 8 * SETS;    // per set: 4 lane quadrants x 2 channel halves
+    static constexpr int EPI0 = 1 + SETS;         // first epilogue warp (warp 0 loads weights)
+    static constexpr int THREADS = 32 * (EPI0 + EPI_WARPS);
+    // slot_full[3], slot_free[3], acc_full[4], acc_empty[4], xchg[2], input_ready, mma_idle, heads_ready, heads_done
+    static constexpr int NBARS = 2 * NSLOT + 2 * NBUF + SETS + 4;
+    static constexpr int HEADW = (3 * C + 3 + 3) / 4 * 4;
+    static constexpr int XFLOATS = SETS * 3 * 4 * 2 * 32;  // [set][3 tiles][4 quadrants][2 halves][32]
+    static constexpr int SMEM = 2 * ACT + NSLOT * SLOT + NBARS * 8 + 16 + HEADW * 4 + (XFLOATS + 32) * 4;
+    static constexpr uint32_t IDESC128 = tc::idesc_bf16(128, 2 * C);
+    static constexpr uint32_t IDESC64 = tc::idesc_bf16(128, C);
+    static_assert(NBUF * NACC <= 512, "accumulators fit in TMEM");
+    static_assert(T * STRIDE >= G * 100, "tiles cover the group");
+    static_assert(TAIL >= 0 && TAIL * 16 <= NSLOT * SLOT, "tail reads stay inside the allocation");
+    static_assert(SMEM <= 232448, "shared memory per CTA");
+};
+
+// Bias, residual, ReLU and padding mask of 16 channels (ch0..ch0+15) of one
+// output row, stored as bf16 when `store` is set and the row is inside the
+// group. Every lane runs the same code; rows past the group read in-bounds
+// neighbouring shared memory and are not stored.
+__device__ __forceinline__ void cols_finish16(uint8_t* out, int m, int ch0, const float* bias, float (&v)[16],
+                                              bool residual, int nimg, bool store) {
+    using K = Cols64;
+    const int img = m / 100, pos = m - img * 100, r = pos / 10, cc = pos - r * 10;
+    const bool valid = img < nimg && r < 9 && cc < 9;
+    const bool keep = store && m < K::G * 100;
+    uint8_t* const row = out + (K::HALO + m) * 16 + (ch0 / 8) * K::CHUNK;
+    uint4 res[2];
+    if (residual) {
+        res[0] = *reinterpret_cast<const uint4*>(row);
+        res[1] = *reinterpret_cast<const uint4*>(row + K::CHUNK);
+    }
+#pragma unroll
+    for (int j = 0; j < 16; ++j) {
+        float x = v[j] + bias[j];
+        if (residual) {
+            const uint4 rv = res[j >> 3];
+            const uint32_t w = (j & 7) < 2 ? rv.x : (j & 7) < 4 ? rv.y : (j & 7) < 6 ? rv.z : rv.w;
+            x += (j & 1) ? bf16_hi(w) : bf16_lo(w);
+        }
+        v[j] = valid ? fmaxf(x, 0.0f) : 0.0f;
+    }
+    if (keep) {
+#pragma unroll
+        for (int k = 0; k < 2; ++k) {
+            const uint4 o = make_uint4(pack_bf16x2(v[8 * k], v[8 * k + 1]), pack_bf16x2(v[8 * k + 2], v[8 * k + 3]),
+                                       pack_bf16x2(v[8 * k + 4], v[8 * k + 5]), pack_bf16x2(v[8 * k + 6], v[8 * k + 7]));
+            *reinterpret_cast<uint4*>(row + k * K::CHUNK) = o;
+        }
+    }
+}
+
+__global__ void __launch_bounds__(Cols64::THREADS, 1)
+    net_tower_cols_kernel(NetParams p, NetInput in, float* headfeat, uint32_t* status) {
+    using K = Cols64;
+    constexpr int C = K::C;
+    extern __shared__ __align__(1024) uint8_t smem[];
+    uint8_t* const bufP = smem;
+    uint8_t* const bufQ = smem + K::ACT;
+    uint8_t* const slots = smem + 2 * K::ACT;
+    uint64_t* const bars = reinterpret_cast<uint64_t*>(slots + K::NSLOT * K::SLOT);
+    uint32_t* const tmem_holder = reinterpret_cast<uint32_t*>(bars + K::NBARS);
+    float* const headw = reinterpret_cast<float*>(tmem_holder + 4);  // [3][C] then [3] biases
+    float* const xp1 = headw + K::HEADW;    // lane 0's P1 per set, tile, quadrant and half
+    float* const zero_row = xp1 + K::XFLOATS;  // zeros: the missing neighbour below quadrant 3
+    const uint32_t slot_full = tc::smem_u32(bars);
+    const uint32_t slot_free = slot_full + 8 * K::NSLOT;
+    const uint32_t acc_full = slot_free + 8 * K::NSLOT;
+    const uint32_t acc_empty = acc_full + 8 * K::NBUF;
+    const uint32_t xchg = acc_empty + 8 * K::NBUF;
+    const uint32_t input_ready = xchg + 8 * K::SETS;
+    const uint32_t mma_idle = input_ready + 8;
+    const uint32_t heads_ready = mma_idle + 8;
+    const uint32_t heads_done = heads_ready + 8;
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int NL = 1 + 2 * p.blocks;
+    const int count = input_count(in);
+    const int groups = (count + K::G - 1) / K::G;
+
+    for (int i = threadIdx.x; i < 2 * K::ACT / 16; i += blockDim.x)
+        reinterpret_cast<uint4*>(smem)[i] = make_uint4(0, 0, 0, 0);
+    for (int i = threadIdx.x; i < 3 * C; i += blockDim.x) headw[i] = p.head_w[i];
+    if (threadIdx.x < 3) headw[3 * C + threadIdx.x] = p.head_b[threadIdx.x];
+    if (threadIdx.x < 32) zero_row[threadIdx.x] = 0.0f;
+    tc::fence_proxy_async_smem();
+    if (threadIdx.x == 0) {
+        for (int b = 0; b < K::NBARS; ++b) {
+            const uint32_t bar = slot_full + 8 * b;
+            uint32_t n = 1u;                                           // producer / commit arrivals
+            if ((bar >= slot_free && bar < acc_full) || bar == mma_idle) n = (uint32_t)K::SETS;  // each MMA warp
+            if (bar >= acc_empty && bar < input_ready) n = 8u;         // one epilogue set
+            if (bar == input_ready || bar == heads_ready || bar == heads_done) n = (uint32_t)K::EPI_WARPS;
+            tc::mbar_init(bar, n);
+        }
+        tc::fence_mbar_init();
+    }
+    if (warp == 0) {
+        tc::tmem_alloc(tc::smem_u32(tmem_holder), 512);
+        tc::tmem_relinquish();
+    }
+    tc::tc_fence_before();
+    __syncthreads();
+    tc::tc_fence_after();
+    const uint32_t tmem = *tmem_holder;
+
+    if (warp == 0 && lane == 0) {
+        // ---------------- weight producer: slot dr <- row offset dr's [Cin/8][3][64][8] block ----------------
+        int u = 0;  // layers issued so far (each layer fills every slot once)
+        for (int g = blockIdx.x; g < groups; g += gridDim.x) {
+            for (int l = 0; l < NL; ++l, ++u) {
+                const int chunks = l == 0 ? 2 : C / 8;  // 8-channel input chunks (stem input padded to 16)
+                for (int dr = 0; dr < 3; ++dr) {
+                    if (u > 0 && !tc::mbar_wait(slot_free + 8 * dr, (uint32_t)(u - 1) & 1u, status)) goto done;
+                    const uint32_t bytes = (uint32_t)(chunks * K::BCHUNK);
+                    const uint8_t* src = l == 0 ? p.conv_w + dr * (2 * K::BCHUNK)
+                                                : p.conv_w + 6 * K::BCHUNK + ((size_t)(l - 1) * 3 + dr) * K::SLOT;
+                    tc::mbar_expect_tx(slot_full + 8 * dr, bytes);
+                    tc::bulk_g2s(tc::smem_u32(slots + dr * K::SLOT), src, bytes, slot_full + 8 * dr);
+                }
+            }
+        }
+    } else if (warp >= 1 && warp < K::EPI0) {
+        // ---------------- MMA warps: warp 1 + ms issues tiles c = ms, ms+2, ... ----------------
+        // Two issuers keep the tensor pipe fed: while one waits on its next
+        // tile's barriers (each a shared-memory round trip competing with
+        // the operand traffic), the other's MMAs run.
+        constexpr uint32_t kChunk16 = K::CHUNK / 16, kBChunk16 = K::BCHUNK / 16, kSlot16 = K::SLOT / 16;
+        constexpr uint32_t kRows64 = C;  // rows 64.. of a slot chunk, in 16-byte units
+        const uint64_t bdesc = tc::smem_desc(tc::smem_u32(slots), K::BCHUNK, 128);
+        const uint64_t adescP = tc::smem_desc(tc::smem_u32(bufP) + K::HALO * 16, K::CHUNK, 128);
+        const uint64_t adescQ = tc::smem_desc(tc::smem_u32(bufQ) + K::HALO * 16, K::CHUNK, 128);
+        const uint32_t a_hi = (uint32_t)(adescP >> 32), b_lo = (uint32_t)bdesc, b_hi = (uint32_t)(bdesc >> 32);
+        const bool leader = lane == 0;
+        const int ms = warp - 1;
+        int c = 0, u = 0, i = 0;
+        for (int g = blockIdx.x; g < groups; g += gridDim.x, ++i) {
+            for (int l = 0; l < NL; ++l, ++u) {
+                const uint32_t a_lo = (uint32_t)(l % 2 == 0 ? adescQ : adescP);
+                const int ks = l == 0 ? 1 : C / 16;
+                for (int t = 0; t < K::T; ++t, ++c) {
+                    if ((c & 1) != ms) continue;
+                    const bool first_use = t == ms;  // this warp's first tile of the layer waits for the weights
+                    const bool last_use = t + 2 >= K::T;  // and its last one releases them
+                    if (l == 0 && first_use && !warp_wait(input_ready, (uint32_t)i & 1u, status, leader))
+                        goto mma_drain;
+                    // The two epilogue sets finish tiles of opposite parity, so wait for
+                    // both tile c-4 (its buffer is this tile's) and tile c-3 (with c-5 of
+                    // the same set, the last of the input rows this tile reads).
+                    if (c >= 4 &&
+                        !warp_wait(acc_empty + 8 * (c % K::NBUF), (uint32_t)((c - 4) / K::NBUF) & 1u, status, leader))
+                        goto mma_drain;
+                    if (c >= 3 &&
+                        !warp_wait(acc_empty + 8 * ((c - 3) % K::NBUF), (uint32_t)((c - 3) / K::NBUF) & 1u, status, leader))
+                        goto mma_drain;
+                    const uint32_t d = tmem + (uint32_t)((c % K::NBUF) * K::NACC);
+#pragma unroll
+                    for (int dr = 0; dr < 3; ++dr) {
+                        if (first_use && !warp_wait(slot_full + 8 * dr, (uint32_t)u & 1u, status, leader)) goto mma_drain;
+                        const uint32_t a = a_lo + (uint32_t)(t * K::STRIDE + (dr - 1) * 10);
+                        const uint32_t b = b_lo + (uint32_t)dr * kSlot16;
+                        for (int s = 0; s < ks; ++s)  // dc = 0, +1 -> columns 0..127
+                            tc::mma_bf16_warp(d, a + 2 * s * kChunk16, a_hi, b + kRows64 + 2 * s * kBChunk16, b_hi,
+                                              K::IDESC128, (dr | s) != 0);
+                        for (int s = 0; s < ks; ++s)  // dc = -1 -> columns 0..63
+                            tc::mma_bf16_warp(d, a - 1 + 2 * s * kChunk16, a_hi, b + 2 * s * kBChunk16, b_hi,
+                                              K::IDESC64, 1u);
+                        if (last_use) tc::mma_commit_warp(slot_free + 8 * dr);
+                    }
+                    tc::mma_commit_warp(acc_full + 8 * (c % K::NBUF));
+                }
+            }
+        }
+    mma_drain:
+        __syncwarp();
+        tc::mma_commit_warp(mma_idle);
+        if (leader) tc::mbar_wait(mma_idle, 0, status);
+        __syncwarp();
+    } else if (warp >= K::EPI0) {
+        // ------- epilogue: set s takes tiles c = s, s+2, ...; warp -> (quadrant q, channel half h) -------
+        const int e = warp - K::EPI0;
+        const int s = e >> 3;
+        const int q = warp & 3;
+        const int h = (e & 7) >> 2;
+        const int ch0 = 32 * h;
+        const int etid = threadIdx.x - 32 * K::EPI0;
+        const uint32_t lane_base = (uint32_t)(q * 32) << 16;
+        const uint32_t xbar = xchg + 8 * s;
+        int c = 0, i = 0;
+        bool first = true;
+        for (int g = blockIdx.x; g < groups; g += gridDim.x, ++i) {
+            const int base_img = g * K::G;
+            const int nimg = count - base_img < K::G ? count - base_img : K::G;
+            if (first) {
+                for (int m = etid; m < K::G * 100; m += 32 * K::EPI_WARPS) build_input_row<C>(bufQ, m, base_img, nimg, in);
+                tc::fence_proxy_async_smem();
+                __syncwarp();
+                if (lane == 0) tc::mbar_arrive(input_ready);
+                first = false;
+            } else {
+                // The previous group's head pass (all warps) must have read buffer P.
+                if (!warp_wait(heads_done, (uint32_t)(i - 1) & 1u, status, lane == 0)) goto epi_exit;
+            }
+            for (int l = 0; l < NL; ++l) {
+                uint8_t* const out = l % 2 == 0 ? bufP : bufQ;
+                const bool residual = l >= 2 && l % 2 == 0;
+                float bias[32];
+#pragma unroll
+                for (int j = 0; j < 32; ++j) bias[j] = __ldg(p.conv_b + l * C + ch0 + j);
+                for (int t = 0; t < K::T; ++t, ++c) {
+                    if ((c & 1) != s) continue;
+                    const int b = c % K::NBUF, k = c >> 1;  // k: this set's tile count
+                    const int x = k % 3;
+                    if (!warp_wait(acc_full + 8 * b, (uint32_t)(c / K::NBUF) & 1u, status, lane == 0)) goto epi_exit;
+                    tc::tc_fence_after();
+                    const uint32_t taddr = tmem + lane_base + (uint32_t)(b * K::NACC + ch0);
+                    {
+                        // Publish lane 0's P1 (the last row of the quadrant above needs it).
+                        float pub[32];
+                        tc::tmem_ld32(taddr + C, pub);
+                        if (lane == 0) {
+                            float4* const w = reinterpret_cast<float4*>(xp1 + (((s * 3 + x) * 4 + q) * 2 + h) * 32);
+#pragma unroll
+                            for (int j = 0; j < 8; ++j)
+                                w[j] = make_float4(pub[4 * j], pub[4 * j + 1], pub[4 * j + 2], pub[4 * j + 3]);
+                        }
+                    }
+                    __syncwarp();
+                    if (lane == 0) tc::mbar_arrive(xbar);
+                    if (!warp_wait(xbar, (uint32_t)k & 1u, status, lane == 0)) goto epi_exit;
+                    const float* const nbr = q < 3 ? xp1 + (((s * 3 + x) * 4 + q + 1) * 2 + h) * 32 : zero_row;
+                    const int m = t * K::STRIDE + q * 32 + lane;
+                    const bool own = !(q == 3 && lane == 31);  // row 127 belongs to the next tile
+#pragma unroll
+                    for (int pass = 0; pass < 2; ++pass) {
+                        float p0[16], p1[16];
+                        tc::tmem_ld16x2(taddr + 16 * pass, taddr + C + 16 * pass, p0, p1);
+#pragma unroll
+                        for (int j = 0; j < 16; ++j) {
+                            const float dn = __shfl_down_sync(0xffffffffu, p1[j], 1);
+                            const float nx = nbr[16 * pass + j];
+                            p0[j] += lane == 31 ? nx : dn;
+                        }
+                        cols_finish16(out, m, ch0 + 16 * pass, bias + 16 * pass, p0, residual, nimg, own);
+                    }
+                    tc::tc_fence_before();
+                    tc::fence_proxy_async_smem();
+                    __syncwarp();
+                    if (lane == 0) tc::mbar_arrive(acc_empty + 8 * b);
+                }
+            }
+            // Build the next group's stem input (buffer Q) before the head pass,
+            // so its MMAs can start, once the group's last MMAs (which read Q)
+            // are complete: the last tile of each MMA warp.
+            {
+                const int gn = g + gridDim.x;
+                if (gn < groups) {
+                    for (int cl = c - 2; cl < c; ++cl)  // the last tile of each MMA warp
+                        if (!warp_wait(acc_full + 8 * (cl % K::NBUF), (uint32_t)(cl / K::NBUF) & 1u, status, lane == 0))
+                            goto epi_exit;
+                    const int nb = gn * K::G;
+                    const int nn = count - nb < K::G ? count - nb : K::G;
+                    for (int mm = etid; mm < K::G * 100; mm += 32 * K::EPI_WARPS) build_input_row<C>(bufQ, mm, nb, nn, in);
+                    tc::fence_proxy_async_smem();
+                    __syncwarp();
+                    if (lane == 0) tc::mbar_arrive(input_ready);
+                }
+            }
+            __syncwarp();
+            if (lane == 0) tc::mbar_arrive(heads_ready);
+            if (!warp_wait(heads_ready, (uint32_t)i & 1u, status, lane == 0)) goto epi_exit;
+            for (int mm = etid; mm < K::G * 100; mm += 32 * K::EPI_WARPS) {
+                const int img = mm / 100, pos = mm - img * 100, r = pos / 10, cc = pos - r * 10;
+                if (!(img < nimg && r < 9 && cc < 9)) continue;
+                const uint8_t* row = bufP + (K::HALO + mm) * 16;
+                float h0 = headw[3 * C], h1 = headw[3 * C + 1], h2 = headw[3 * C + 2];
+#pragma unroll 4
+                for (int kk = 0; kk < C / 8; ++kk) {
+                    const uint4 rv = *reinterpret_cast<const uint4*>(row + kk * K::CHUNK);
+                    const uint32_t w[4] = {rv.x, rv.y, rv.z, rv.w};
+#pragma unroll
+                    for (int j = 0; j < 8; ++j) {
+                        const float xv = (j & 1) ? bf16_hi(w[j >> 1]) : bf16_lo(w[j >> 1]);
+                        const int ch = kk * 8 + j;
+                        h0 = fmaf(xv, headw[ch], h0);
+                        h1 = fmaf(xv, headw[C + ch], h1);
+                        h2 = fmaf(xv, headw[2 * C + ch], h2);
+                    }
+                }
+                float* hf = headfeat + (int64_t)(base_img + img) * 243 + r * 9 + cc;
+                hf[0] = fmaxf(h0, 0.0f);
+                hf[81] = fmaxf(h1, 0.0f);
+                hf[162] = fmaxf(h2, 0.0f);
+            }
+            __syncwarp();
+            if (lane == 0) tc::mbar_arrive(heads_done);
+        }
+    epi_exit:;
+    }
+done:
+    tc::tc_fence_before();
+    __syncthreads();
+    if (warp == 0) {
+        tc::tc_fence_after();
+        tc::tmem_dealloc(tmem, 512);
+    }
+}
+
+int launch_tower_cols(const NetParams& p, const NetInput& in, float* headfeat, uint32_t* status,
+                      cudaStream_t stream) {
+    using K = Cols64;
+    static bool done[64] = {};
+    if (!once_per_device(done, [] {
+            return cudaFuncSetAttribute(net_tower_cols_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, K::SMEM) ==
+                   cudaSuccess;
+        }))
+        return launch_status();
+    const int64_t groups = (in.n + K::G - 1) / K::G;
+    const int grid = (int)(groups < kSmCount ? groups : kSmCount);
+    net_tower_cols_kernel<<<grid < 1 ? 1 : grid, K::THREADS, K::SMEM, stream>>>(p, in, headfeat, status);
+    return launch_status();
 }
 
 // ---- fully connected heads -------------------------------------------------------
@@ -694,7 +1051,7 @@ int run_forward(const gk_net_t* net, const NetInput& in, float* headfeat, const 
                 cudaStream_t stream, cudaEvent_t tower_start = nullptr, cudaEvent_t tower_stop = nullptr) {
     const NetParams p = make_params(net);
     if (tower_start) cudaEventRecord(tower_start, stream);
-    const int s = net->channels == 64 ? launch_tower<64>(p, in, headfeat, status, stream)
+    const int s = net->channels == 64 ? launch_tower_cols(p, in, headfeat, status, stream)
                                       : launch_tower<128>(p, in, headfeat, status, stream);
     if (tower_stop) cudaEventRecord(tower_stop, stream);
     if (s) return s;

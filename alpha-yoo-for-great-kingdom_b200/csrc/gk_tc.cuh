@@ -200,5 +200,100 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
     for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
 }
 
+
+// Three 32x32b.x32 loads (e.g. three column blocks of one accumulator) under a
+// single wait. Empty asm statements after the wait pin the first two
+// destination sets behind it, as the wait names only the third.
+__device__ __forceinline__ void tmem_ld32_issue(uint32_t taddr, uint32_t (&r)[32]) {
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+        : "r"(taddr)
+        : "memory");
+}
+__device__ __forceinline__ void tmem_pin32(uint32_t (&r)[32]) {
+    asm volatile("" : "+r"(r[0]), "+r"(r[1]), "+r"(r[2]), "+r"(r[3]), "+r"(r[4]), "+r"(r[5]), "+r"(r[6]), "+r"(r[7]), "+r"(r[8]), "+r"(r[9]), "+r"(r[10]), "+r"(r[11]), "+r"(r[12]), "+r"(r[13]), "+r"(r[14]), "+r"(r[15]), "+r"(r[16]), "+r"(r[17]), "+r"(r[18]), "+r"(r[19]), "+r"(r[20]), "+r"(r[21]), "+r"(r[22]), "+r"(r[23]), "+r"(r[24]), "+r"(r[25]), "+r"(r[26]), "+r"(r[27]), "+r"(r[28]), "+r"(r[29]), "+r"(r[30]), "+r"(r[31]) : : "memory");
+}
+__device__ __forceinline__ void tmem_ld32x3(uint32_t a0, uint32_t a1, uint32_t a2, float (&v0)[32], float (&v1)[32],
+                                            float (&v2)[32]) {
+    uint32_t r0[32], r1[32], r2[32];
+    tmem_ld32_issue(a0, r0);
+    tmem_ld32_issue(a1, r1);
+    tmem_ld32_issue(a2, r2);
+    {
+        uint32_t (&r)[32] = r2;
+        asm volatile("tcgen05.wait::ld.sync.aligned;" : "+r"(r[0]), "+r"(r[1]), "+r"(r[2]), "+r"(r[3]), "+r"(r[4]), "+r"(r[5]), "+r"(r[6]), "+r"(r[7]), "+r"(r[8]), "+r"(r[9]), "+r"(r[10]), "+r"(r[11]), "+r"(r[12]), "+r"(r[13]), "+r"(r[14]), "+r"(r[15]), "+r"(r[16]), "+r"(r[17]), "+r"(r[18]), "+r"(r[19]), "+r"(r[20]), "+r"(r[21]), "+r"(r[22]), "+r"(r[23]), "+r"(r[24]), "+r"(r[25]), "+r"(r[26]), "+r"(r[27]), "+r"(r[28]), "+r"(r[29]), "+r"(r[30]), "+r"(r[31]) : : "memory");
+    }
+    tmem_pin32(r0);
+    tmem_pin32(r1);
+#pragma unroll
+    for (int i = 0; i < 32; ++i) {
+        v0[i] = __uint_as_float(r0[i]);
+        v1[i] = __uint_as_float(r1[i]);
+        v2[i] = __uint_as_float(r2[i]);
+    }
+}
+
+// The same for 16 columns per load (32x32b.x16).
+__device__ __forceinline__ void tmem_ld16_issue(uint32_t taddr, uint32_t (&r)[16]) {
+    asm volatile("tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];" : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]) : "r"(taddr) : "memory");
+}
+__device__ __forceinline__ void tmem_pin16(uint32_t (&r)[16]) {
+    asm volatile("" : "+r"(r[0]), "+r"(r[1]), "+r"(r[2]), "+r"(r[3]), "+r"(r[4]), "+r"(r[5]), "+r"(r[6]), "+r"(r[7]), "+r"(r[8]), "+r"(r[9]), "+r"(r[10]), "+r"(r[11]), "+r"(r[12]), "+r"(r[13]), "+r"(r[14]), "+r"(r[15]) : : "memory");
+}
+__device__ __forceinline__ void tmem_ld16x3(uint32_t a0, uint32_t a1, uint32_t a2, float (&v0)[16], float (&v1)[16],
+                                            float (&v2)[16]) {
+    uint32_t r0[16], r1[16], r2[16];
+    tmem_ld16_issue(a0, r0);
+    tmem_ld16_issue(a1, r1);
+    tmem_ld16_issue(a2, r2);
+    {
+        uint32_t (&r)[16] = r2;
+        asm volatile("tcgen05.wait::ld.sync.aligned;" : "+r"(r[0]), "+r"(r[1]), "+r"(r[2]), "+r"(r[3]), "+r"(r[4]), "+r"(r[5]), "+r"(r[6]), "+r"(r[7]), "+r"(r[8]), "+r"(r[9]), "+r"(r[10]), "+r"(r[11]), "+r"(r[12]), "+r"(r[13]), "+r"(r[14]), "+r"(r[15]) : : "memory");
+    }
+    tmem_pin16(r0);
+    tmem_pin16(r1);
+#pragma unroll
+    for (int i = 0; i < 16; ++i) {
+        v0[i] = __uint_as_float(r0[i]);
+        v1[i] = __uint_as_float(r1[i]);
+        v2[i] = __uint_as_float(r2[i]);
+    }
+}
+
+// Two 32x32b.x32 loads under a single wait.
+__device__ __forceinline__ void tmem_ld32x2(uint32_t a0, uint32_t a1, float (&v0)[32], float (&v1)[32]) {
+    uint32_t r0[32], r1[32];
+    tmem_ld32_issue(a0, r0);
+    tmem_ld32_issue(a1, r1);
+    {
+        uint32_t (&r)[32] = r1;
+        asm volatile("tcgen05.wait::ld.sync.aligned;" : "+r"(r[0]), "+r"(r[1]), "+r"(r[2]), "+r"(r[3]), "+r"(r[4]), "+r"(r[5]), "+r"(r[6]), "+r"(r[7]), "+r"(r[8]), "+r"(r[9]), "+r"(r[10]), "+r"(r[11]), "+r"(r[12]), "+r"(r[13]), "+r"(r[14]), "+r"(r[15]), "+r"(r[16]), "+r"(r[17]), "+r"(r[18]), "+r"(r[19]), "+r"(r[20]), "+r"(r[21]), "+r"(r[22]), "+r"(r[23]), "+r"(r[24]), "+r"(r[25]), "+r"(r[26]), "+r"(r[27]), "+r"(r[28]), "+r"(r[29]), "+r"(r[30]), "+r"(r[31]) : : "memory");
+    }
+    tmem_pin32(r0);
+#pragma unroll
+    for (int i = 0; i < 32; ++i) {
+        v0[i] = __uint_as_float(r0[i]);
+        v1[i] = __uint_as_float(r1[i]);
+    }
+}
+
+// Two 32x32b.x16 loads under a single wait.
+__device__ __forceinline__ void tmem_ld16x2(uint32_t a0, uint32_t a1, float (&v0)[16], float (&v1)[16]) {
+    uint32_t r0[16], r1[16];
+    tmem_ld16_issue(a0, r0);
+    tmem_ld16_issue(a1, r1);
+    {
+        uint32_t (&r)[16] = r1;
+        asm volatile("tcgen05.wait::ld.sync.aligned;" : "+r"(r[0]), "+r"(r[1]), "+r"(r[2]), "+r"(r[3]), "+r"(r[4]), "+r"(r[5]), "+r"(r[6]), "+r"(r[7]), "+r"(r[8]), "+r"(r[9]), "+r"(r[10]), "+r"(r[11]), "+r"(r[12]), "+r"(r[13]), "+r"(r[14]), "+r"(r[15]) : : "memory");
+    }
+    tmem_pin16(r0);
+#pragma unroll
+    for (int i = 0; i < 16; ++i) {
+        v0[i] = __uint_as_float(r0[i]);
+        v1[i] = __uint_as_float(r1[i]);
+    }
+}
+
 }  // namespace tc
 }  // namespace gk

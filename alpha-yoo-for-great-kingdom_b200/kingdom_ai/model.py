@@ -127,11 +127,20 @@ def fold(conv: nn.Conv2d, bn: nn.BatchNorm2d):
 # Native (sm_100a) network
 # ---------------------------------------------------------------------------
 
-def _pack_conv(weight: torch.Tensor, cin_pad: int) -> torch.Tensor:
-    """[Cout][Cin][3][3] fp32 -> per tap (row-major over (dr, dc)) bf16 [Cin/8][Cout][8]."""
+def _pack_conv(weight: torch.Tensor, cin_pad: int, column_fused: bool) -> torch.Tensor:
+    """[Cout][Cin][3][3] fp32 -> the bf16 operand layout of the native tower.
+
+    Per tap (row-major over (dr, dc)) [Cin/8][Cout][8] for 128 channels; for 64
+    channels, per row offset dr [Cin/8][3 (dc)][Cout][8], i.e. the three column
+    taps of a row offset side by side, which the tower reads as one 192-column
+    operand (include/gk.h, gk_net_t).
+    """
     cout, cin = weight.shape[:2]
     w = torch.zeros((cout, cin_pad, 3, 3), dtype=torch.float32)
     w[:, :cin] = weight
+    if column_fused:
+        rows = w.permute(2, 1, 3, 0).reshape(3, cin_pad // 8, 8, 3, cout)  # [dr][k/8][k%8][dc][n]
+        return rows.permute(0, 1, 3, 4, 2).contiguous().to(torch.bfloat16)  # [dr][k/8][dc][n][k%8]
     taps = w.permute(2, 3, 1, 0).reshape(9, cin_pad, cout)          # [tap][k][n]
     taps = taps.reshape(9, cin_pad // 8, 8, cout).permute(0, 1, 3, 2)  # [tap][k/8][n][k%8]
     return taps.contiguous().to(torch.bfloat16)
@@ -159,7 +168,9 @@ class NativePolicyValueNet:
             for block in model.blocks:
                 convs.append(fold(block.conv1, block.bn1))
                 convs.append(fold(block.conv2, block.bn2))
-            packed = [_pack_conv(convs[0][0].cpu(), 16)] + [_pack_conv(w.cpu(), self.channels) for w, _ in convs[1:]]
+            fused = self.channels == 64
+            packed = [_pack_conv(convs[0][0].cpu(), 16, fused)] + [_pack_conv(w.cpu(), self.channels, fused)
+                                                                    for w, _ in convs[1:]]
             conv_w = torch.cat([p.reshape(-1) for p in packed])
             pw, pb = fold(model.policy_conv, model.policy_bn)
             vw, vb = fold(model.value_conv, model.value_bn)

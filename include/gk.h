@@ -206,9 +206,11 @@ GK_API int gk_puct_search_hash_noalloc(int64_t batch, int simulations, const uin
 /* -------------------------------------------------------------- network */
 
 /* Device pointers of a packed policy/value network (BN folded). Layout of
- * conv_w: for each 3x3 layer (stem first, then two per residual block), for
- * each of the 9 taps (row-major over (dr, dc)), bf16 [Cin/8][Cout][8]; the
- * stem's Cin is padded from 10 to 16. conv_b: fp32 [layers][C]. head_w/head_b:
+ * conv_w, for each 3x3 layer (stem first, then two per residual block), the
+ * stem's Cin padded from 10 to 16: with 128 channels, for each of the 9 taps
+ * (row-major over (dr, dc)), bf16 [Cin/8][Cout][8]; with 64 channels, for each
+ * row offset dr (-1, 0, 1), bf16 [Cin/8][3 (dc = -1, 0, 1)][Cout][8], the
+ * three column taps side by side. conv_b: fp32 [layers][C]. head_w/head_b:
  * the 1x1 policy (2 rows) and value (1 row) convolutions. The rest are the
  * fully connected heads of python/kingdom_ai/model.py:51-69 (value hidden 64). */
 typedef struct {
