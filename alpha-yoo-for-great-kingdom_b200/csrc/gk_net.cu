@@ -815,7 +815,8 @@ struct HeadOut {
 
 constexpr int kPolStride = 163;  // odd row stride: conflict-free lane-per-row reads
 constexpr int kValStride = 81;
-constexpr size_t kHeadSmem = (size_t)(82 * kPolStride + 64 * kValStride + 8 * 244) * sizeof(float);
+constexpr int kHeadWarps = 16;  // two 16-warp blocks per SM keep 32 warps in flight
+constexpr size_t kHeadSmem = (size_t)(82 * kPolStride + 64 * kValStride + kHeadWarps * 244) * sizeof(float);
 
 // Copies an N-float row-major matrix of COLS columns into shared memory with
 // row stride STRIDE. Each thread issues a batch of independent read-only
@@ -840,7 +841,8 @@ __device__ __forceinline__ void stage_matrix(float* dst, const float* src) {
     }
 }
 
-__global__ void __launch_bounds__(256) net_heads_kernel(NetParams p, const float* headfeat, NetInput in, HeadOut out) {
+__global__ void __launch_bounds__(32 * kHeadWarps) net_heads_kernel(NetParams p, const float* headfeat, NetInput in,
+                                                               HeadOut out) {
     extern __shared__ float hs[];
     float* wp = hs;
     float* w1 = wp + 82 * kPolStride;
@@ -858,7 +860,7 @@ __global__ void __launch_bounds__(256) net_heads_kernel(NetParams p, const float
     const float* wc = wp + (lane + 64 < GK_ACTIONS ? lane + 64 : GK_ACTIONS - 1) * kPolStride;
     const float* va = w1 + lane * kValStride;
     const float* vb = w1 + (lane + 32) * kValStride;
-    for (int img = blockIdx.x * 8 + warp; img < count; img += gridDim.x * 8) {
+    for (int img = blockIdx.x * kHeadWarps + warp; img < count; img += gridDim.x * kHeadWarps) {
         const float* hf = headfeat + (int64_t)img * 243;
         float fv[8];
 #pragma unroll
@@ -1035,9 +1037,9 @@ int launch_heads(const NetParams& p, const float* headfeat, const NetInput& in, 
                                         (int)kHeadSmem) == cudaSuccess;
         }))
         return launch_status();
-    int64_t blocks = (in.n + 7) / 8;
+    int64_t blocks = (in.n + kHeadWarps - 1) / kHeadWarps;
     if (blocks > 2 * kSmCount) blocks = 2 * kSmCount;
-    net_heads_kernel<<<(int)(blocks < 1 ? 1 : blocks), 256, kHeadSmem, stream>>>(p, headfeat, in, out);
+    net_heads_kernel<<<(int)(blocks < 1 ? 1 : blocks), 32 * kHeadWarps, kHeadSmem, stream>>>(p, headfeat, in, out);
     return launch_status();
 }
 

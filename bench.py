@@ -40,10 +40,10 @@ CHANNELS, BLOCKS = 64, 6
 TOWER_FLOPS_PER_EVAL = (2 * 81 * 9 * 10 * CHANNELS + 2 * BLOCKS * 2 * 81 * 9 * CHANNELS * CHANNELS
                         + 2 * 81 * CHANNELS * 3)  # 72.63 MFLOP
 # DRAM bytes of one tower launch (dram__bytes_read.sum + dram__bytes_write.sum)
-# from an ncu capture of net_tower_kernel<64> on 4096 positions: the bf16
+# from an ncu capture of net_tower_cols_kernel on 4096 positions: the bf16
 # weights streamed once per image group plus the packed input states;
 # activations never leave shared memory and the head features stay in L2.
-TOWER_DRAM_BYTES_PER_LAUNCH = 1_286_912
+TOWER_DRAM_BYTES_PER_LAUNCH = 1_257_216
 # Kernel launches per ply: begin, noise, finish, advance; (compact, tower,
 # heads, expand/backup) per evaluation; select per simulation.
 LAUNCHES_PER_PLY = 4 + 4 * (SIMULATIONS + 1) + SIMULATIONS
@@ -377,7 +377,7 @@ def main():
                                    "plies then best, 1M-row replay FIFO",
                        "lanes_per_gpu": LANES, "simulations": SIMULATIONS, "parallelism": f"games sharded x{world}",
                        "l2": "working set (search trees 3.2 GB/GPU) far larger than L2"},
-            "roofline": {"bound": "tensor", "kernel": "net_tower_kernel<64>",
+            "roofline": {"bound": "tensor", "kernel": "net_tower_cols_kernel",
                          "achieved": tflops, "peak": peak_tf, "unit": "TFLOP/s",
                          "frac": (tflops / peak_tf) if tflops else None, "traffic": TOWER_DRAM_BYTES_PER_LAUNCH,
                          "peak_kind": f"{peak_kind} bf16 sustained",
