@@ -158,6 +158,69 @@ __device__ __forceinline__ void claim_territory(gk_bits& s) {
     gk_put(&s, GK_PLANE_OWN_WHITE, gk_or(ow, gk_and(pw, unowned)));
 }
 
+__device__ __forceinline__ bool touches_four_edges(gk_b96 x) {
+    return (x.w[0] & GK_ROW0_0) && (x.w[2] & GK_ROW8_2) &&
+           ((x.w[0] & GK_COL0_0) | (x.w[1] & GK_COL0_1) | (x.w[2] & GK_COL0_2)) &&
+           ((x.w[0] & GK_COL8_0) | (x.w[1] & GK_COL8_1) | (x.w[2] & GK_COL8_2));
+}
+
+// The same claim after a placement of `mover` at `here`, for a state whose
+// territory was settled before the move (GK_META_SETTLED: every qualifying
+// empty component already owned). No stone is removed by a non-final move,
+// so an empty component that does not touch `here` keeps its neighbours and
+// its edges, qualifies exactly as before and is already owned. Only the
+// pieces of the component the stone split are examined: each touches the
+// mover's new stone, so it is territory of the mover unless it reaches a cell
+// next to an enemy stone (the flood stops there) or touches all four edges.
+// `E` is the empty set after the move.
+__device__ __forceinline__ void claim_around(gk_bits& s, gk_b96 here, gk_b96 E, gk_b96 enemy, int mover) {
+    const gk_b96 enemy_adj = gk_and(E, gk_neighbours(enemy));
+    const gk_b96 mr = rev96(E);
+    gk_b96 pending = gk_and(gk_neighbours(here), E);
+    gk_b96 gained = gk_b(0u, 0u, 0u);
+    while (gk_any(pending)) {
+        gk_b96 x = run_fill(E, mr, lowest_bit(pending));
+        bool dead = gk_any(gk_and(x, enemy_adj));
+        while (!dead) {
+            const gk_b96 fresh = gk_andnot(gk_and(gk_or(gk_shl(x, 10), gk_shr(x, 10)), E), x);
+            if (!gk_any(fresh)) break;
+            x = gk_or(x, run_fill(E, mr, fresh));
+            dead = gk_any(gk_and(x, enemy_adj));
+        }
+        // A dead flood may stop short of other seeds of its component; they
+        // are flooded again and die the same way.
+        pending = gk_andnot(pending, x);
+        if (!dead && !touches_four_edges(x)) gained = gk_or(gained, x);
+    }
+    if (!gk_any(gained)) return;
+    const gk_b96 ob = gk_get(&s, GK_PLANE_OWN_BLACK), ow = gk_get(&s, GK_PLANE_OWN_WHITE);
+    const gk_b96 unowned = gk_andnot(gk_valid(), gk_or(ob, ow));
+    if (mover == 1) gk_put(&s, GK_PLANE_OWN_BLACK, gk_or(ob, gk_and(gained, unowned)));
+    else gk_put(&s, GK_PLANE_OWN_WHITE, gk_or(ow, gk_and(gained, unowned)));
+}
+
+// True when the group of `mask` holding `seed` has a cell next to `libs`.
+// `group` receives the cells flooded before the answer was known: the whole
+// group when it has no liberty, possibly part of it otherwise.
+__device__ __forceinline__ bool group_has_liberty(gk_b96 mask, gk_b96 libs, gk_b96 seed, gk_b96& group) {
+    gk_b96 x = seed;
+    for (;;) {
+        // Shifted bits that leave the board land in the zero padding column or
+        // above bit 88, outside both `libs` and `mask`.
+        const gk_b96 d = gk_or(x, gk_or(gk_or(gk_shl(x, 1), gk_shr(x, 1)), gk_or(gk_shl(x, 10), gk_shr(x, 10))));
+        if (gk_any(gk_and(d, libs))) {
+            group = x;
+            return true;
+        }
+        const gk_b96 y = gk_and(d, mask);
+        if (gk_eq(x, y)) {
+            group = x;
+            return false;
+        }
+        x = y;
+    }
+}
+
 // One transition; returns false (state unchanged) for rejected actions.
 __device__ __forceinline__ bool play(gk_bits& s, int action) {
     const uint32_t meta = s.w[15];
@@ -198,15 +261,16 @@ __device__ __forceinline__ bool play(gk_bits& s, int action) {
     gk_b96 captured = gk_b(0u, 0u, 0u);
     gk_b96 pending = gk_and(gk_neighbours(here), opp);
     while (gk_any(pending)) {
-        const gk_b96 group = gk_flood(opp, lowest_bit(pending));
+        gk_b96 group;
+        const bool alive = group_has_liberty(opp, E, lowest_bit(pending), group);
         pending = gk_andnot(pending, group);
-        if (!gk_any(gk_and(gk_neighbours(group), E))) captured = gk_or(captured, group);
+        if (!alive) captured = gk_or(captured, group);
     }
     const int captured_count = gk_popc(captured);
     bool suicide = false;
     if (captured_count == 0) {
-        const gk_b96 group = gk_flood(own, here);
-        suicide = !gk_any(gk_and(gk_neighbours(group), E));
+        gk_b96 group;
+        suicide = !group_has_liberty(own, E, here, group);
     }
     if (actor == 1) --bstock;
     else --wstock;
@@ -224,7 +288,11 @@ __device__ __forceinline__ bool play(gk_bits& s, int action) {
         captured_field = 0;
     }
     s.w[15] = gk_pack_meta(enemy, bstock, wstock, 0, reason, winner, captured_field) | (meta & 0xf8000000u);
-    if (reason == GK_NONE) claim_territory(s);
+    if (reason == GK_NONE) {
+        if (meta & GK_META_SETTLED) claim_around(s, here, E, opp, actor);
+        else claim_territory(s);
+        s.w[15] |= GK_META_SETTLED;
+    }
     return true;
 }
 
@@ -233,7 +301,8 @@ __device__ __forceinline__ gk_bits initial_bits(int neutral_cell) {
 #pragma unroll
     for (int i = 0; i < 16; ++i) s.w[i] = 0u;
     if (neutral_cell >= 0 && neutral_cell < GK_CELLS) gk_put(&s, GK_PLANE_NEUTRAL, gk_single(gk_cell_bit(neutral_cell)));
-    s.w[15] = gk_pack_meta(1, GK_STONES, GK_STONES, 0, GK_NONE, 0, 0);
+    // No black or white stone: no territory, so the state is settled.
+    s.w[15] = gk_pack_meta(1, GK_STONES, GK_STONES, 0, GK_NONE, 0, 0) | GK_META_SETTLED;
     return s;
 }
 

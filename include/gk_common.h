@@ -89,6 +89,13 @@ typedef struct {
 #define GK_META_REASON_SHIFT 16   /* 2 bits: wire reason code */
 #define GK_META_WINNER_SHIFT 18   /* 2 bits: 0, 1, 2 */
 #define GK_META_CAPTURED_SHIFT 20 /* 7 bits: 0..81 */
+/* Bit 27: territory settled. Set only by the device transitions (initial state
+ * and every placement, which run the territory claim) and meaning that every
+ * empty component that qualifies as territory is already owned; states packed
+ * from wire records have it clear, and their next placement runs the full
+ * claim over the whole board. A state settled this way needs only the
+ * component the new stone splits to be re-examined. Bits 28..31 are zero. */
+#define GK_META_SETTLED (1u << 27)
 
 #define GK_VALID0 0xdff7fdffu
 #define GK_VALID1 0xf7fdff7fu

@@ -209,3 +209,42 @@ def test_generated_positions_and_encodings_full_size(kai, oracle, golden):
     batch = kai.GpuStateBatch.from_records(exp)
     f2, m2 = batch.encode()
     assert torch.equal(f2, f) and torch.equal(m2, m)
+
+
+def test_settled_and_unsettled_packed_states_play_alike(kai, oracle):
+    """Packed states carry a territory-settled flag (meta bit 27) that lets a
+    placement re-examine only the empty component it splits. States packed
+    from records have it clear and run the full claim; states whose owned
+    territory was stripped (unclaimed territory far from the next move) must
+    be claimed in full too. Every variant is played for several plies against
+    the oracle."""
+    from kingdom_ai import _native as native
+    from kingdom_ai.gpu_rules import bits_to_records, records_to_bits
+
+    n = 4096
+    settled = torch.empty((n, 16), dtype=torch.int32, device="cuda")
+    native.call("gk_gen_positions", 99, 0, n, native.ptr(settled), native.stream_of(settled.device))
+    assert bool(((settled[:, 15] >> 27) & 1).all())
+    recs = bits_to_records(settled).cpu().numpy()
+    stripped = recs.copy()
+    stripped[:, 81:162] = 0
+    variants = [(settled, recs.copy()), (records_to_bits(torch.from_numpy(recs).cuda()), recs.copy()),
+                (records_to_bits(torch.from_numpy(stripped).cuda()), stripped.copy())]
+    assert not bool(((variants[1][0][:, 15] >> 27) & 1).any())
+    rng = np.random.default_rng(5)
+    for ply in range(12):
+        base = variants[0][1]
+        acts = np.full(n, 81, dtype=np.int32)
+        for i in range(n):
+            cand = [a for a in range(81) if base[i, a] == 0]
+            if cand:
+                acts[i] = rng.choice(cand)
+        a = torch.from_numpy(acts).cuda()
+        for k, (bits, exp) in enumerate(variants):
+            accepted = torch.empty(n, dtype=torch.bool, device="cuda")
+            native.call("gk_play_bits", native.ptr(bits), native.ptr(a), 4, native.ptr(accepted), n,
+                        native.stream_of(bits.device))
+            exp2, exp_acc = oracle.play(exp, acts)
+            assert np.array_equal(accepted.cpu().numpy(), exp_acc.astype(bool)), (ply, k)
+            assert np.array_equal(bits_to_records(bits).cpu().numpy()[:, :169], exp2[:, :169]), (ply, k)
+            variants[k] = (bits, exp2)
