@@ -164,61 +164,54 @@ __device__ __forceinline__ bool touches_four_edges(gk_b96 x) {
            ((x.w[0] & GK_COL8_0) | (x.w[1] & GK_COL8_1) | (x.w[2] & GK_COL8_2));
 }
 
-// The same claim after a placement of `mover` at `here`, for a state whose
-// territory was settled before the move (GK_META_SETTLED: every qualifying
-// empty component already owned). No stone is removed by a non-final move,
-// so an empty component that does not touch `here` keeps its neighbours and
-// its edges, qualifies exactly as before and is already owned. Only the
-// pieces of the component the stone split are examined: each touches the
-// mover's new stone, so it is territory of the mover unless it reaches a cell
-// next to an enemy stone (the flood stops there) or touches all four edges.
-// `E` is the empty set after the move.
-__device__ __forceinline__ void claim_around(gk_bits& s, gk_b96 here, gk_b96 E, gk_b96 enemy, int mover) {
-    const gk_b96 enemy_adj = gk_and(E, gk_neighbours(enemy));
-    const gk_b96 mr = rev96(E);
-    gk_b96 pending = gk_and(gk_neighbours(here), E);
-    gk_b96 gained = gk_b(0u, 0u, 0u);
-    while (gk_any(pending)) {
-        gk_b96 x = run_fill(E, mr, lowest_bit(pending));
-        bool dead = gk_any(gk_and(x, enemy_adj));
-        while (!dead) {
-            const gk_b96 fresh = gk_andnot(gk_and(gk_or(gk_shl(x, 10), gk_shr(x, 10)), E), x);
-            if (!gk_any(fresh)) break;
-            x = gk_or(x, run_fill(E, mr, fresh));
-            dead = gk_any(gk_and(x, enemy_adj));
+// Union of the components of `m` that hold a cell of `seeds` and no cell of
+// `hit` (with kEdges, and that do not touch all four edges). Each component
+// grows one run closure and one vertical step at a time and is abandoned at
+// its first `hit` cell; a seed on a `hit` cell settles its component at once.
+// One loop runs over the steps of all components, so a thread's flood steps
+// are not nested per component and the threads of a warp stay together.
+template <bool kEdges>
+__device__ __forceinline__ gk_b96 closed_components(gk_b96 m, gk_b96 hit, gk_b96 seeds) {
+    gk_b96 result = gk_b(0u, 0u, 0u);
+    seeds = gk_andnot(seeds, hit);
+    if (!gk_any(seeds)) return result;
+    const gk_b96 mr = rev96(m);
+    gk_b96 x = gk_b(0u, 0u, 0u), f = lowest_bit(seeds);
+    for (;;) {
+        x = gk_or(x, run_fill(m, mr, f));
+        if (gk_any(gk_and(x, hit))) {
+            f = gk_b(0u, 0u, 0u);
+            seeds = gk_andnot(seeds, x);
+            x = f;
+        } else {
+            f = gk_andnot(gk_and(gk_or(gk_shl(x, 10), gk_shr(x, 10)), m), x);
+            if (gk_any(f)) continue;
+            // x is a whole component without a `hit` cell.
+            if (!kEdges || !touches_four_edges(x)) result = gk_or(result, x);
+            seeds = gk_andnot(seeds, x);
+            x = f;
         }
-        // A dead flood may stop short of other seeds of its component; they
-        // are flooded again and die the same way.
-        pending = gk_andnot(pending, x);
-        if (!dead && !touches_four_edges(x)) gained = gk_or(gained, x);
+        if (!gk_any(seeds)) return result;
+        f = lowest_bit(seeds);
     }
+}
+
+// The same claim after a placement of `mover` next to the empty cells
+// `around`, for a state whose territory was settled before the move
+// (GK_META_SETTLED: every qualifying empty component already owned). No
+// stone is removed by a non-final move, so an empty component that does not
+// touch the new stone keeps its neighbours and its edges, qualifies exactly
+// as before and is already owned. Only the pieces of the component the stone
+// split are examined: each touches the mover's new stone, so it is territory
+// of the mover unless it reaches a cell next to an enemy stone or touches all
+// four edges. `E` is the empty set after the move.
+__device__ __forceinline__ void claim_around(gk_bits& s, gk_b96 around, gk_b96 E, gk_b96 enemy, int mover) {
+    const gk_b96 gained = closed_components<true>(E, gk_and(E, gk_neighbours(enemy)), gk_and(around, E));
     if (!gk_any(gained)) return;
     const gk_b96 ob = gk_get(&s, GK_PLANE_OWN_BLACK), ow = gk_get(&s, GK_PLANE_OWN_WHITE);
     const gk_b96 unowned = gk_andnot(gk_valid(), gk_or(ob, ow));
     if (mover == 1) gk_put(&s, GK_PLANE_OWN_BLACK, gk_or(ob, gk_and(gained, unowned)));
     else gk_put(&s, GK_PLANE_OWN_WHITE, gk_or(ow, gk_and(gained, unowned)));
-}
-
-// True when the group of `mask` holding `seed` has a cell next to `libs`.
-// `group` receives the cells flooded before the answer was known: the whole
-// group when it has no liberty, possibly part of it otherwise.
-__device__ __forceinline__ bool group_has_liberty(gk_b96 mask, gk_b96 libs, gk_b96 seed, gk_b96& group) {
-    gk_b96 x = seed;
-    for (;;) {
-        // Shifted bits that leave the board land in the zero padding column or
-        // above bit 88, outside both `libs` and `mask`.
-        const gk_b96 d = gk_or(x, gk_or(gk_or(gk_shl(x, 1), gk_shr(x, 1)), gk_or(gk_shl(x, 10), gk_shr(x, 10))));
-        if (gk_any(gk_and(d, libs))) {
-            group = x;
-            return true;
-        }
-        const gk_b96 y = gk_and(d, mask);
-        if (gk_eq(x, y)) {
-            group = x;
-            return false;
-        }
-        x = y;
-    }
 }
 
 // One transition; returns false (state unchanged) for rejected actions.
@@ -257,21 +250,13 @@ __device__ __forceinline__ bool play(gk_bits& s, int action) {
     gk_b96 opp = actor == 1 ? white : black;
     own = gk_or(own, here);
     const gk_b96 E = gk_andnot(gk_valid(), gk_or(gk_or(own, opp), neutral));
-    // Enemy groups adjacent to the new stone with no liberty are captured.
-    gk_b96 captured = gk_b(0u, 0u, 0u);
-    gk_b96 pending = gk_and(gk_neighbours(here), opp);
-    while (gk_any(pending)) {
-        gk_b96 group;
-        const bool alive = group_has_liberty(opp, E, lowest_bit(pending), group);
-        pending = gk_andnot(pending, group);
-        if (!alive) captured = gk_or(captured, group);
-    }
+    const gk_b96 lib = gk_neighbours(E);  // cells next to an empty cell
+    const gk_b96 around = gk_neighbours(here);
+    // Enemy groups next to the new stone with no liberty are captured.
+    const gk_b96 captured = closed_components<false>(opp, gk_and(opp, lib), gk_and(around, opp));
     const int captured_count = gk_popc(captured);
     bool suicide = false;
-    if (captured_count == 0) {
-        gk_b96 group;
-        suicide = !group_has_liberty(own, E, here, group);
-    }
+    if (captured_count == 0) suicide = gk_any(closed_components<false>(own, gk_and(own, lib), here));
     if (actor == 1) --bstock;
     else --wstock;
     opp = gk_andnot(opp, captured);
@@ -289,7 +274,7 @@ __device__ __forceinline__ bool play(gk_bits& s, int action) {
     }
     s.w[15] = gk_pack_meta(enemy, bstock, wstock, 0, reason, winner, captured_field) | (meta & 0xf8000000u);
     if (reason == GK_NONE) {
-        if (meta & GK_META_SETTLED) claim_around(s, here, E, opp, actor);
+        if (meta & GK_META_SETTLED) claim_around(s, around, E, opp, actor);
         else claim_territory(s);
         s.w[15] |= GK_META_SETTLED;
     }
