@@ -484,11 +484,13 @@ struct Cols64 {
     static constexpr int EPI_WARPS = 8 * SETS;    // per set: 4 lane quadrants x 2 channel halves
     static constexpr int EPI0 = 1 + SETS;         // first epilogue warp (warp 0 loads weights)
     static constexpr int THREADS = 32 * (EPI0 + EPI_WARPS);
-    // slot_full[3], slot_free[3], acc_full[4], acc_empty[4], xchg[2], input_ready, mma_idle, heads_ready, heads_done
-    static constexpr int NBARS = 2 * NSLOT + 2 * NBUF + SETS + 4;
+    static constexpr int NDONE = 8;               // epilogue-done barriers, a ring over tiles
+    // slot_full[3], slot_free[3], acc_full[4], epi_done[8], xchg[2], input_ready, mma_idle, heads_ready,
+    // heads_done
+    static constexpr int NBARS = 2 * NSLOT + NBUF + NDONE + SETS + 4;
     static constexpr int HEADW = (3 * C + 3 + 3) / 4 * 4;
     static constexpr int XFLOATS = SETS * 3 * 4 * 2 * 32;  // [set][3 tiles][4 quadrants][2 halves][32]
-    static constexpr int SMEM = 2 * ACT + NSLOT * SLOT + NBARS * 8 + 16 + HEADW * 4 + (XFLOATS + 32) * 4;
+    static constexpr int SMEM = 2 * ACT + NSLOT * SLOT + NBARS * 8 + 16 + HEADW * 4 + XFLOATS * 4;
     static constexpr uint32_t IDESC128 = tc::idesc_bf16(128, 2 * C);
     static constexpr uint32_t IDESC64 = tc::idesc_bf16(128, C);
     static_assert(NBUF * NACC <= 512, "accumulators fit in TMEM");
@@ -497,39 +499,16 @@ struct Cols64 {
     static_assert(SMEM <= 232448, "shared memory per CTA");
 };
 
-// Bias, residual, ReLU and padding mask of 16 channels (ch0..ch0+15) of one
-// output row, stored as bf16 when `store` is set and the row is inside the
-// group. Every lane runs the same code; rows past the group read in-bounds
-// neighbouring shared memory and are not stored.
-__device__ __forceinline__ void cols_finish16(uint8_t* out, int m, int ch0, const float* bias, float (&v)[16],
-                                              bool residual, int nimg, bool store) {
-    using K = Cols64;
-    const int img = m / 100, pos = m - img * 100, r = pos / 10, cc = pos - r * 10;
-    const bool valid = img < nimg && r < 9 && cc < 9;
-    const bool keep = store && m < K::G * 100;
-    uint8_t* const row = out + (K::HALO + m) * 16 + (ch0 / 8) * K::CHUNK;
-    uint4 res[2];
-    if (residual) {
-        res[0] = *reinterpret_cast<const uint4*>(row);
-        res[1] = *reinterpret_cast<const uint4*>(row + K::CHUNK);
-    }
+// ReLU(pre + p1) of 32 channels of one output row (zero on padding rows),
+// stored as bf16 into four 8-channel chunks.
+__device__ __forceinline__ void store_row32(uint8_t* row, const float (&pre)[32], const float (&p1)[32], bool valid) {
 #pragma unroll
-    for (int j = 0; j < 16; ++j) {
-        float x = v[j] + bias[j];
-        if (residual) {
-            const uint4 rv = res[j >> 3];
-            const uint32_t w = (j & 7) < 2 ? rv.x : (j & 7) < 4 ? rv.y : (j & 7) < 6 ? rv.z : rv.w;
-            x += (j & 1) ? bf16_hi(w) : bf16_lo(w);
-        }
-        v[j] = valid ? fmaxf(x, 0.0f) : 0.0f;
-    }
-    if (keep) {
+    for (int k2 = 0; k2 < 4; ++k2) {
+        float v[8];
 #pragma unroll
-        for (int k = 0; k < 2; ++k) {
-            const uint4 o = make_uint4(pack_bf16x2(v[8 * k], v[8 * k + 1]), pack_bf16x2(v[8 * k + 2], v[8 * k + 3]),
-                                       pack_bf16x2(v[8 * k + 4], v[8 * k + 5]), pack_bf16x2(v[8 * k + 6], v[8 * k + 7]));
-            *reinterpret_cast<uint4*>(row + k * K::CHUNK) = o;
-        }
+        for (int j = 0; j < 8; ++j) v[j] = valid ? fmaxf(pre[8 * k2 + j] + p1[8 * k2 + j], 0.0f) : 0.0f;
+        *reinterpret_cast<uint4*>(row + k2 * Cols64::CHUNK) =
+            make_uint4(pack_bf16x2(v[0], v[1]), pack_bf16x2(v[2], v[3]), pack_bf16x2(v[4], v[5]), pack_bf16x2(v[6], v[7]));
     }
 }
 
@@ -545,12 +524,11 @@ __global__ void __launch_bounds__(Cols64::THREADS, 1)
     uint32_t* const tmem_holder = reinterpret_cast<uint32_t*>(bars + K::NBARS);
     float* const headw = reinterpret_cast<float*>(tmem_holder + 4);  // [3][C] then [3] biases
     float* const xp1 = headw + K::HEADW;    // lane 0's P1 per set, tile, quadrant and half
-    float* const zero_row = xp1 + K::XFLOATS;  // zeros: the missing neighbour below quadrant 3
     const uint32_t slot_full = tc::smem_u32(bars);
     const uint32_t slot_free = slot_full + 8 * K::NSLOT;
     const uint32_t acc_full = slot_free + 8 * K::NSLOT;
-    const uint32_t acc_empty = acc_full + 8 * K::NBUF;
-    const uint32_t xchg = acc_empty + 8 * K::NBUF;
+    const uint32_t epi_done = acc_full + 8 * K::NBUF;
+    const uint32_t xchg = epi_done + 8 * K::NDONE;
     const uint32_t input_ready = xchg + 8 * K::SETS;
     const uint32_t mma_idle = input_ready + 8;
     const uint32_t heads_ready = mma_idle + 8;
@@ -565,14 +543,13 @@ __global__ void __launch_bounds__(Cols64::THREADS, 1)
         reinterpret_cast<uint4*>(smem)[i] = make_uint4(0, 0, 0, 0);
     for (int i = threadIdx.x; i < 3 * C; i += blockDim.x) headw[i] = p.head_w[i];
     if (threadIdx.x < 3) headw[3 * C + threadIdx.x] = p.head_b[threadIdx.x];
-    if (threadIdx.x < 32) zero_row[threadIdx.x] = 0.0f;
     tc::fence_proxy_async_smem();
     if (threadIdx.x == 0) {
         for (int b = 0; b < K::NBARS; ++b) {
             const uint32_t bar = slot_full + 8 * b;
             uint32_t n = 1u;                                           // producer / commit arrivals
             if ((bar >= slot_free && bar < acc_full) || bar == mma_idle) n = (uint32_t)K::SETS;  // each MMA warp
-            if (bar >= acc_empty && bar < input_ready) n = 8u;         // one epilogue set
+            if (bar >= epi_done && bar < input_ready) n = 8u;          // one epilogue set (done, exchange)
             if (bar == input_ready || bar == heads_ready || bar == heads_done) n = (uint32_t)K::EPI_WARPS;
             tc::mbar_init(bar, n);
         }
@@ -627,15 +604,22 @@ __global__ void __launch_bounds__(Cols64::THREADS, 1)
                     const bool last_use = t + 2 >= K::T;  // and its last one releases them
                     if (l == 0 && first_use && !warp_wait(input_ready, (uint32_t)i & 1u, status, leader))
                         goto mma_drain;
-                    // The two epilogue sets finish tiles of opposite parity, so wait for
-                    // both tile c-4 (its buffer is this tile's) and tile c-3 (with c-5 of
-                    // the same set, the last of the input rows this tile reads).
-                    if (c >= 4 &&
-                        !warp_wait(acc_empty + 8 * (c % K::NBUF), (uint32_t)((c - 4) / K::NBUF) & 1u, status, leader))
+                    // Tile t reads the rows the previous layer's tiles t-1..t+1 wrote
+                    // (tiles c-5, c-4, c-3), and tile c-4's epilogue also frees this
+                    // tile's accumulator. Each epilogue set finishes its tiles in order,
+                    // so tile c-3 stands for c-5 when t < T-1; the last tile has no
+                    // tile below it and waits for c-5 itself. The epilogue-done ring is
+                    // NDONE deep: no tile waited for here can be overtaken NDONE tiles
+                    // later before this tile is issued.
+                    if (c >= 4 && !warp_wait(epi_done + 8 * ((c - 4) % K::NDONE), (uint32_t)((c - 4) / K::NDONE) & 1u,
+                                             status, leader))
                         goto mma_drain;
-                    if (c >= 3 &&
-                        !warp_wait(acc_empty + 8 * ((c - 3) % K::NBUF), (uint32_t)((c - 3) / K::NBUF) & 1u, status, leader))
-                        goto mma_drain;
+                    {
+                        const int dep = t == K::T - 1 ? c - 5 : c - 3;
+                        if (dep >= 0 && !warp_wait(epi_done + 8 * (dep % K::NDONE), (uint32_t)(dep / K::NDONE) & 1u,
+                                                   status, leader))
+                            goto mma_drain;
+                    }
                     const uint32_t d = tmem + (uint32_t)((c % K::NBUF) * K::NACC);
 #pragma unroll
                     for (int dr = 0; dr < 3; ++dr) {
@@ -687,49 +671,73 @@ __global__ void __launch_bounds__(Cols64::THREADS, 1)
             for (int l = 0; l < NL; ++l) {
                 uint8_t* const out = l % 2 == 0 ? bufP : bufQ;
                 const bool residual = l >= 2 && l % 2 == 0;
-                float bias[32];
-#pragma unroll
-                for (int j = 0; j < 32; ++j) bias[j] = __ldg(p.conv_b + l * C + ch0 + j);
+                const float* const bias = p.conv_b + l * C + ch0;
                 for (int t = 0; t < K::T; ++t, ++c) {
                     if ((c & 1) != s) continue;
                     const int b = c % K::NBUF, k = c >> 1;  // k: this set's tile count
                     const int x = k % 3;
-                    if (!warp_wait(acc_full + 8 * b, (uint32_t)(c / K::NBUF) & 1u, status, lane == 0)) goto epi_exit;
-                    tc::tc_fence_after();
-                    const uint32_t taddr = tmem + lane_base + (uint32_t)(b * K::NACC + ch0);
-                    {
-                        // Publish lane 0's P1 (the last row of the quadrant above needs it).
-                        float pub[32];
-                        tc::tmem_ld32(taddr + C, pub);
-                        if (lane == 0) {
-                            float4* const w = reinterpret_cast<float4*>(xp1 + (((s * 3 + x) * 4 + q) * 2 + h) * 32);
+                    const int m = t * K::STRIDE + q * 32 + lane;
+                    uint8_t* const row = out + (K::HALO + m) * 16 + (ch0 / 8) * K::CHUNK;
+                    // Bias plus residual (the block input, which this warp wrote two
+                    // layers ago and now overwrites in place) before the accumulator
+                    // is ready. Row 127 belongs to the next tile and is not stored.
+                    float pre[32];
 #pragma unroll
-                            for (int j = 0; j < 8; ++j)
-                                w[j] = make_float4(pub[4 * j], pub[4 * j + 1], pub[4 * j + 2], pub[4 * j + 3]);
+                    for (int j = 0; j < 32; ++j) pre[j] = __ldg(bias + j);
+                    if (residual) {
+#pragma unroll
+                        for (int k2 = 0; k2 < 4; ++k2) {
+                            const uint4 rv = *reinterpret_cast<const uint4*>(row + k2 * K::CHUNK);
+                            const uint32_t w[4] = {rv.x, rv.y, rv.z, rv.w};
+#pragma unroll
+                            for (int j = 0; j < 8; ++j) pre[8 * k2 + j] += (j & 1) ? bf16_hi(w[j >> 1]) : bf16_lo(w[j >> 1]);
                         }
+                    }
+                    if (!warp_wait(acc_full + 8 * b, (uint32_t)(c / K::NBUF) & 1u, status, lane == 0)) goto epi_exit;
+                    const uint32_t taddr = tmem + lane_base + (uint32_t)(b * K::NACC + ch0);
+                    float p1[32], p0[16];
+                    tc::tmem_ld32_16(taddr + C, taddr, p1, p0);
+                    if (q > 0 && lane == 0) {
+                        // Publish lane 0's P1: the last row of the quadrant above needs it.
+                        float4* const w = reinterpret_cast<float4*>(xp1 + (((s * 3 + x) * 4 + q) * 2 + h) * 32);
+#pragma unroll
+                        for (int j = 0; j < 8; ++j) w[j] = make_float4(p1[4 * j], p1[4 * j + 1], p1[4 * j + 2], p1[4 * j + 3]);
                     }
                     __syncwarp();
                     if (lane == 0) tc::mbar_arrive(xbar);
+                    // y[m] = P0[m] + P1[m + 1]: P1 of the next row comes from the next lane.
+#pragma unroll
+                    for (int j = 0; j < 32; ++j) p1[j] = __shfl_down_sync(0xffffffffu, p1[j], 1);
+#pragma unroll
+                    for (int j = 0; j < 16; ++j) pre[j] += p0[j];
+                    tc::tmem_ld16(taddr + 16, p0);
+#pragma unroll
+                    for (int j = 0; j < 16; ++j) pre[16 + j] += p0[j];
+                    const int img = m / 100, pos = m - img * 100, r = pos / 10, cc = pos - r * 10;
+                    const bool valid = img < nimg && r < 9 && cc < 9;
+                    // Lane 31's next row is lane 0 of the quadrant below, published
+                    // above; the wait comes after this warp's own TMEM reads so the
+                    // other warps' publishing overlaps them. Quadrant 3's lane 31 is
+                    // row 127, which belongs to the next tile and is not stored.
                     if (!warp_wait(xbar, (uint32_t)k & 1u, status, lane == 0)) goto epi_exit;
-                    const float* const nbr = q < 3 ? xp1 + (((s * 3 + x) * 4 + q + 1) * 2 + h) * 32 : zero_row;
-                    const int m = t * K::STRIDE + q * 32 + lane;
-                    const bool own = !(q == 3 && lane == 31);  // row 127 belongs to the next tile
+                    if (q < 3) {
+                        const float4* const nb = reinterpret_cast<const float4*>(xp1 + (((s * 3 + x) * 4 + q + 1) * 2 + h) * 32);
 #pragma unroll
-                    for (int pass = 0; pass < 2; ++pass) {
-                        float p0[16], p1[16];
-                        tc::tmem_ld16x2(taddr + 16 * pass, taddr + C + 16 * pass, p0, p1);
-#pragma unroll
-                        for (int j = 0; j < 16; ++j) {
-                            const float dn = __shfl_down_sync(0xffffffffu, p1[j], 1);
-                            const float nx = nbr[16 * pass + j];
-                            p0[j] += lane == 31 ? nx : dn;
+                        for (int j = 0; j < 8; ++j) {
+                            const float4 v = nb[j];
+                            if (lane == 31) {
+                                p1[4 * j] = v.x;
+                                p1[4 * j + 1] = v.y;
+                                p1[4 * j + 2] = v.z;
+                                p1[4 * j + 3] = v.w;
+                            }
                         }
-                        cols_finish16(out, m, ch0 + 16 * pass, bias + 16 * pass, p0, residual, nimg, own);
                     }
+                    if (m < K::G * 100 && !(q == 3 && lane == 31)) store_row32(row, pre, p1, valid);
                     tc::tc_fence_before();
                     tc::fence_proxy_async_smem();
                     __syncwarp();
-                    if (lane == 0) tc::mbar_arrive(acc_empty + 8 * b);
+                    if (lane == 0) tc::mbar_arrive(epi_done + 8 * (c % K::NDONE));
                 }
             }
             // Build the next group's stem input (buffer Q) before the head pass,

@@ -278,6 +278,31 @@ __device__ __forceinline__ void tmem_ld32x2(uint32_t a0, uint32_t a1, float (&v0
     }
 }
 
+// A 32x32b.x32 load and a 32x32b.x16 load under a single wait.
+__device__ __forceinline__ void tmem_ld32_16(uint32_t a0, uint32_t a1, float (&v0)[32], float (&v1)[16]) {
+    uint32_t r0[32], r1[16];
+    tmem_ld32_issue(a0, r0);
+    tmem_ld16_issue(a1, r1);
+    {
+        uint32_t (&r)[16] = r1;
+        asm volatile("tcgen05.wait::ld.sync.aligned;" : "+r"(r[0]), "+r"(r[1]), "+r"(r[2]), "+r"(r[3]), "+r"(r[4]), "+r"(r[5]), "+r"(r[6]), "+r"(r[7]), "+r"(r[8]), "+r"(r[9]), "+r"(r[10]), "+r"(r[11]), "+r"(r[12]), "+r"(r[13]), "+r"(r[14]), "+r"(r[15]) : : "memory");
+    }
+    tmem_pin32(r0);
+#pragma unroll
+    for (int i = 0; i < 32; ++i) v0[i] = __uint_as_float(r0[i]);
+#pragma unroll
+    for (int i = 0; i < 16; ++i) v1[i] = __uint_as_float(r1[i]);
+}
+
+// One 32x32b.x16 load and its wait.
+__device__ __forceinline__ void tmem_ld16(uint32_t a0, float (&v0)[16]) {
+    uint32_t r[16];
+    tmem_ld16_issue(a0, r);
+    asm volatile("tcgen05.wait::ld.sync.aligned;" : "+r"(r[0]), "+r"(r[1]), "+r"(r[2]), "+r"(r[3]), "+r"(r[4]), "+r"(r[5]), "+r"(r[6]), "+r"(r[7]), "+r"(r[8]), "+r"(r[9]), "+r"(r[10]), "+r"(r[11]), "+r"(r[12]), "+r"(r[13]), "+r"(r[14]), "+r"(r[15]) : : "memory");
+#pragma unroll
+    for (int i = 0; i < 16; ++i) v0[i] = __uint_as_float(r[i]);
+}
+
 // Two 32x32b.x16 loads under a single wait.
 __device__ __forceinline__ void tmem_ld16x2(uint32_t a0, uint32_t a1, float (&v0)[16], float (&v1)[16]) {
     uint32_t r0[16], r1[16];
