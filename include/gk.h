@@ -71,7 +71,11 @@ GK_API int gk_records_to_bits(const int32_t* recs, uint32_t* bits, uint32_t* sta
 GK_API int gk_bits_to_records(const uint32_t* bits, int32_t* recs, int64_t n, void* stream);
 
 /* One transition per packed state, in place (the HBM-bound rules kernel).
- * Same rules as gpu_play (gpu_rules.py:185-252) / State::play (engine/src/State.cpp:92-167). */
+ * Same rules as gpu_play (gpu_rules.py:185-252) / State::play (engine/src/State.cpp:92-167).
+ * Packed states must come from gk_records_to_bits, gk_initial_bits or earlier
+ * library transitions: the territory-settled flag (GK_META_SETTLED) that the
+ * transitions set lets a placement re-examine only the empty component it
+ * splits; hand-built states leave meta bits 27..31 zero. */
 GK_API int gk_play_bits(uint32_t* bits, const void* actions, int action_bytes, uint8_t* accepted, int64_t n, void* stream);
 
 /* Encoder from packed states; same outputs as gk_encode_records (reference
