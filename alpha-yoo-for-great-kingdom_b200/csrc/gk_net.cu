@@ -823,8 +823,10 @@ struct HeadOut {
 
 constexpr int kPolStride = 163;  // odd row stride: conflict-free lane-per-row reads
 constexpr int kValStride = 81;
-constexpr int kHeadWarps = 16;  // two 16-warp blocks per SM keep 32 warps in flight
-constexpr size_t kHeadSmem = (size_t)(82 * kPolStride + 64 * kValStride + kHeadWarps * 244) * sizeof(float);
+constexpr int kHeadWarps = 8;   // per block
+constexpr int kHeadPos = 4;     // positions per warp: each weight read from shared memory feeds four
+constexpr size_t kHeadSmem =
+    (size_t)(82 * kPolStride + 64 * kValStride + kHeadWarps * kHeadPos * 244) * sizeof(float);
 
 // Copies an N-float row-major matrix of COLS columns into shared memory with
 // row stride STRIDE. Each thread issues a batch of independent read-only
@@ -859,81 +861,111 @@ __global__ void __launch_bounds__(32 * kHeadWarps) net_heads_kernel(NetParams p,
     stage_matrix<64 * 81, 81, kValStride>(w1, p.val_w1);
     __syncthreads();
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    float* feat = feat_all + warp * 244;
+    float* feat = feat_all + warp * (kHeadPos * 244);
     const int count = input_count(in);
     // Lane l owns actions l, l+32, l+64 (the last only for l < 18) and hidden
-    // units l, l+32 of the value head.
+    // units l, l+32 of the value head, for each of the warp's kHeadPos
+    // positions. Every accumulation runs over the features in order, so each
+    // position's sums are those of a one-position loop.
     const float* wa = wp + lane * kPolStride;
     const float* wb = wp + (lane + 32) * kPolStride;
     const float* wc = wp + (lane + 64 < GK_ACTIONS ? lane + 64 : GK_ACTIONS - 1) * kPolStride;
     const float* va = w1 + lane * kValStride;
     const float* vb = w1 + (lane + 32) * kValStride;
-    for (int img = blockIdx.x * kHeadWarps + warp; img < count; img += gridDim.x * kHeadWarps) {
-        const float* hf = headfeat + (int64_t)img * 243;
-        float fv[8];
+    for (int img0 = (blockIdx.x * kHeadWarps + warp) * kHeadPos; img0 < count;
+         img0 += gridDim.x * kHeadWarps * kHeadPos) {
 #pragma unroll
-        for (int u = 0; u < 8; ++u) fv[u] = lane + 32 * u < 243 ? __ldg(hf + lane + 32 * u) : 0.f;
+        for (int u = 0; u < kHeadPos; ++u) {
+            const int img = img0 + u;
+            const float* hf = headfeat + (int64_t)img * 243;
+            float fv[8];
 #pragma unroll
-        for (int u = 0; u < 8; ++u)
-            if (lane + 32 * u < 243) feat[lane + 32 * u] = fv[u];
+            for (int v = 0; v < 8; ++v) fv[v] = img < count && lane + 32 * v < 243 ? __ldg(hf + lane + 32 * v) : 0.f;
+#pragma unroll
+            for (int v = 0; v < 8; ++v)
+                if (lane + 32 * v < 243) feat[u * 244 + lane + 32 * v] = fv[v];
+        }
         __syncwarp();
-        // Three independent accumulation chains, each summed in feature order.
-        float la = 0.f, lb = 0.f, lc = 0.f;
-#pragma unroll 6
+        float la[kHeadPos], lb[kHeadPos], lc[kHeadPos];
+#pragma unroll
+        for (int u = 0; u < kHeadPos; ++u) la[u] = lb[u] = lc[u] = 0.f;
+#pragma unroll 3
         for (int j = 0; j < 162; ++j) {
-            const float f = feat[j];
-            la = fmaf(wa[j], f, la);
-            lb = fmaf(wb[j], f, lb);
-            lc = fmaf(wc[j], f, lc);
+            const float xa = wa[j], xb = wb[j], xc = wc[j];
+#pragma unroll
+            for (int u = 0; u < kHeadPos; ++u) {
+                const float f = feat[u * 244 + j];
+                la[u] = fmaf(xa, f, la[u]);
+                lb[u] = fmaf(xb, f, lb[u]);
+                lc[u] = fmaf(xc, f, lc[u]);
+            }
         }
-        float logit[3];
-        logit[0] = la + __ldg(p.pol_b + lane);
-        logit[1] = lb + __ldg(p.pol_b + lane + 32);
-        logit[2] = lane + 64 < GK_ACTIONS ? lc + __ldg(p.pol_b + lane + 64) : 0.f;
-        float ha = __ldg(p.val_b1 + lane), hb = __ldg(p.val_b1 + lane + 32);
-#pragma unroll 9
+        float ha[kHeadPos], hb[kHeadPos];
+        const float ba = __ldg(p.val_b1 + lane), bb = __ldg(p.val_b1 + lane + 32);
+#pragma unroll
+        for (int u = 0; u < kHeadPos; ++u) {
+            ha[u] = ba;
+            hb[u] = bb;
+        }
+#pragma unroll 3
         for (int j = 0; j < 81; ++j) {
-            const float f = feat[162 + j];
-            ha = fmaf(va[j], f, ha);
-            hb = fmaf(vb[j], f, hb);
+            const float xa = va[j], xb = vb[j];
+#pragma unroll
+            for (int u = 0; u < kHeadPos; ++u) {
+                const float f = feat[u * 244 + 162 + j];
+                ha[u] = fmaf(xa, f, ha[u]);
+                hb[u] = fmaf(xb, f, hb[u]);
+            }
         }
-        float vpart = fmaf(fmaxf(ha, 0.f), __ldg(p.val_w2 + lane), 0.f);
-        vpart = fmaf(fmaxf(hb, 0.f), __ldg(p.val_w2 + lane + 32), vpart);
+        const float pa = __ldg(p.pol_b + lane), pb = __ldg(p.pol_b + lane + 32);
+        const float pc = lane + 64 < GK_ACTIONS ? __ldg(p.pol_b + lane + 64) : 0.f;
+        const float w2a = __ldg(p.val_w2 + lane), w2b = __ldg(p.val_w2 + lane + 32), b2 = __ldg(p.val_b2);
 #pragma unroll
-        for (int off = 16; off; off >>= 1) vpart += __shfl_xor_sync(0xffffffffu, vpart, off);
-        const float value = tanhf(vpart + __ldg(p.val_b2));
-        if (out.logits) {
+        for (int u = 0; u < kHeadPos; ++u) {
+            const int img = img0 + u;
+            if (img >= count) break;  // warp-uniform
+            float logit[3];
+            logit[0] = la[u] + pa;
+            logit[1] = lb[u] + pb;
+            logit[2] = lane + 64 < GK_ACTIONS ? lc[u] + pc : 0.f;
+            float vpart = fmaf(fmaxf(ha[u], 0.f), w2a, 0.f);
+            vpart = fmaf(fmaxf(hb[u], 0.f), w2b, vpart);
 #pragma unroll
-            for (int k = 0; k < 3; ++k)
-                if (lane + 32 * k < GK_ACTIONS) out.logits[(int64_t)img * GK_ACTIONS + lane + 32 * k] = logit[k];
-            if (lane == 0) out.values[img] = value;
-        } else {
-            // Masked softmax over the leaf's legal actions (gpu_puct.py:500-501).
-            const int tree = in.index ? in.index[img] : img;
-            const gk_bits s = out.states[tree];
-            const gk_b96 placements = legal_placements(s);
-            bool legal[3];
-            float mx = -INFINITY;
+            for (int off = 16; off; off >>= 1) vpart += __shfl_xor_sync(0xffffffffu, vpart, off);
+            const float value = tanhf(vpart + b2);
+            if (out.logits) {
 #pragma unroll
-            for (int k = 0; k < 3; ++k) {
-                const int a = lane + 32 * k;
-                legal[k] = a < GK_ACTIONS && (a == GK_PASS ? true : gk_test(placements, a + a / 9) != 0);
-                if (legal[k]) mx = fmaxf(mx, logit[k]);
+                for (int k = 0; k < 3; ++k)
+                    if (lane + 32 * k < GK_ACTIONS) out.logits[(int64_t)img * GK_ACTIONS + lane + 32 * k] = logit[k];
+                if (lane == 0) out.values[img] = value;
+            } else {
+                // Masked softmax over the leaf's legal actions (gpu_puct.py:500-501).
+                const int tree = in.index ? in.index[img] : img;
+                const gk_bits s = out.states[tree];
+                const gk_b96 placements = legal_placements(s);
+                bool legal[3];
+                float mx = -INFINITY;
+#pragma unroll
+                for (int k = 0; k < 3; ++k) {
+                    const int a = lane + 32 * k;
+                    legal[k] = a < GK_ACTIONS && (a == GK_PASS ? true : gk_test(placements, a + a / 9) != 0);
+                    if (legal[k]) mx = fmaxf(mx, logit[k]);
+                }
+#pragma unroll
+                for (int off = 16; off; off >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
+                float e[3], sum = 0.f;
+#pragma unroll
+                for (int k = 0; k < 3; ++k) {
+                    e[k] = legal[k] ? __expf(logit[k] - mx) : 0.f;
+                    sum += e[k];
+                }
+#pragma unroll
+                for (int off = 16; off; off >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, off);
+#pragma unroll
+                for (int k = 0; k < 3; ++k)
+                    if (lane + 32 * k < GK_ACTIONS) out.policy[(int64_t)tree * GK_ACTIONS + lane + 32 * k] = e[k] / sum;
+                if (lane == 0) out.leaf_value[tree] = value;
             }
-#pragma unroll
-            for (int off = 16; off; off >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
-            float e[3], sum = 0.f;
-#pragma unroll
-            for (int k = 0; k < 3; ++k) {
-                e[k] = legal[k] ? __expf(logit[k] - mx) : 0.f;
-                sum += e[k];
-            }
-#pragma unroll
-            for (int off = 16; off; off >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, off);
-#pragma unroll
-            for (int k = 0; k < 3; ++k)
-                if (lane + 32 * k < GK_ACTIONS) out.policy[(int64_t)tree * GK_ACTIONS + lane + 32 * k] = e[k] / sum;
-            if (lane == 0) out.leaf_value[tree] = value;
         }
         __syncwarp();
     }
@@ -1045,7 +1077,7 @@ int launch_heads(const NetParams& p, const float* headfeat, const NetInput& in, 
                                         (int)kHeadSmem) == cudaSuccess;
         }))
         return launch_status();
-    int64_t blocks = (in.n + kHeadWarps - 1) / kHeadWarps;
+    int64_t blocks = (in.n + kHeadWarps * kHeadPos - 1) / (kHeadWarps * kHeadPos);
     if (blocks > 2 * kSmCount) blocks = 2 * kSmCount;
     net_heads_kernel<<<(int)(blocks < 1 ? 1 : blocks), 32 * kHeadWarps, kHeadSmem, stream>>>(p, headfeat, in, out);
     return launch_status();
