@@ -204,7 +204,7 @@ __device__ __forceinline__ void select_tree(const PuctView& v, int64_t t, int C,
     }
 }
 
-__global__ void __launch_bounds__(32 * kWarpsPerBlock, 6) puct_select_kernel(PuctView v, int64_t B, int C, PuctOptions o) {
+__global__ void __launch_bounds__(32 * kWarpsPerBlock, 7) puct_select_kernel(PuctView v, int64_t B, int C, PuctOptions o) {
     const int lane = threadIdx.x & 31;
     const int64_t t = (blockIdx.x * (int64_t)blockDim.x + threadIdx.x) >> 5;
     if (t < B) select_tree(v, t, C, o, lane);
