@@ -354,18 +354,59 @@ GK_HD void gk_eval_words_from_record(const int32_t* rec, uint64_t* words) {
                ((uint64_t)(uint32_t)rec[GK_CAPTURED] << 48);
 }
 
-/* Same 7 words computed directly from the packed bitboard state. */
+/* Cells 9r+c of a 96-bit board (rows of 10 bits) as an 81-bit mask:
+ * *lo holds cells 0..63, *hi cells 64..80. */
+GK_HD void gk_board_cells(gk_b96 b, uint64_t* lo, uint64_t* hi) {
+    const uint64_t blo = (uint64_t)b.w[0] | ((uint64_t)b.w[1] << 32), bhi = b.w[2];
+    uint64_t l = 0u, h = 0u;
+    for (int r = 0; r < 9; ++r) {
+        const int src = 10 * r, dst = 9 * r;
+        uint64_t row;
+        if (src + 9 <= 64) row = (blo >> src) & 0x1FFu;
+        else if (src >= 64) row = (bhi >> (src - 64)) & 0x1FFu;
+        else row = ((blo >> src) | (bhi << (64 - src))) & 0x1FFu;
+        if (dst + 9 <= 64) l |= row << dst;
+        else if (dst >= 64) h |= row << (dst - 64);
+        else {
+            l |= row << dst;
+            h |= row >> (64 - dst);
+        }
+    }
+    *lo = l;
+    *hi = h;
+}
+
+/* Bit j of the low 32 bits of x -> bit 2j. */
+GK_HD uint64_t gk_spread32(uint64_t x) {
+    x &= 0xFFFFFFFFull;
+    x = (x | (x << 16)) & 0x0000FFFF0000FFFFull;
+    x = (x | (x << 8)) & 0x00FF00FF00FF00FFull;
+    x = (x | (x << 4)) & 0x0F0F0F0F0F0F0F0Full;
+    x = (x | (x << 2)) & 0x3333333333333333ull;
+    x = (x | (x << 1)) & 0x5555555555555555ull;
+    return x;
+}
+
+/* Same 7 words computed directly from the packed bitboard state: the 2-bit
+ * codes of gk_eval_words_from_record (cell: black 1, else white 2, else
+ * neutral 3; owner: black 1, else white 2) as two bit-planes each, compacted
+ * to cell order and interleaved. */
 GK_HD void gk_eval_words_from_bits(const gk_bits* s, uint64_t* words) {
-    for (int i = 0; i < GK_EVAL_WORDS; ++i) words[i] = 0u;
-    gk_b96 black = gk_get(s, GK_PLANE_BLACK), white = gk_get(s, GK_PLANE_WHITE);
-    gk_b96 neutral = gk_get(s, GK_PLANE_NEUTRAL);
-    gk_b96 ob = gk_get(s, GK_PLANE_OWN_BLACK), ow = gk_get(s, GK_PLANE_OWN_WHITE);
-    for (int i = 0; i < GK_CELLS; ++i) {
-        int b = gk_cell_bit(i);
-        uint64_t cell = gk_test(black, b) ? 1u : gk_test(white, b) ? 2u : gk_test(neutral, b) ? 3u : 0u;
-        uint64_t own = gk_test(ob, b) ? 1u : gk_test(ow, b) ? 2u : 0u;
-        words[i >> 5] |= cell << (2 * (i & 31));
-        words[3 + (i >> 5)] |= own << (2 * (i & 31));
+    const gk_b96 black = gk_get(s, GK_PLANE_BLACK), white = gk_get(s, GK_PLANE_WHITE);
+    const gk_b96 neutral = gk_get(s, GK_PLANE_NEUTRAL);
+    const gk_b96 ob = gk_get(s, GK_PLANE_OWN_BLACK), ow = gk_get(s, GK_PLANE_OWN_WHITE);
+    gk_b96 planes[4];
+    planes[0] = gk_or(black, gk_andnot(neutral, white));       /* cell code bit 0 */
+    planes[1] = gk_andnot(gk_or(white, neutral), black);       /* cell code bit 1 */
+    planes[2] = ob;                                            /* owner code bit 0 */
+    planes[3] = gk_andnot(ow, ob);                             /* owner code bit 1 */
+    for (int k = 0; k < 2; ++k) {
+        uint64_t lo0, hi0, lo1, hi1;
+        gk_board_cells(planes[2 * k], &lo0, &hi0);
+        gk_board_cells(planes[2 * k + 1], &lo1, &hi1);
+        words[3 * k] = gk_spread32(lo0) | (gk_spread32(lo1) << 1);
+        words[3 * k + 1] = gk_spread32(lo0 >> 32) | (gk_spread32(lo1 >> 32) << 1);
+        words[3 * k + 2] = gk_spread32(hi0) | (gk_spread32(hi1) << 1);
     }
     words[6] = (uint64_t)gk_actor(s) | ((uint64_t)gk_stock(s, 1) << 8) | ((uint64_t)gk_stock(s, 2) << 16) |
                ((uint64_t)gk_passes(s) << 24) | ((uint64_t)gk_reason(s) << 32) |
