@@ -829,25 +829,14 @@ constexpr size_t kHeadSmem =
     (size_t)(82 * kPolStride + 64 * kValStride + kHeadWarps * kHeadPos * 244) * sizeof(float);
 
 // Copies an N-float row-major matrix of COLS columns into shared memory with
-// row stride STRIDE. Each thread issues a batch of independent read-only
-// loads before its shared stores; a load-store pair per iteration would
-// serialise on global latency (a generic source pointer may alias shared
-// memory, so the compiler cannot move loads ahead of the stores).
+// row stride STRIDE, as 4-byte asynchronous copies: every copy of the block
+// is in flight at once instead of one global round trip per batch of loads.
+// The caller commits and waits (cp.async.wait_all) before reading.
 template <int N, int COLS, int STRIDE>
 __device__ __forceinline__ void stage_matrix(float* dst, const float* src) {
-    constexpr int kBatch = 8;
-    for (int base = threadIdx.x; base < N; base += blockDim.x * kBatch) {
-        float v[kBatch];
-#pragma unroll
-        for (int u = 0; u < kBatch; ++u) {
-            const int i = base + u * (int)blockDim.x;
-            v[u] = i < N ? __ldg(src + i) : 0.f;
-        }
-#pragma unroll
-        for (int u = 0; u < kBatch; ++u) {
-            const int i = base + u * (int)blockDim.x;
-            if (i < N) dst[(i / COLS) * STRIDE + i % COLS] = v[u];
-        }
+    for (int i = threadIdx.x; i < N; i += blockDim.x) {
+        const uint32_t d = tc::smem_u32(dst + (i / COLS) * STRIDE + i % COLS);
+        asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(d), "l"(src + i) : "memory");
     }
 }
 
@@ -859,6 +848,7 @@ __global__ void __launch_bounds__(32 * kHeadWarps) net_heads_kernel(NetParams p,
     float* feat_all = w1 + 64 * kValStride;
     stage_matrix<82 * 162, 162, kPolStride>(wp, p.pol_w);
     stage_matrix<64 * 81, 81, kValStride>(w1, p.val_w1);
+    asm volatile("cp.async.wait_all;" ::: "memory");
     __syncthreads();
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     float* feat = feat_all + warp * (kHeadPos * 244);
