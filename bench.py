@@ -255,7 +255,8 @@ def e2e_arm(model, steps: int, warmup: int, device):
     elapsed = time.perf_counter() - start
     return {"value": steps * LANES * SIMULATIONS / elapsed, "unit": "simulations/s",
             "moves_per_s": steps * LANES / elapsed, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
-            "api": "GpuStateBatch + GpuPUCT.search + GpuStateBatch.play with pinned host records"}
+            "api": "GpuStateBatch + GpuPUCT.search + GpuStateBatch.play with pinned host records",
+            "_moves": steps * LANES, "_elapsed": elapsed}
 
 
 def main():
@@ -353,10 +354,17 @@ def main():
     e2e = None
     if args.e2e_steps > 0:
         e2e = e2e_arm(model, args.e2e_steps, 1, device)
+        moves, elapsed = float(e2e.pop("_moves")), e2e.pop("_elapsed")
         if world > 1:
-            t = torch.tensor([e2e["value"]], dtype=torch.float64, device=device)
+            # Whole job: every rank's moves over the slowest rank's time.
+            t = torch.tensor([moves], dtype=torch.float64, device=device)
             dist.all_reduce(t, op=dist.ReduceOp.SUM)
-            e2e["value"] = t.item()
+            moves = t.item()
+            t = torch.tensor([elapsed], dtype=torch.float64, device=device)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            elapsed = t.item()
+        e2e["value"] = moves * SIMULATIONS / elapsed
+        e2e["moves_per_s"] = moves / elapsed
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         try:
