@@ -354,17 +354,17 @@ def main():
     e2e = None
     if args.e2e_steps > 0:
         e2e = e2e_arm(model, args.e2e_steps, 1, device)
-        moves, elapsed = float(e2e.pop("_moves")), e2e.pop("_elapsed")
+        e2e_moves, e2e_elapsed = float(e2e.pop("_moves")), e2e.pop("_elapsed")
         if world > 1:
             # Whole job: every rank's moves over the slowest rank's time.
-            t = torch.tensor([moves], dtype=torch.float64, device=device)
+            t = torch.tensor([e2e_moves], dtype=torch.float64, device=device)
             dist.all_reduce(t, op=dist.ReduceOp.SUM)
-            moves = t.item()
-            t = torch.tensor([elapsed], dtype=torch.float64, device=device)
+            e2e_moves = t.item()
+            t = torch.tensor([e2e_elapsed], dtype=torch.float64, device=device)
             dist.all_reduce(t, op=dist.ReduceOp.MAX)
-            elapsed = t.item()
-        e2e["value"] = moves * SIMULATIONS / elapsed
-        e2e["moves_per_s"] = moves / elapsed
+            e2e_elapsed = t.item()
+        e2e["value"] = e2e_moves * SIMULATIONS / e2e_elapsed
+        e2e["moves_per_s"] = e2e_moves / e2e_elapsed
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         try:
