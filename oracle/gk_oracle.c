@@ -347,11 +347,20 @@ static double edge_value(const o_edge* e) { return e->visits == 0 ? 0.0 : e->val
 /* Evaluator used by the search: 0 = injected hash evaluator, 1 = uniform
  * (weight 1 for every action, value 0 - what a zero-weight network gives). */
 static __thread int g_uniform_evaluator = 0;
+/* Root candidates of a search with tactical checks (NULL: every legal action). */
+static __thread const uint8_t* g_root_allow = NULL;
 
 /* PUCT.cpp:53-86 */
-static int expand(o_node* node, const int32_t* rec, o_edge* storage, double* leaf_value, int64_t* evaluations) {
+static int expand(o_node* node, const int32_t* rec, o_edge* storage, double* leaf_value, int64_t* evaluations,
+                  const uint8_t* allow) {
     int moves[GK_ACTIONS];
     int n = legal_list(rec, moves);
+    if (allow) {
+        int kept = 0;
+        for (int i = 0; i < n; ++i)
+            if (allow[moves[i]]) moves[kept++] = moves[i];
+        n = kept;
+    }
     if (n == 0) return -1;
     float w[GK_ACTIONS], v;
     if (g_uniform_evaluator) {
@@ -428,7 +437,7 @@ int gko_puct_search(const int32_t* root, int simulations, double c_puct, int32_t
     int64_t evaluations = 0;
     double ignored;
     tree[0].player = root[GK_ACTOR];
-    if (expand(&tree[0], root, pool, &ignored, &evaluations) != 0) {
+    if (expand(&tree[0], root, pool, &ignored, &evaluations, g_root_allow) != 0) {
         status = -2;
         goto done;
     }
@@ -444,7 +453,8 @@ int gko_puct_search(const int32_t* root, int simulations, double c_puct, int32_t
                 break;
             }
             if (!tree[node].expanded) {
-                if (expand(&tree[node], sim, pool + (size_t)node * GK_ACTIONS, &leaf_value, &evaluations) != 0) {
+                if (expand(&tree[node], sim, pool + (size_t)node * GK_ACTIONS, &leaf_value, &evaluations,
+                           node == 0 ? g_root_allow : NULL) != 0) {
                     status = -2;
                     goto done;
                 }
@@ -512,6 +522,81 @@ done:
     free(pool);
     free(path_node);
     free(path_edge);
+    return status;
+}
+
+/* Root tactical checks of the GPU search (python/kingdom_ai/gpu_puct.py:84-161).
+ * After the mover's action the opponent can win at once only by a second
+ * pass or by taking the last liberty of one of the mover's groups; each
+ * candidate reply is checked with the ordinary transition. */
+static int opponent_wins_next(const int32_t* next, int mover) {
+    const int opponent = next[GK_ACTOR];
+    int32_t reply[GK_STATE_WIDTH];
+    if (next[GK_PASSES] == 1) {
+        memcpy(reply, next, sizeof reply);
+        if (gko_play(reply, GK_PASS) && reply[GK_REASON] != GK_NONE && reply[GK_WINNER] == opponent) return 1;
+    }
+    if (next[opponent == 1 ? GK_BLACK_STOCK : GK_WHITE_STOCK] < 1) return 0;
+    unsigned char seen[GK_CELLS];
+    memset(seen, 0, sizeof seen);
+    int group[GK_CELLS];
+    for (int point = 0; point < GK_CELLS; ++point) {
+        if (next[point] != mover || seen[point]) continue;
+        const int length = collect_group(next, point, group);
+        int liberty = -1, several = 0;
+        for (int i = 0; i < length; ++i) {
+            seen[group[i]] = 1;
+            int nb[4];
+            const int count = nbrs(group[i], nb);
+            for (int j = 0; j < count; ++j) {
+                if (next[nb[j]] != 0) continue;
+                if (liberty < 0) liberty = nb[j];
+                else if (liberty != nb[j]) several = 1;
+            }
+        }
+        if (several || liberty < 0) continue;
+        memcpy(reply, next, sizeof reply);
+        if (gko_play(reply, liberty) && reply[GK_REASON] == GK_CAPTURE && reply[GK_WINNER] == opponent) return 1;
+    }
+    return 0;
+}
+
+/* outcome[a] = +1 (the mover wins at once), -1 (loses at once or the
+ * opponent can win with its next move), 0 otherwise or illegal; allow[a] =
+ * the legal actions narrowed to the wins if any, else to the safe ones if
+ * any, else all of them. */
+void gko_root_tactics(const int32_t* rec, int8_t* outcome, uint8_t* allow) {
+    int winning = 0, safe = 0;
+    for (int a = 0; a < GK_ACTIONS; ++a) {
+        outcome[a] = 0;
+        allow[a] = (uint8_t)gko_legal(rec, a);
+        if (!allow[a]) continue;
+        int32_t next[GK_STATE_WIDTH];
+        memcpy(next, rec, sizeof next);
+        gko_play(next, a);
+        if (next[GK_REASON] != GK_NONE) outcome[a] = next[GK_WINNER] == rec[GK_ACTOR] ? 1 : -1;
+        else if (opponent_wins_next(next, rec[GK_ACTOR])) outcome[a] = -1;
+        winning |= outcome[a] > 0;
+        safe |= outcome[a] >= 0;
+    }
+    for (int a = 0; a < GK_ACTIONS; ++a) {
+        if (winning) allow[a] = allow[a] && outcome[a] > 0;
+        else if (safe) allow[a] = allow[a] && outcome[a] >= 0;
+    }
+}
+
+/* The injected-evaluator search with the root narrowed by gko_root_tactics
+ * (uniform = 1: the uniform evaluator). */
+int gko_puct_search_tactics(const int32_t* rec, int simulations, double c_puct, int uniform, int32_t* visits,
+                            double* priors, int32_t* stats, double* values) {
+    int8_t outcome[GK_ACTIONS];
+    uint8_t allow[GK_ACTIONS];
+    gko_root_tactics(rec, outcome, allow);
+    g_root_allow = allow;
+    g_uniform_evaluator = uniform ? 1 : 0;
+    int status = gko_puct_search(rec, simulations, c_puct, visits, priors, stats, values);
+    g_uniform_evaluator = 0;
+    g_root_allow = NULL;
     return status;
 }
 

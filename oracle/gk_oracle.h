@@ -45,6 +45,12 @@ int gko_puct_search(const int32_t* rec, int simulations, double c_puct, int32_t*
 /* Same search with a uniform evaluator (all weights 1, value 0). */
 int gko_puct_search_uniform(const int32_t* rec, int simulations, double c_puct, int32_t* visits, double* priors,
                             int32_t* stats, double* values);
+/* Root tactical checks (python/kingdom_ai/gpu_puct.py:84-161): per action
+ * outcome +1 / -1 / 0 and the narrowed root candidates. */
+void gko_root_tactics(const int32_t* rec, int8_t* outcome, uint8_t* allow);
+/* The search above with the root narrowed by gko_root_tactics. */
+int gko_puct_search_tactics(const int32_t* rec, int simulations, double c_puct, int uniform, int32_t* visits,
+                            double* priors, int32_t* stats, double* values);
 int gko_puct_search_batch(const int32_t* recs, int64_t n, int simulations, double c_puct, int32_t* visits,
                           int32_t* best, double* root_values, int threads);
 

@@ -78,6 +78,8 @@ class Oracle:
         _bind(L, "gko_puct_search", [_i32p, _int, ctypes.c_double, _i32p, _f64p, _i32p, _f64p], _int)
         _bind(L, "gko_puct_search_uniform", [_i32p, _int, ctypes.c_double, _i32p, _f64p, _i32p, _f64p], _int)
         _bind(L, "gko_puct_search_batch", [_i32p, _i64, _int, ctypes.c_double, _i32p, _i32p, _f64p, _int], _int)
+        _bind(L, "gko_root_tactics", [_i32p, _i8p, _u8p])
+        _bind(L, "gko_puct_search_tactics", [_i32p, _int, ctypes.c_double, _int, _i32p, _f64p, _i32p, _f64p], _int)
 
     def initial(self, n: int = 1, neutral: int = 40) -> np.ndarray:
         recs = np.zeros((n, STATE_WIDTH), dtype=np.int32)
@@ -119,13 +121,26 @@ class Oracle:
         self.lib.gko_eval(np.ascontiguousarray(rec, dtype=np.int32), w, v)
         return w, float(v[0])
 
-    def puct(self, rec: np.ndarray, simulations: int, c_puct: float = 1.5, uniform: bool = False):
+    def root_tactics(self, rec: np.ndarray):
+        """Per-action outcome (+1 win, -1 loss or losing reply, 0) and the narrowed root candidates."""
+        outcome = np.zeros(ACTIONS, dtype=np.int8)
+        allow = np.zeros(ACTIONS, dtype=np.uint8)
+        self.lib.gko_root_tactics(np.ascontiguousarray(rec, dtype=np.int32), outcome, allow)
+        return outcome, allow.astype(bool)
+
+    def puct(self, rec: np.ndarray, simulations: int, c_puct: float = 1.5, uniform: bool = False,
+             tactics: bool = False):
         visits = np.zeros(ACTIONS, dtype=np.int32)
         priors = np.zeros(ACTIONS, dtype=np.float64)
         stats = np.zeros(4, dtype=np.int32)
         values = np.zeros(2, dtype=np.float64)
-        fn = self.lib.gko_puct_search_uniform if uniform else self.lib.gko_puct_search
-        status = fn(np.ascontiguousarray(rec, dtype=np.int32), simulations, c_puct, visits, priors, stats, values)
+        rec = np.ascontiguousarray(rec, dtype=np.int32)
+        if tactics:
+            status = self.lib.gko_puct_search_tactics(rec, simulations, c_puct, int(uniform), visits, priors, stats,
+                                                      values)
+        else:
+            fn = self.lib.gko_puct_search_uniform if uniform else self.lib.gko_puct_search
+            status = fn(rec, simulations, c_puct, visits, priors, stats, values)
         if status != 0:
             raise RuntimeError(f"oracle PUCT failed ({status})")
         return dict(visits=visits, priors=priors, best=int(stats[0]), simulations=int(stats[1]),

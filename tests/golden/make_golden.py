@@ -17,8 +17,14 @@ Fixtures
   positions.npz         generated mid-game positions with their encodings.
   puct.npz              root visits / priors / best move / root value of the
                         reference PUCT::search with the injected evaluator.
-  puct_uniform.npz      the reference PUCT with a uniform evaluator on the
-                        states of tests/gpu_puct_test.py:152-177.
+  tactics.npz           root positions of the reference's tactical-check tests
+                        (tests/gpu_puct_test.py:196-295) and generated
+                        positions, with each root action's outcome found by
+                        playing it and then every legal reply in the
+                        reference engine (+1 win, -1 loss or a winning reply
+                        for the opponent, 0 otherwise).
+
+Run with the argument ``tactics`` to write only tactics.npz.
 """
 
 from __future__ import annotations
@@ -90,6 +96,88 @@ def trajectory(ref, states, action_rows, encode_every=1):
                 masks=np.stack(masks).astype(np.uint8), encode_steps=np.asarray(enc_steps, dtype=np.int32))
 
 
+def transform(point, symmetry):
+    """tests/gpu_puct_test.py:35-41: the 8 board symmetries."""
+    row, col = point
+    if symmetry >= 4:
+        col = 8 - col
+    for _ in range(symmetry % 4):
+        row, col = col, 8 - row
+    return row, col
+
+
+def brute_outcomes(state):
+    """+1 / -1 / 0 per root action by exhaustive one-ply lookahead in the reference engine."""
+    rec = state.record()
+    actor = int(rec[162])
+    out = np.zeros(82, dtype=np.int8)
+    for a in state.legal():
+        nxt = state.copy()
+        assert nxt.play(a)
+        r = nxt.record()
+        if r[166] != 0:
+            out[a] = 1 if r[167] == actor else -1
+            continue
+        for b in nxt.legal():
+            reply = nxt.copy()
+            assert reply.play(b)
+            rr = reply.record()
+            if rr[166] != 0 and rr[167] == 3 - actor:
+                out[a] = -1
+                break
+    return out
+
+
+def tactics_fixture(ref):
+    from_board = lambda cells, to_play: RefState.from_board(ref, cells, to_play)  # noqa: E731
+    states, group, expected = [], [], []
+    # :196-229 a low-prior capture in every symmetry, for both colours
+    for actor in (BLACK, WHITE):
+        for sym in range(8):
+            own = tuple(transform(p, sym) for p in ((0, 1), (1, 0), (2, 1)))
+            other = (transform((1, 1), sym),)
+            cells = board(own, other) if actor == BLACK else board(other, own)
+            states.append(from_board(cells, actor))
+            group.append(0)
+            r, c = transform((1, 2), sym)
+            expected.append(r * 9 + c)
+    # :231-259 the one safe reply after a reported opening, in every symmetry
+    opening = [(4, 8), (5, 8), (2, 8), (6, 8), (2, 4), (4, 4), (6, 2), (4, 7), (3, 7), (5, 9), (4, 6)]
+    for sym in range(8):
+        s = RefState.initial(ref, 40)
+        for row, col in opening:
+            r, c = transform((row - 1, col - 1), sym)
+            assert s.play(r * 9 + c)
+        states.append(s)
+        group.append(1)
+        r, c = transform((4, 6), sym)
+        expected.append(r * 9 + c)
+    # :261-295 suicide, simultaneous capture, pass win, pass loss, no safe move
+    suicide = from_board(board(((0, 1), (6, 7), (7, 6), (8, 7)),
+                               ((0, 0), (0, 2), (1, 0), (1, 2), (2, 1), (7, 7))), BLACK)
+    capture = from_board(board(((0, 6), (1, 6), (1, 8), (2, 7)), ((0, 7), (1, 7), (2, 8))), BLACK)
+    white_pass_win = RefState.initial(ref, 40)
+    assert white_pass_win.play(81)
+    black_pass_loss = from_board(board(neutral=(4, 4)), WHITE)
+    assert black_pass_loss.play(81)
+    full = np.asarray([BLACK] * 41 + [WHITE] * 40, dtype=np.int32)
+    forced_loss = from_board(full, WHITE)
+    assert forced_loss.play(81)
+    for s, e in ((suicide, -1), (capture, 8), (white_pass_win, 81), (black_pass_loss, -1), (forced_loss, 81)):
+        states.append(s)
+        group.append(2)
+        expected.append(e)
+    # generated mid-game positions
+    for i in range(48):
+        states.append(RefState.generated(ref, 23, i))
+        group.append(3)
+        expected.append(-1)
+    roots = np.stack([s.record() for s in states]).astype(np.int32)
+    outcomes = np.stack([brute_outcomes(s) for s in states])
+    return dict(roots=roots, group=np.asarray(group, np.int32), expected=np.asarray(expected, np.int32),
+                outcomes=outcomes)
+
+
 def save(name, data):
     np.savez_compressed(HERE / name, **data)
     print(name, {k: v.shape for k, v in data.items()})
@@ -97,6 +185,9 @@ def save(name, data):
 
 def main():
     ref = Reference()
+    if len(sys.argv) > 1 and sys.argv[1] == "tactics":
+        save("tactics.npz", tactics_fixture(ref))
+        return
     from_board = lambda cells, to_play: RefState.from_board(ref, cells, to_play)  # noqa: E731
 
     # tests/gpu_rules_test.py:137-148 (initial variants)
@@ -208,6 +299,7 @@ def main():
         values[i] = (r["root_value"], r["best_value"])
     save("puct.npz", dict(seed=np.asarray([5]), simulations=np.asarray([sims]), roots=roots, visits=visits,
                           priors=priors, stats=stats, values=values))
+    save("tactics.npz", tactics_fixture(ref))
 
 
 if __name__ == "__main__":

@@ -107,3 +107,39 @@ def test_injected_evaluator_is_a_pure_function(oracle, golden):
     # Approximately standard-normal logits: log-weights have mean ~0, sd ~1.
     logs = np.log(np.concatenate([oracle.evaluate(r)[0] for r in golden("positions.npz")["records"]]))
     assert abs(logs.mean()) < 0.1 and abs(logs.std() - 1.0) < 0.1
+
+
+def test_oracle_root_tactics_match_reference_engine_lookahead(oracle, golden):
+    """Root tactical checks (gpu_puct.py:84-161) against the reference engine:
+    each root action played, then every legal reply, in the compiled
+    reference (tests/golden/tactics.npz)."""
+    g = golden("tactics.npz")
+    for rec, expected in zip(g["roots"], g["outcomes"]):
+        outcome, allow = oracle.root_tactics(rec)
+        legal = np.asarray([oracle.lib.gko_legal(rec, a) for a in range(82)], dtype=bool)
+        assert np.array_equal(outcome[legal], expected[legal])
+        winning, safe = (expected[legal] > 0).any(), (expected[legal] >= 0).any()
+        keep = expected > 0 if winning else expected >= 0 if safe else np.ones(82, bool)
+        assert np.array_equal(allow, legal & keep)
+
+
+def test_oracle_tactical_search_known_answers(oracle, golden):
+    """The expectations of the reference's tactical-check tests
+    (tests/gpu_puct_test.py:196-295) with the oracle's search."""
+    g = golden("tactics.npz")
+    for rec, group, expected in zip(g["roots"], g["group"], g["expected"]):
+        if group > 1:
+            continue
+        r = oracle.puct(rec, 8, uniform=True, tactics=True)
+        assert r["best"] == expected and r["visits"][expected] == 8
+    cases = [i for i, grp in enumerate(g["group"]) if grp == 2]
+    suicide, capture, pass_win, pass_loss, forced = (g["roots"][i] for i in cases)
+    r = oracle.puct(suicide, 8, uniform=True, tactics=True)
+    assert r["visits"][10] == 0 and r["priors"][10] == 0.0
+    r = oracle.puct(capture, 8, uniform=True, tactics=True)
+    assert r["best"] == 8 and r["best_value"] == 1.0
+    r = oracle.puct(pass_win, 8, uniform=True, tactics=True)
+    assert r["best"] == 81 and r["best_value"] == 1.0
+    assert oracle.puct(pass_loss, 8, uniform=True, tactics=True)["visits"][81] == 0
+    r = oracle.puct(forced, 8, uniform=True, tactics=True)
+    assert r["best"] == 81 and r["best_value"] == -1.0
