@@ -819,6 +819,8 @@ struct HeadOut {
     float* policy;       // search mode: [B][82] masked softmax, row index[i]
     float* leaf_value;   // search mode: [B]
     const gk_bits* states;  // search mode: leaf states for the legal mask
+    const int32_t* leaf;    // search mode: [B] leaf node (0: the root, masked by root_allow too)
+    const uint32_t* root_allow;  // search mode: [B][3] root candidates
 };
 
 constexpr int kPolStride = 163;  // odd row stride: conflict-free lane-per-row reads
@@ -938,7 +940,8 @@ __global__ void __launch_bounds__(32 * kHeadWarps) net_heads_kernel(NetParams p,
 #pragma unroll
                 for (int k = 0; k < 3; ++k) {
                     const int a = lane + 32 * k;
-                    legal[k] = a < GK_ACTIONS && (a == GK_PASS ? true : gk_test(placements, a + a / 9) != 0);
+                    legal[k] = a < GK_ACTIONS && (a == GK_PASS ? true : gk_test(placements, a + a / 9) != 0) &&
+                               (out.leaf[tree] != 0 || ((out.root_allow[tree * 3 + k] >> lane) & 1u) != 0u);
                     if (legal[k]) mx = fmaxf(mx, logit[k]);
                 }
 #pragma unroll
@@ -1099,7 +1102,7 @@ int net_evaluate(const gk_net_t* net, void* ws, int64_t batch, int capacity, flo
     PuctView v;
     puct_layout(ws, batch, capacity, &v);
     NetInput in{v.leaf_bits, nullptr, v.active, v.active_count, batch};
-    HeadOut out{nullptr, nullptr, v.policy, v.leaf_value, v.leaf_bits};
+    HeadOut out{nullptr, nullptr, v.policy, v.leaf_value, v.leaf_bits, v.leaf, v.root_allow};
     return run_forward(net, in, headfeat, out, status, stream, tower_start, tower_stop);
 }
 
@@ -1135,7 +1138,7 @@ int gk_net_forward(const gk_net_t* net, const uint32_t* states, const float* fea
         return GK_EINVAL;
     if (n == 0) return 0;
     NetInput in{reinterpret_cast<const gk_bits*>(states), features, nullptr, nullptr, n};
-    HeadOut out{logits, values, nullptr, nullptr, nullptr};
+    HeadOut out{logits, values, nullptr, nullptr, nullptr, nullptr, nullptr};
     return run_forward(net, in, headfeat, out, status, as_stream(stream));
 }
 

@@ -34,6 +34,13 @@ __device__ __forceinline__ bool action_legal(const gk_b96& placements, bool pass
     return a == GK_PASS ? pass_ok : gk_test(placements, a + a / 9) != 0;
 }
 
+// This lane's root-candidate bits for actions lane, lane+32, lane+64 of tree
+// t's node `node`: the root's words, all ones elsewhere.
+__device__ __forceinline__ void allow_bits(const PuctView& v, int64_t t, int node, int lane, bool (&ok)[3]) {
+#pragma unroll
+    for (int k = 0; k < 3; ++k) ok[k] = node != 0 || ((v.root_allow[t * 3 + k] >> lane) & 1u) != 0u;
+}
+
 __device__ __forceinline__ float terminal_value(const gk_bits& s) {
     return gk_winner(&s) == gk_actor(&s) ? 1.0f : -1.0f;
 }
@@ -69,6 +76,9 @@ __global__ void puct_begin_kernel(PuctView v, int64_t B, int C, const gk_bits* r
         v.needs_eval[t] = live ? 1 : 0;
         v.leaf_bits[t] = r;
         v.leaf_value[t] = live ? 0.0f : terminal_value(r);
+        v.root_allow[t * 3] = 0xffffffffu;
+        v.root_allow[t * 3 + 1] = 0xffffffffu;
+        v.root_allow[t * 3 + 2] = (1u << (GK_ACTIONS - 64)) - 1u;
     }
 }
 
@@ -120,12 +130,14 @@ __device__ __forceinline__ void select_tree(const PuctView& v, int64_t t, int C,
         }
         const double scale = sqrt((double)node_n);
         const gk_b96 placements = legal_placements(st);
+        bool allowed[3];
+        allow_bits(v, t, node, lane, allowed);
         int best = -1;
         double best_score = 0.0, best_prior = 0.0;
 #pragma unroll
         for (int k = 0; k < 3; ++k) {
             const int a = lane + 32 * k;
-            if (a >= GK_ACTIONS || !action_legal(placements, true, a)) continue;
+            if (a >= GK_ACTIONS || !allowed[k] || !action_legal(placements, true, a)) continue;
             const int n = en[k];
             const double p = ep[k];
             double q;
@@ -223,6 +235,8 @@ __device__ __forceinline__ void expand_backup_tree(const PuctView& v, int64_t t,
     if (v.needs_eval[t]) {
         const gk_b96 placements = legal_placements(st);
         const int64_t ebase = vtx * GK_ACTIONS, row = t * GK_ACTIONS;
+        bool allowed[3];
+        allow_bits(v, t, node, lane, allowed);
         bool bad = !(isfinite(leaf_value) && fabsf(leaf_value) <= 1.0f);
         bool use[3];
         double w[3], nz[3];
@@ -231,7 +245,7 @@ __device__ __forceinline__ void expand_backup_tree(const PuctView& v, int64_t t,
 #pragma unroll
         for (int k = 0; k < 3; ++k) {
             const int a = lane + 32 * k;
-            use[k] = a < GK_ACTIONS && action_legal(placements, true, a);
+            use[k] = a < GK_ACTIONS && allowed[k] && action_legal(placements, true, a);
             w[k] = 0.0;
             nz[k] = 0.0;
             if (use[k]) {
@@ -374,6 +388,8 @@ __global__ void __launch_bounds__(32 * kWarpsPerBlock) puct_finish_kernel(PuctVi
     const int sims = v.sims[t];
     const gk_b96 placements = legal_placements(root);
     const bool expanded = v.expanded[vtx] != 0;
+    bool allowed[3];
+    allow_bits(v, t, 0, lane, allowed);
     bool use[3];
     double ws[3];
     int best = -1, best_n = 0;
@@ -381,7 +397,7 @@ __global__ void __launch_bounds__(32 * kWarpsPerBlock) puct_finish_kernel(PuctVi
 #pragma unroll
     for (int k = 0; k < 3; ++k) {
         const int a = lane + 32 * k;
-        use[k] = expanded && a < GK_ACTIONS && action_legal(placements, true, a);
+        use[k] = expanded && a < GK_ACTIONS && allowed[k] && action_legal(placements, true, a);
         ws[k] = 0.0;
         if (a >= GK_ACTIONS) continue;
         const int n = expanded ? v.visits[ebase + a] : 0;
@@ -468,12 +484,80 @@ __global__ void __launch_bounds__(32 * kWarpsPerBlock, 8) puct_search_hash_kerne
     }
 }
 
+// ---- root tactical checks ----------------------------------------------------
+// GpuPUCT's tactical_checks (python/kingdom_ai/gpu_puct.py:84-161): each legal
+// root action is played; an action that ends the game is a win (+1) or a
+// loss (-1) for the mover, and one after which the opponent can win with its
+// next move is a loss too. The opponent can win at once only by a second
+// pass or by taking the last liberty of one of the mover's groups, so only
+// those replies are tried, each with the ordinary transition. The root then
+// keeps its winning actions if it has any, else its safe ones if it has any,
+// else all of them.
+
+// True when the player to move in `next` can win with one move against `mover`.
+__device__ bool opponent_wins_next(const gk_bits& next, int mover) {
+    const int opponent = gk_actor(&next);
+    if (gk_passes(&next) == 1) {
+        gk_bits reply = next;
+        if (play(reply, GK_PASS) && gk_reason(&reply) != GK_NONE && gk_winner(&reply) == opponent) return true;
+    }
+    if (gk_stock(&next, opponent) < 1) return false;
+    const gk_b96 own = gk_get(&next, mover == 1 ? GK_PLANE_BLACK : GK_PLANE_WHITE);
+    const gk_b96 empty = empty_cells(next);
+    gk_b96 pending = own;
+    while (gk_any(pending)) {
+        const gk_b96 group = gk_flood(own, lowest_bit(pending));
+        pending = gk_andnot(pending, group);
+        const gk_b96 libs = gk_and(gk_neighbours(group), empty);
+        if (gk_popc(libs) != 1) continue;
+        const int bit = libs.w[0] ? __ffs(libs.w[0]) - 1 : libs.w[1] ? 31 + __ffs(libs.w[1]) : 63 + __ffs(libs.w[2]);
+        gk_bits reply = next;
+        if (play(reply, gk_bit_cell(bit)) && gk_reason(&reply) == GK_CAPTURE && gk_winner(&reply) == opponent)
+            return true;
+    }
+    return false;
+}
+
+// One warp per tree; lane l judges actions l, l+32, l+64 of the root.
+__global__ void __launch_bounds__(32 * kWarpsPerBlock) puct_root_tactics_kernel(PuctView v, int64_t B, int C) {
+    const int lane = threadIdx.x & 31;
+    const int64_t t = (blockIdx.x * (int64_t)blockDim.x + threadIdx.x) >> 5;
+    if (t >= B || v.node_count[t] == 0) return;  // a finished root has no candidates
+    const gk_bits root = v.node_state[t * C];
+    const int mover = gk_actor(&root);
+    const gk_b96 placements = legal_placements(root);
+    bool cand[3];
+    int outcome[3];
+    bool win = false, safe = false;
+#pragma unroll
+    for (int k = 0; k < 3; ++k) {
+        const int a = lane + 32 * k;
+        cand[k] = a < GK_ACTIONS && action_legal(placements, true, a);
+        outcome[k] = 0;
+        if (!cand[k]) continue;
+        gk_bits next = root;
+        play(next, a);
+        if (gk_reason(&next) != GK_NONE) outcome[k] = gk_winner(&next) == mover ? 1 : -1;
+        else if (opponent_wins_next(next, mover)) outcome[k] = -1;
+        win |= outcome[k] > 0;
+        safe |= outcome[k] >= 0;
+    }
+    win = __any_sync(kFull, win);
+    safe = __any_sync(kFull, safe);
+#pragma unroll
+    for (int k = 0; k < 3; ++k) {
+        const bool keep = cand[k] && (win ? outcome[k] > 0 : safe ? outcome[k] >= 0 : true);
+        const uint32_t word = __ballot_sync(kFull, keep);
+        if (lane == 0) v.root_allow[t * 3 + k] = word;
+    }
+}
+
 // ---- root Dirichlet noise ---------------------------------------------------
 // Stream per tree: PCG32 (seed, stream_base + tree); draws in gk_random.cuh.
 __global__ void puct_noise_kernel(PuctView v, int64_t B, int C, uint64_t seed, uint64_t stream_base, double alpha) {
     for (int64_t t = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; t < B; t += (int64_t)gridDim.x * blockDim.x) {
         gk_pcg32 r = gk_pcg32_seed(seed, stream_base + (uint64_t)t);
-        root_noise(v.node_state[t * C], alpha, r, v.noise + t * GK_ACTIONS);
+        root_noise(v.node_state[t * C], alpha, r, v.noise + t * GK_ACTIONS, v.root_allow + t * 3);
     }
 }
 
@@ -566,7 +650,17 @@ int gk_puct_buffers(void* ws, int64_t batch, int capacity, gk_puct_buffers_t* ou
     out->active = v.active;
     out->active_count = v.active_count;
     out->errors = v.errors;
+    out->leaf = v.leaf;
+    out->root_allow = v.root_allow;
     return 0;
+}
+
+int gk_puct_root_tactics(void* ws, int64_t batch, int capacity, void* stream) {
+    if (!valid_ws(ws, batch, capacity)) return GK_EINVAL;
+    PuctView v;
+    puct_layout(ws, batch, capacity, &v);
+    puct_root_tactics_kernel<<<warp_grid(batch), 32 * kWarpsPerBlock, 0, as_stream(stream)>>>(v, batch, capacity);
+    return launch_status();
 }
 
 int gk_puct_begin(void* ws, int64_t batch, int capacity, const uint32_t* root_bits, void* stream) {

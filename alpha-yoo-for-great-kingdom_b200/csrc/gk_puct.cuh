@@ -43,6 +43,9 @@ struct PuctView {
     float* noise;          // [B*82] root noise (max-normalised gamma draws)
     int32_t* active;       // [B] compacted indices of trees needing evaluation
     int32_t* active_count; // [1]
+    // root candidates: bit (a & 31) of word a >> 5 is set when the root may
+    // choose action a (all actions after begin; narrowed by the tactical checks)
+    uint32_t* root_allow;  // [B*3]
 };
 
 constexpr int kPathCap = GK_MAX_PLIES + 4;  // a path never exceeds the game length
@@ -85,6 +88,7 @@ inline size_t puct_layout(void* base, int64_t B, int C, PuctView* v) {
     t.noise = (float*)take(B * GK_ACTIONS * 4);
     t.active = (int32_t*)take(B * 4);
     t.active_count = (int32_t*)take(4);
+    t.root_allow = (uint32_t*)take(B * 3 * 4);
     if (v) *v = t;
     return off;
 }

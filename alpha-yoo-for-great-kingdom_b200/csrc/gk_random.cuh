@@ -40,10 +40,11 @@ __device__ inline double gamma_draw(double alpha, gk_pcg32& r) {
     return d * boost;
 }
 
-// Max-normalised gamma draws over the legal actions of `root` into out[82]
-// (0 for illegal actions), as GpuPUCT._search prepares them
-// (python/kingdom_ai/gpu_puct.py:509-517).
-__device__ inline void root_noise(const gk_bits& root, double alpha, gk_pcg32& r, float* out) {
+// Max-normalised gamma draws over the legal actions of `root` that `allow`
+// keeps (bit a & 31 of allow[a >> 5]) into out[82] (0 for the others), as
+// GpuPUCT._search prepares them (python/kingdom_ai/gpu_puct.py:509-517).
+__device__ inline void root_noise(const gk_bits& root, double alpha, gk_pcg32& r, float* out,
+                                  const uint32_t* allow = nullptr) {
     const bool live = gk_reason(&root) == GK_NONE;
     gk_b96 placements = gk_b(0u, 0u, 0u);
     if (live && gk_stock(&root, gk_actor(&root)) > 0) {
@@ -56,7 +57,8 @@ __device__ inline void root_noise(const gk_bits& root, double alpha, gk_pcg32& r
     double largest = 0.0;
     for (int a = 0; a < GK_ACTIONS; ++a) {
         g[a] = 0.0;
-        const bool legal = live && (a == GK_PASS || gk_test(placements, a + a / 9));
+        const bool legal = live && (a == GK_PASS || gk_test(placements, a + a / 9)) &&
+                           (allow == nullptr || ((allow[a >> 5] >> (a & 31)) & 1u) != 0u);
         if (legal) {
             double x = gamma_draw(alpha, r);
             if (!isfinite(x) || x < 0.0) x = 0.0;

@@ -90,7 +90,7 @@ __global__ void selfplay_reset_kernel(SelfPlayView v, int64_t B, int neutral, ui
 __global__ void selfplay_noise_kernel(SelfPlayView v, PuctView p, int64_t B, int C, uint64_t seed, double alpha) {
     for (int64_t b = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; b < B; b += (int64_t)gridDim.x * blockDim.x) {
         gk_pcg32 r = gk_pcg32_seed(seed ^ kNoiseSalt, v.game_id[b] * 256u + (uint64_t)v.lane_ply[b]);
-        root_noise(p.node_state[b * C], alpha, r, p.noise + b * GK_ACTIONS);
+        root_noise(p.node_state[b * C], alpha, r, p.noise + b * GK_ACTIONS, p.root_allow + b * 3);
     }
 }
 
@@ -352,6 +352,7 @@ int gk_selfplay_ply(void* sp_ws, void* puct_ws, int64_t lanes, const gk_net_t* n
     gk_puct_options o{prm->c_puct, prm->dirichlet_epsilon, prm->fpu_enabled, prm->fpu_reduction};
     int s = gk_puct_begin(puct_ws, lanes, C, reinterpret_cast<const uint32_t*>(v.states), stream);
     if (s) return s;
+    if (prm->tactical_checks && (s = gk_puct_root_tactics(puct_ws, lanes, C, stream))) return s;
     if ((s = evaluate())) return s;
     if (prm->dirichlet_epsilon != 0.0) {
         selfplay_noise_kernel<<<blocks_for(lanes, 128, kSmCount * 8), 128, 0, st>>>(v, pv, lanes, C, prm->seed,

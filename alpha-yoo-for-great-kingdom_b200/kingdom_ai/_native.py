@@ -33,7 +33,7 @@ class PuctOptions(ctypes.Structure):
 class PuctBuffers(ctypes.Structure):
     _fields_ = [("needs_eval", c_void_p), ("leaf_bits", c_void_p), ("leaf_value", c_void_p),
                 ("policy", c_void_p), ("noise", c_void_p), ("active", c_void_p), ("active_count", c_void_p),
-                ("errors", c_void_p)]
+                ("errors", c_void_p), ("leaf", c_void_p), ("root_allow", c_void_p)]
 
 
 class PuctResults(ctypes.Structure):
@@ -62,6 +62,7 @@ _SIGNATURES = {
     "gk_gen_positions": [c_uint64, c_uint64, c_int64, c_void_p, c_void_p],
     "gk_puct_buffers": [c_void_p, c_int64, c_int, ctypes.POINTER(PuctBuffers)],
     "gk_puct_begin": [c_void_p, c_int64, c_int, c_void_p, c_void_p],
+    "gk_puct_root_tactics": [c_void_p, c_int64, c_int, c_void_p],
     "gk_puct_noise": [c_void_p, c_int64, c_int, c_uint64, c_uint64, c_double, c_void_p],
     "gk_puct_select": [c_void_p, c_int64, c_int, ctypes.POINTER(PuctOptions), c_void_p],
     "gk_puct_hash_eval": [c_void_p, c_int64, c_int, c_void_p],

@@ -93,7 +93,8 @@ class HashEvaluator:
 class SearchWorkspace:
     """One device allocation holding every tree array of a batched search."""
 
-    _FIELDS = ("needs_eval", "leaf_bits", "leaf_value", "policy", "noise", "active", "active_count", "errors")
+    _FIELDS = ("needs_eval", "leaf_bits", "leaf_value", "policy", "noise", "active", "active_count", "errors",
+               "leaf", "root_allow")
 
     def __init__(self, batch: int, capacity: int, device: torch.device):
         lib = native.library()
@@ -119,6 +120,14 @@ class SearchWorkspace:
         self.active = view(buffers.active, batch, torch.int32, (batch,))
         self.active_count = view(buffers.active_count, 1, torch.int32, (1,))
         self.errors = view(buffers.errors, batch, torch.int32, (batch,))
+        self.leaf = view(buffers.leaf, batch, torch.int32, (batch,))
+        self.root_allow = view(buffers.root_allow, batch * 3, torch.int32, (batch, 3))
+
+    def root_masks(self, rows: torch.Tensor) -> torch.Tensor:
+        """bool [len(rows), 82]: the root candidates of the given trees."""
+        actions = torch.arange(ACTION_SIZE, device=rows.device)
+        words = self.root_allow.index_select(0, rows)[:, actions // 32]
+        return ((words >> (actions % 32)) & 1).bool()
 
     @property
     def pointer(self):
@@ -219,6 +228,11 @@ class GpuPUCT:
         if active.numel() == 0:
             return
         features, masks = encode_packed(ws.leaf_bits.index_select(0, active))
+        if self.options.tactical_checks:
+            # A root leaf's mask is its tactically narrowed candidate set
+            # (gpu_puct.py:475-479, 499); the features keep rule legality.
+            at_root = ws.leaf.index_select(0, active) == 0
+            masks = torch.where(at_root[:, None], masks & ws.root_masks(active), masks)
         logits, values = self.model(features)
         if logits.shape != (active.numel(), ACTION_SIZE) or values.shape != (active.numel(),):
             raise ValueError("model must return logits [N, 82] and values [N]")
@@ -236,8 +250,6 @@ class GpuPUCT:
         batch = roots.shape[0]
         if batch < 1:
             raise ValueError("Search needs at least one state")
-        if self.options.tactical_checks:
-            raise NotImplementedError("tactical_checks is not available in this engine yet")
         capacity = self.options.simulations + 1
         device = self.device
         ws = self._workspace_for(batch, capacity)
@@ -245,6 +257,8 @@ class GpuPUCT:
         opts = self._options_struct()
         stream = _launch_scope(device, roots, ws.storage)
         native.call("gk_puct_begin", ws.pointer, batch, capacity, native.ptr(roots), stream)
+        if self.options.tactical_checks:
+            native.call("gk_puct_root_tactics", ws.pointer, batch, capacity, stream)
         self._evaluate(ws, stream)
         if self.options.dirichlet_epsilon:
             native.call("gk_puct_noise", ws.pointer, batch, capacity, self._seed & (2**64 - 1),

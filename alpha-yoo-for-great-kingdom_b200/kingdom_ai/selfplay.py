@@ -32,7 +32,8 @@ class SelfPlayParams(ctypes.Structure):
                 ("dirichlet_epsilon", ctypes.c_double), ("fpu_enabled", ctypes.c_int),
                 ("fpu_reduction", ctypes.c_double), ("temperature_moves", ctypes.c_int),
                 ("temperature", ctypes.c_double), ("final_temperature", ctypes.c_double),
-                ("seed", ctypes.c_uint64), ("game_stride", ctypes.c_uint64), ("neutral_cell", ctypes.c_int)]
+                ("seed", ctypes.c_uint64), ("game_stride", ctypes.c_uint64), ("neutral_cell", ctypes.c_int),
+                ("tactical_checks", ctypes.c_int)]
 
 
 class ReplayStruct(ctypes.Structure):
@@ -123,8 +124,6 @@ class SelfPlayEngine:
         lib = _bind()
         self.device = native.require_cuda(device)
         self.options = options or GpuPUCTOptions()
-        if self.options.tactical_checks:
-            raise NotImplementedError("tactical_checks is not available in this engine yet")
         self.lanes = int(lanes)
         self.net = model if isinstance(model, NativePolicyValueNet) else NativePolicyValueNet(model, self.device)
         seed = self.options.seed if seed is None else seed
@@ -134,7 +133,8 @@ class SelfPlayEngine:
             float(self.options.dirichlet_epsilon), 1 if self.options.fpu_reduction is not None else 0,
             float(self.options.fpu_reduction or 0.0),
             self.options.simulations + 10**9 if temperature_moves is None else int(temperature_moves),
-            float(temperature), float(final_temperature), seed & (2**64 - 1), world_size * self.lanes, neutral_cell)
+            float(temperature), float(final_temperature), seed & (2**64 - 1), world_size * self.lanes, neutral_cell,
+            1 if self.options.tactical_checks else 0)
         self.first_game = rank * self.lanes
         self.neutral_cell = neutral_cell
         nbytes = lib.gk_selfplay_workspace_bytes(self.lanes)

@@ -116,6 +116,8 @@ typedef struct {
     int32_t* active;       /* [B] compacted tree indices (gk_puct_compact) */
     int32_t* active_count; /* [1] */
     uint32_t* errors;      /* [B] GK_ERR_* per tree */
+    int32_t* leaf;         /* [B] node of the leaf to evaluate (0: the root) */
+    uint32_t* root_allow;  /* [B,3] root candidates: bit a%32 of word a/32 (all after gk_puct_begin) */
 } gk_puct_buffers_t;
 
 /* Search outputs (GpuSearchResult, gpu_puct.py:66-76); any pointer may be
@@ -145,6 +147,14 @@ GK_API int gk_puct_buffers(void* ws, int64_t batch, int capacity, gk_puct_buffer
 /* Reset the trees at the given packed roots. Replaces gpu_search_initialize
  * (gpu_puct.py:163-180). */
 GK_API int gk_puct_begin(void* ws, int64_t batch, int capacity, const uint32_t* root_bits, void* stream);
+
+/* Root tactical checks: narrow each root's candidate actions to the ones that
+ * win at once if there are any, else to those after which the opponent has
+ * no winning reply if there are any (else all stay). Call after gk_puct_begin
+ * and before the root's evaluation; select, expand, noise, finish and the
+ * native evaluator then honour the candidates. Replaces gpu_search_root_tactics
+ * and gpu_search_root_filter (gpu_puct.py:84-161, launched at :475-479). */
+GK_API int gk_puct_root_tactics(void* ws, int64_t batch, int capacity, void* stream);
 
 /* Root Dirichlet noise over each root's legal actions, max-normalised, from
  * PCG32 stream (seed, stream_base + tree). Replaces the torch._standard_gamma
@@ -281,6 +291,7 @@ typedef struct {
     uint64_t seed;            /* root noise and move sampling */
     uint64_t game_stride;     /* game-id step when a lane starts its next game */
     int neutral_cell;         /* start position's neutral stone, -1 for none */
+    int tactical_checks;      /* nonzero: gk_puct_root_tactics at every root (GpuPUCTOptions.tactical_checks) */
 } gk_selfplay_params_t;
 
 /* FIFO replay ring in the CPU ReplayBuffer's row schema
