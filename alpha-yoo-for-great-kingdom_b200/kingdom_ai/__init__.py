@@ -11,4 +11,5 @@ from .gpu_rules import (  # noqa: F401
     GPU_WINNER, GpuStateBatch,
 )
 from .gpu_puct import GpuPUCT, GpuPUCTOptions, GpuSearchResult, HashEvaluator  # noqa: F401
-from .training import Cell, EndReason, GameData, TrainingSample, collect_gpu_puct_games  # noqa: F401
+from .training import Cell, EndReason, GameData, TrainingBatch, TrainingSample, collect_gpu_puct_games  # noqa: F401
+from .replay import DeviceReplayBuffer, validate_rows  # noqa: F401

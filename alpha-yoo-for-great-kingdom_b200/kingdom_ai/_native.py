@@ -63,6 +63,7 @@ _SIGNATURES = {
     "gk_puct_buffers": [c_void_p, c_int64, c_int, ctypes.POINTER(PuctBuffers)],
     "gk_puct_begin": [c_void_p, c_int64, c_int, c_void_p, c_void_p],
     "gk_puct_root_tactics": [c_void_p, c_int64, c_int, c_void_p],
+    "gk_replay_validate": [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_int64, c_void_p, c_void_p],
     "gk_puct_noise": [c_void_p, c_int64, c_int, c_uint64, c_uint64, c_double, c_void_p],
     "gk_puct_select": [c_void_p, c_int64, c_int, ctypes.POINTER(PuctOptions), c_void_p],
     "gk_puct_hash_eval": [c_void_p, c_int64, c_int, c_void_p],

@@ -59,6 +59,15 @@ class TrainingSample:
 
 
 @dataclass(frozen=True)
+class TrainingBatch:
+    """A sampled minibatch (python/kingdom_ai/training.py:33-38)."""
+    features: torch.Tensor    # float32 [N,10,9,9]
+    legal_mask: torch.Tensor  # bool [N,82]
+    policy: torch.Tensor      # float32 [N,82]
+    value: torch.Tensor       # float32 [N]
+
+
+@dataclass(frozen=True)
 class GameData:
     samples: list
     winner: Cell

@@ -267,7 +267,8 @@ def main():
     parser.add_argument("--impl", choices=["ours", "reference"], default="ours")
     parser.add_argument("--e2e-steps", type=int, default=3)
     parser.add_argument("--no-cpu-baseline", action="store_true")
-    parser.add_argument("--workload", choices=["selfplay", "network", "rules", "encode", "puct"], default="selfplay",
+    parser.add_argument("--workload", choices=["selfplay", "network", "rules", "encode", "puct", "replay"],
+                        default="selfplay",
                         help="selfplay is the headline; the others time one kernel family each")
     parser.add_argument("--net", default="128x10", help="network workload: CHANNELSxBLOCKS")
     parser.add_argument("--batch", type=int, default=8192, help="network workload batch")
@@ -275,6 +276,7 @@ def main():
     parser.add_argument("--positions", type=int, default=65536, help="encode workload: positions")
     parser.add_argument("--trees", type=int, default=1024, help="puct workload: trees")
     parser.add_argument("--sims", type=int, default=800, help="puct workload: simulations per tree")
+    parser.add_argument("--rows", type=int, default=1 << 20, help="replay workload: rows validated per launch")
     args = parser.parse_args()
     if args.impl == "reference":
         reference_arm(args)

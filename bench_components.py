@@ -4,6 +4,7 @@
     rules    4096 uniform-random complete playouts, and one transition of 2^22 packed states
     encode   observation planes + legal masks for 65,536 and 2^20 generated positions
     puct     1024 trees x 800 simulations with the injected evaluator
+    replay   replay-row checks of DeviceReplayBuffer ingest on 2^20 rows (3.66 GB)
 
 Every timed launch is bracketed by CUDA events on the launching stream; an L2
 flush (a 256 MB write) separates timed launches so each one reads its inputs
@@ -165,3 +166,54 @@ def bench_puct(args, peaks):
     emit({"workload": f"PUCT {n} trees x {sims} simulations, injected evaluator, c_puct 1.5", "metric": "simulations/s",
           "value": n * sims / (ms / 1e3), "unit": "simulations/s", "ms_per_search": ms,
           "nodes_mean": float(r.nodes.float().mean().item())})
+
+
+def bench_replay(args, peaks):
+    """gk_replay_validate over `--rows` valid replay rows (the reference's
+    ReplayBuffer ingest checks, replay.py:35-74); CPU baseline: the numpy
+    restatement of the same checks on a bounded sample, one thread."""
+    import time
+
+    import numpy as np
+
+    device = torch.device("cuda", 0)
+    flush = Flusher(device)
+    stream = native.stream_of(device)
+    n = args.rows
+    bits = positions(n, 29, device)
+    feats = torch.empty((n, 10, 9, 9), dtype=torch.float32, device=device)
+    masks = torch.empty((n, 82), dtype=torch.bool, device=device)
+    native.call("gk_encode_bits", native.ptr(bits), native.ptr(feats), native.ptr(masks), n, stream)
+    del bits
+    policy = masks.float() / masks.sum(dim=1, keepdim=True).float()
+    value = torch.where(torch.arange(n, device=device) % 3 == 0, 1.0, -1.0).float()
+    to_play = torch.where(feats[:, 5, 0, 0] == 1.0, 1, 2).to(torch.int8)
+    flags = torch.zeros(1, dtype=torch.int32, device=device)
+    args_ = (native.ptr(feats), native.ptr(masks), native.ptr(policy), native.ptr(value), native.ptr(to_play), n,
+             native.ptr(flags), stream)
+    ms = timed(lambda: native.call("gk_replay_validate", *args_), args.steps, args.warmup, flush)
+    assert int(flags.item()) == 0, "generated rows must be valid"
+    row_bytes = 3240 + 82 + 328 + 4 + 1
+    gbs = n * row_bytes / (ms / 1e3) / 1e9
+    cpu = None
+    try:
+        from oracle.oracle import replay_violation
+        m = min(n, 1 << 16)
+        host = [t[:m].cpu().numpy() for t in (feats, masks, policy, value, to_play)]
+        start = time.perf_counter()
+        reps = 0
+        while True:
+            assert replay_violation(*host) is None
+            reps += 1
+            if time.perf_counter() - start > 10.0:
+                break
+        elapsed = time.perf_counter() - start
+        cpu = {"value": reps * m / elapsed, "unit": "rows/s", "cores": 1, "kind": "port",
+               "sample": f"{reps} passes over {m} rows (numpy restatement of replay.py:35-74), {elapsed:.1f} s"}
+    except Exception as exc:  # noqa: BLE001 - reported, not fatal
+        cpu = {"value": None, "unavailable": str(exc)}
+    emit({"workload": f"replay row checks, {n} generated positions with masked-uniform policies",
+          "metric": "rows/s", "value": n / (ms / 1e3), "unit": "rows/s", "ms": ms, "dtype": "f32",
+          "roofline": {"bound": "hbm", "kernel": "replay_validate_kernel", "achieved": gbs, "peak": peaks[1],
+                       "unit": "GB/s", "frac": gbs / peaks[1], "bytes_per_row": row_bytes},
+          "cpu_baseline": cpu})

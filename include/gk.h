@@ -341,6 +341,35 @@ GK_API int gk_selfplay_ply(void* sp_ws, void* puct_ws, int64_t lanes, const gk_n
                            const gk_selfplay_params_t* params, const gk_replay_t* replay, float* headfeat,
                            uint32_t* status, void* timer, void* stream);
 
+/* --------------------------------------------------------------- replay */
+
+/* Checks of a replay row, in the order the reference applies them
+ * (python/kingdom_ai/replay.py:35-74, _validate_rows). */
+#define GK_REPLAY_NONFINITE (1u << 0)    /* features or policy not finite */
+#define GK_REPLAY_RANGE (1u << 1)        /* a feature outside [0, 1] */
+#define GK_REPLAY_BINARY (1u << 2)       /* planes 0-5, 9 not 0/1 */
+#define GK_REPLAY_SCALAR (1u << 3)       /* planes 5-8 not constant */
+#define GK_REPLAY_ACTOR (1u << 4)        /* to_play not 1 or 2 */
+#define GK_REPLAY_PERSPECTIVE (1u << 5)  /* plane 5 disagrees with to_play */
+#define GK_REPLAY_TERMINAL (1u << 6)     /* passes plane not 0 or 0.5 */
+#define GK_REPLAY_PASS (1u << 7)         /* pass not legal */
+#define GK_REPLAY_MASK (1u << 8)         /* plane 9 disagrees with the mask */
+#define GK_REPLAY_STONES (1u << 9)       /* stone planes overlap */
+#define GK_REPLAY_NEUTRAL (1u << 10)     /* more than one neutral stone */
+#define GK_REPLAY_TERRITORY (1u << 11)   /* territory planes overlap */
+#define GK_REPLAY_POLICY (1u << 12)      /* negative or illegal policy mass */
+#define GK_REPLAY_SUM (1u << 13)         /* policy sum not 1 within 1e-6 (summed in double) */
+#define GK_REPLAY_VALUE (1u << 14)       /* value not -1 or +1 */
+
+/* Validate n replay rows (features fp32[n,10,9,9], masks bool[n,82], policy
+ * fp32[n,82], value fp32[n], to_play int8[n]): *violations (device) is set to
+ * the OR over rows of the GK_REPLAY_* checks they fail; the lowest set bit is
+ * the reference's error. One pass over the rows on the GPU. Replaces the CPU
+ * _validate_rows of ReplayBuffer.extend (python/kingdom_ai/replay.py:35-74,
+ * 133-161). */
+GK_API int gk_replay_validate(const float* features, const uint8_t* masks, const float* policy, const float* value,
+                              const int8_t* to_play, int64_t n, uint32_t* violations, void* stream);
+
 /* CUDA-event timer for kernel launches inside gk_selfplay_ply: a host object
  * holding `pairs` start/stop event pairs (NULL on failure). No reference
  * counterpart: the reference times phases with perf_counter (loop.py:563-621). */

@@ -275,3 +275,48 @@ class RefState:
         return dict(visits=visits, priors=priors, best=int(stats[0]), simulations=int(stats[1]),
                     nodes=int(stats[2]), evaluations=int(stats[3]), root_value=float(values[0]),
                     best_value=float(values[1]))
+
+
+def replay_violation(features, legal_mask, policy, value, to_play):
+    """Restatement of the reference's replay row checks (python/kingdom_ai/replay.py:35-74)
+    in numpy: the message of the first check some row fails, or None. The
+    policy sum is taken in float64."""
+    f = np.asarray(features, dtype=np.float32).reshape(-1, 10, 9, 9)
+    m = np.asarray(legal_mask, dtype=bool).reshape(-1, 82)
+    p = np.asarray(policy, dtype=np.float32).reshape(-1, 82)
+    v = np.asarray(value, dtype=np.float32).reshape(-1)
+    t = np.asarray(to_play, dtype=np.int8).reshape(-1)
+    if len(f) == 0:
+        return None
+    with np.errstate(invalid="ignore"):
+        if not np.isfinite(f).all() or not np.isfinite(p).all():
+            return "Replay features and policies must be finite"
+        if ((f < 0) | (f > 1)).any():
+            return "Replay features must lie between zero and one"
+        if any(((f[:, q] != 0) & (f[:, q] != 1)).any() for q in (0, 1, 2, 3, 4, 5, 9)):
+            return "Binary observation planes must contain only zero or one"
+        if any((f[:, q].reshape(len(f), 81) != f[:, q, :1, :1].reshape(len(f), 1)).any() for q in (5, 6, 7, 8)):
+            return "Scalar observation planes must be constant"
+        if ((t != 1) & (t != 2)).any():
+            return "Replay actors must be Black or White"
+        if (f[:, 5, 0, 0] != (t == 1).astype(np.float32)).any():
+            return "Observation player perspective does not match its actor"
+        if ((f[:, 8, 0, 0] != 0) & (f[:, 8, 0, 0] != 0.5)).any():
+            return "Replay observations must be taken before game termination"
+        if not m[:, 81].all():
+            return "Nonterminal replay observations must allow passing"
+        if not np.array_equal(f[:, 9].reshape(len(f), 81) != 0, m[:, :81]):
+            return "Observation legal placements do not match the action mask"
+        if (f[:, :3].sum(axis=1) > 1).any():
+            return "Stone observation planes cannot overlap"
+        if (f[:, 2].sum(axis=(1, 2)) > 1).any():
+            return "An observation can contain at most one neutral stone"
+        if (f[:, 3] + f[:, 4] > 1).any():
+            return "Opposing territory observation planes cannot overlap"
+        if (p < 0).any() or (p[~m] != 0).any():
+            return "Replay policies must assign non-negative mass to legal actions only"
+        if not (np.abs(p.astype(np.float64).sum(axis=1) - 1.0) <= 1e-6).all():
+            return "Each replay policy must sum to one"
+        if not np.isfinite(v).all() or ((v != -1) & (v != 1)).any():
+            return "Completed-game replay values must be -1 or +1"
+    return None

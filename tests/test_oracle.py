@@ -143,3 +143,54 @@ def test_oracle_tactical_search_known_answers(oracle, golden):
     assert oracle.puct(pass_loss, 8, uniform=True, tactics=True)["visits"][81] == 0
     r = oracle.puct(forced, 8, uniform=True, tactics=True)
     assert r["best"] == 81 and r["best_value"] == -1.0
+
+
+def replay_sample(oracle, index=0, white=False):
+    """The valid replay row of the reference's replay tests (tests/replay_test.py:16-25)."""
+    rec = oracle.initial(1, 40)
+    if white:
+        oracle.play(rec, [81])
+    features, masks = oracle.encode(rec)
+    policy = np.zeros((1, 82), dtype=np.float32)
+    policy[0, index % 40] = 1.0
+    value = np.asarray([1.0 if index % 2 == 0 else -1.0], dtype=np.float32)
+    return features, masks, policy, value, np.asarray([2 if white else 1], dtype=np.int8)
+
+
+def replay_corruptions(oracle):
+    """(message, row) pairs of the reference's rejected contents (tests/replay_test.py:237-274)."""
+    f, m, p, v, t = replay_sample(oracle)
+    cases = []
+
+    def case(message, **changes):
+        row = dict(features=f.copy(), legal_mask=m.copy(), policy=p.copy(), value=v.copy(), to_play=t.copy())
+        for name, (index, value) in changes.items():
+            row[name][(0, *index) if isinstance(index, tuple) else (0, index)] = value
+        cases.append((message, row))
+
+    case("Replay features and policies must be finite", features=((0, 0, 0), np.nan))
+    case("Replay features must lie between zero and one", features=((6, 0, 0), -1.0))
+    case("Binary observation planes must contain only zero or one", features=((0, 0, 0), 0.5))
+    case("Scalar observation planes must be constant", features=((6, 0, 0), 0.7))
+    case("Replay observations must be taken before game termination",
+         features=((8, slice(None), slice(None)), 1.0))
+    case("Replay policies must assign non-negative mass to legal actions only", policy=(0, -1.0))
+    case("Replay policies must assign non-negative mass to legal actions only", policy=(40, 1.0))
+    case("Replay features and policies must be finite", policy=(0, np.inf))
+    case("Each replay policy must sum to one", policy=(slice(None), 0.0))
+    case("Nonterminal replay observations must allow passing", legal_mask=(slice(None), False))
+    case("Observation legal placements do not match the action mask", legal_mask=(0, False))
+    case("Nonterminal replay observations must allow passing", legal_mask=(81, False))
+    case("Completed-game replay values must be -1 or +1", value=((), np.nan))
+    case("Completed-game replay values must be -1 or +1", value=((), 0.0))
+    case("Replay actors must be Black or White", to_play=((), 3))
+    case("Observation player perspective does not match its actor", to_play=((), 2))
+    return cases
+
+
+def test_replay_checks_restatement_rejects_reference_cases(oracle):
+    from oracle.oracle import replay_violation
+    for index, white in ((0, False), (3, False), (5, True)):
+        assert replay_violation(*replay_sample(oracle, index, white)) is None
+    for message, row in replay_corruptions(oracle):
+        assert replay_violation(**row) == message
