@@ -656,3 +656,430 @@ int gko_puct_search_batch(const int32_t* recs, int64_t n, int simulations, doubl
     }
     return status;
 }
+
+/* ----------------------------------------------------------- BatchedPUCT */
+/* The evaluation searcher of mcts/src/BatchedPUCT.cpp restated: leaf batches
+ * gathered under a virtual loss of one per pending simulation (143-227), the
+ * subtree promotion of advance() (290-326) and the search loop with its
+ * per-search statistics (328-442). Selection is the reference's depth-first
+ * walk: at each node the edges are tried in score order and a subtree that
+ * holds only pending leaves is skipped for the next-scored edge. The tree is
+ * one growable node array; edges are the legal actions in action order. */
+
+typedef struct {
+    int move;
+    double prior;
+    int64_t visits;
+    double value_sum;
+    int64_t reserved;
+    int64_t child; /* -1: none */
+} ob_edge;
+
+typedef struct {
+    int32_t rec[GK_STATE_WIDTH];
+    int64_t visits;
+    int64_t reserved;
+    int expanded;
+    int pending;
+    int nedges;
+    ob_edge edges[GK_ACTIONS];
+} ob_node;
+
+typedef struct {
+    int64_t node;
+    int depth;
+    int64_t path_node[GK_MAX_PLIES + 4];
+    int path_edge[GK_MAX_PLIES + 4];
+} ob_leaf;
+
+typedef struct {
+    int64_t simulations;
+    double c_puct;
+    int64_t leaf_batch;
+    int reuse;
+    int evaluator;
+    ob_node* tree;
+    int64_t size, cap;
+    int64_t stats[GKO_BPUCT_STATS];
+} ob_search;
+
+enum { OB_EVALS, OB_BATCHES, OB_MAX_BATCH, OB_REUSED, OB_INHERITED, OB_ADVANCES, OB_REUSE_HITS };
+
+void* gko_bpuct_new(int64_t simulations, double c_puct, int64_t leaf_batch, int reuse, int evaluator) {
+    if (simulations < 1 || !(c_puct > 0.0) || !isfinite(c_puct) || leaf_batch < 1) return NULL;
+    ob_search* s = (ob_search*)calloc(1, sizeof(ob_search));
+    if (!s) return NULL;
+    s->simulations = simulations;
+    s->c_puct = c_puct;
+    s->leaf_batch = leaf_batch;
+    s->reuse = reuse != 0;
+    s->evaluator = evaluator;
+    return s;
+}
+
+void gko_bpuct_free(void* h) {
+    ob_search* s = (ob_search*)h;
+    if (!s) return;
+    free(s->tree);
+    free(s);
+}
+
+void gko_bpuct_clear(void* h) { ((ob_search*)h)->size = 0; }
+
+int64_t gko_bpuct_size(const void* h) { return ((const ob_search*)h)->size; }
+
+void gko_bpuct_stats(const void* h, int64_t* out) {
+    for (int i = 0; i < GKO_BPUCT_STATS; ++i) out[i] = ((const ob_search*)h)->stats[i];
+}
+
+static int64_t ob_push(ob_search* s, const int32_t* rec) {
+    if (s->size == s->cap) {
+        int64_t cap = s->cap ? 2 * s->cap : 64;
+        ob_node* grown = (ob_node*)realloc(s->tree, (size_t)cap * sizeof(ob_node));
+        if (!grown) return -1;
+        s->tree = grown;
+        s->cap = cap;
+    }
+    ob_node* n = &s->tree[s->size];
+    memcpy(n->rec, rec, sizeof n->rec);
+    n->visits = 0;
+    n->reserved = 0;
+    n->expanded = 0;
+    n->pending = 0;
+    n->nedges = 0;
+    return s->size++;
+}
+
+/* BatchedPUCT.cpp:52-67: every field that defines a position, rules and result included. */
+static int ob_same_state(const int32_t* a, const int32_t* b) {
+    for (int i = 0; i <= GK_CAPTURED; ++i)
+        if (a[i] != b[i]) return 0;
+    return 1;
+}
+
+/* The evaluators of the search: the injected hash evaluator, a uniform one,
+ * and the fixed evaluator of the reference's own tests
+ * (tests/batched_puct_test.cpp:21-28: weight (i + 1) / 81 on cell i, none on
+ * pass; value 0.25 for Black to play, -0.5 for White). */
+static void ob_evaluate(int kind, const int32_t* rec, double* w, double* v) {
+    if (kind == GKO_EVAL_UNIFORM) {
+        for (int a = 0; a < GK_ACTIONS; ++a) w[a] = 1.0;
+        *v = 0.0;
+    } else if (kind == GKO_EVAL_RAMP) {
+        for (int a = 0; a < GK_CELLS; ++a) w[a] = (double)(a + 1) / 81.0;
+        w[GK_PASS] = 0.0;
+        *v = rec[GK_ACTOR] == 1 ? 0.25 : -0.5;
+    } else {
+        float wf[GK_ACTIONS], vf;
+        gko_eval(rec, wf, &vf);
+        for (int a = 0; a < GK_ACTIONS; ++a) w[a] = (double)wf[a];
+        *v = (double)vf;
+    }
+}
+
+/* BatchedPUCT.cpp:72-81 (evaluation checks) and 229-250 (edges). */
+static int ob_expand(ob_node* n, const double* w, double v) {
+    if (!isfinite(v) || v < -1.0 || v > 1.0) return GKO_BPUCT_BAD_VALUE;
+    for (int a = 0; a < GK_ACTIONS; ++a)
+        if (!isfinite(w[a]) || w[a] < 0.0) return GKO_BPUCT_BAD_POLICY;
+    int moves[GK_ACTIONS];
+    const int count = legal_list(n->rec, moves);
+    double largest = 0.0;
+    for (int i = 0; i < count; ++i) largest = fmax(largest, w[moves[i]]);
+    if (largest == 0.0) return GKO_BPUCT_ZERO_POLICY;
+    double total = 0.0;
+    for (int i = 0; i < count; ++i) total += w[moves[i]] / largest;
+    for (int i = 0; i < count; ++i) {
+        ob_edge* e = &n->edges[i];
+        e->move = moves[i];
+        e->prior = (w[moves[i]] / largest) / total;
+        e->visits = 0;
+        e->value_sum = 0.0;
+        e->reserved = 0;
+        e->child = -1;
+    }
+    n->nedges = count;
+    n->expanded = 1;
+    return 0;
+}
+
+/* BatchedPUCT.cpp:143-196. Returns 1 with the leaf and its path, 0 when
+ * every path below `node` ends in a pending leaf, negative on failure. */
+static int ob_select(ob_search* s, int64_t node, ob_leaf* leaf) {
+    if (s->tree[node].pending) return 0;
+    if (!s->tree[node].expanded || s->tree[node].rec[GK_REASON] != GK_NONE) {
+        leaf->node = node;
+        return 1;
+    }
+    const int count = s->tree[node].nedges;
+    if (count == 0) return GKO_BPUCT_LOGIC;
+    uint8_t tried[GK_ACTIONS] = {0};
+    for (int attempt = 0; attempt < count; ++attempt) {
+        const ob_node* n = &s->tree[node];
+        const double scale = sqrt((double)n->visits + (double)n->reserved);
+        int best = -1;
+        double best_score = -INFINITY;
+        for (int i = 0; i < count; ++i) {
+            if (tried[i]) continue;
+            const ob_edge* e = &n->edges[i];
+            const double effective = (double)e->visits + (double)e->reserved;
+            const double value = effective == 0.0 ? 0.0 : (e->value_sum - (double)e->reserved) / effective;
+            const double exploration = e->prior * scale / (1.0 + effective);
+            const double score = s->c_puct >= 1.0 ? value / s->c_puct + exploration : value + s->c_puct * exploration;
+            if (best < 0 || score > best_score ||
+                (score == best_score && (e->prior > n->edges[best].prior ||
+                                         (e->prior == n->edges[best].prior && e->move < n->edges[best].move)))) {
+                best = i;
+                best_score = score;
+            }
+        }
+        if (best < 0) return 0;
+        tried[best] = 1;
+        int64_t child = s->tree[node].edges[best].child;
+        if (child < 0) {
+            int32_t next[GK_STATE_WIDTH];
+            memcpy(next, s->tree[node].rec, sizeof next);
+            if (!gko_play(next, s->tree[node].edges[best].move)) return GKO_BPUCT_LOGIC;
+            child = ob_push(s, next);
+            if (child < 0) return GKO_BPUCT_LOGIC;
+            s->tree[node].edges[best].child = child;
+        }
+        if (leaf->depth >= GK_MAX_PLIES + 4) return GKO_BPUCT_LOGIC;
+        leaf->path_node[leaf->depth] = node;
+        leaf->path_edge[leaf->depth] = best;
+        ++leaf->depth;
+        const int found = ob_select(s, child, leaf);
+        if (found != 0) return found;
+        --leaf->depth;
+    }
+    return 0;
+}
+
+/* BatchedPUCT.cpp:198-227 */
+static void ob_reserve(ob_search* s, const ob_leaf* l, int64_t delta) {
+    s->tree[l->node].pending = delta > 0;
+    s->tree[0].reserved += delta;
+    for (int d = 0; d < l->depth; ++d) {
+        ob_edge* e = &s->tree[l->path_node[d]].edges[l->path_edge[d]];
+        e->reserved += delta;
+        s->tree[e->child].reserved += delta;
+    }
+}
+
+static void ob_backup(ob_search* s, const ob_leaf* l, double value) {
+    ++s->tree[0].visits;
+    const int player = s->tree[l->node].rec[GK_ACTOR];
+    for (int d = 0; d < l->depth; ++d) {
+        ob_node* parent = &s->tree[l->path_node[d]];
+        ob_edge* e = &parent->edges[l->path_edge[d]];
+        e->value_sum += parent->rec[GK_ACTOR] == player ? value : -value;
+        ++e->visits;
+        ++s->tree[e->child].visits;
+    }
+}
+
+static double ob_terminal_value(const int32_t* rec) { return rec[GK_WINNER] == rec[GK_ACTOR] ? 1.0 : -1.0; }
+
+static void ob_note_batch(ob_search* s, int64_t rows) {
+    s->stats[OB_EVALS] += rows;
+    s->stats[OB_BATCHES] += 1;
+    if (rows > s->stats[OB_MAX_BATCH]) s->stats[OB_MAX_BATCH] = rows;
+}
+
+/* BatchedPUCT.cpp:328-442. Outputs per action: visits and mean value gained
+ * in this search, priors, legal (the root's edges); info = {best action,
+ * simulations, nodes, network evaluations}; values = {root value, best value}.
+ * Any failure clears the tree and returns a negative GKO_BPUCT_* code. */
+int gko_bpuct_search(void* h, const int32_t* root, int32_t* visits, double* priors, double* move_values,
+                     uint8_t* legal, int32_t* info, double* values) {
+    ob_search* s = (ob_search*)h;
+    for (int a = 0; a < GK_ACTIONS; ++a) {
+        visits[a] = 0;
+        priors[a] = 0.0;
+        move_values[a] = 0.0;
+        legal[a] = 0;
+    }
+    info[0] = -1;
+    info[1] = info[2] = info[3] = 0;
+    values[0] = values[1] = 0.0;
+    for (int i = OB_EVALS; i <= OB_INHERITED; ++i) s->stats[i] = 0;
+    if (!s->reuse || (s->size > 0 && !ob_same_state(s->tree[0].rec, root))) s->size = 0;
+    if (root[GK_REASON] != GK_NONE) {
+        s->size = 0;
+        values[0] = ob_terminal_value(root);
+        return 0;
+    }
+    if (s->size == 0) {
+        if (ob_push(s, root) < 0) return GKO_BPUCT_LOGIC;
+    } else {
+        s->stats[OB_REUSED] = s->size;
+        s->stats[OB_INHERITED] = s->tree[0].visits;
+    }
+    int status = 0;
+    double w[GK_ACTIONS], v;
+    if (!s->tree[0].expanded) {
+        ob_evaluate(s->evaluator, s->tree[0].rec, w, &v);
+        if ((status = ob_expand(&s->tree[0], w, v)) != 0) goto failed;
+        ob_note_batch(s, 1);
+    }
+    int64_t initial_visits[GK_ACTIONS];
+    double initial_values[GK_ACTIONS];
+    for (int i = 0; i < s->tree[0].nedges; ++i) {
+        initial_visits[i] = s->tree[0].edges[i].visits;
+        initial_values[i] = s->tree[0].edges[i].value_sum;
+    }
+    ob_leaf* pending = (ob_leaf*)malloc((size_t)s->leaf_batch * sizeof(ob_leaf));
+    double* weights = (double*)malloc((size_t)s->leaf_batch * GK_ACTIONS * sizeof(double));
+    double* leaf_values = (double*)malloc((size_t)s->leaf_batch * sizeof(double));
+    if (!pending || !weights || !leaf_values) {
+        status = GKO_BPUCT_LOGIC;
+        goto release;
+    }
+    int64_t sims = 0;
+    while (sims < s->simulations) {
+        const int64_t remaining = s->simulations - sims;
+        const int64_t capacity = remaining < s->leaf_batch ? remaining : s->leaf_batch;
+        int64_t count = 0;
+        while (count < capacity && count < s->simulations - sims) {
+            ob_leaf* l = &pending[count];
+            l->depth = 0;
+            const int found = ob_select(s, 0, l);
+            if (found < 0) {
+                status = found;
+                goto release;
+            }
+            if (found == 0) break;
+            if (s->tree[l->node].rec[GK_REASON] != GK_NONE) {
+                ob_backup(s, l, ob_terminal_value(s->tree[l->node].rec));
+                ++sims;
+                continue;
+            }
+            ob_reserve(s, l, 1);
+            ++count;
+        }
+        if (count > 0) {
+            for (int64_t i = 0; i < count; ++i)
+                ob_evaluate(s->evaluator, s->tree[pending[i].node].rec, weights + i * GK_ACTIONS, &leaf_values[i]);
+            for (int64_t i = 0; i < count; ++i) {
+                const double lv = leaf_values[i];
+                if (!isfinite(lv) || lv < -1.0 || lv > 1.0) {
+                    status = GKO_BPUCT_BAD_VALUE;
+                    goto release;
+                }
+                for (int a = 0; a < GK_ACTIONS; ++a)
+                    if (!isfinite(weights[i * GK_ACTIONS + a]) || weights[i * GK_ACTIONS + a] < 0.0) {
+                        status = GKO_BPUCT_BAD_POLICY;
+                        goto release;
+                    }
+            }
+            ob_note_batch(s, count);
+            for (int64_t i = 0; i < count; ++i) {
+                if ((status = ob_expand(&s->tree[pending[i].node], weights + i * GK_ACTIONS, leaf_values[i])) != 0)
+                    goto release;
+                ob_reserve(s, &pending[i], -1);
+                ob_backup(s, &pending[i], leaf_values[i]);
+                ++sims;
+            }
+        } else if (sims < s->simulations) {
+            status = GKO_BPUCT_LOGIC;
+            goto release;
+        }
+    }
+    {
+        const ob_node* r = &s->tree[0];
+        double root_sum = 0.0;
+        int best = -1;
+        int64_t best_visits = 0;
+        double best_value = 0.0;
+        for (int i = 0; i < r->nedges; ++i) {
+            const ob_edge* e = &r->edges[i];
+            const int64_t n = e->visits - initial_visits[i];
+            const double sum = e->value_sum - initial_values[i];
+            const double mean = n == 0 ? 0.0 : sum / (double)n;
+            visits[e->move] = (int32_t)n;
+            priors[e->move] = e->prior;
+            move_values[e->move] = mean;
+            legal[e->move] = 1;
+            root_sum += sum;
+            /* BatchedPUCT.cpp:118-123 over moves in action order. */
+            int better;
+            if (best < 0) better = 1;
+            else if (n != best_visits) better = n > best_visits;
+            else if (mean != best_value) better = mean > best_value;
+            else if (e->prior != r->edges[best].prior) better = e->prior > r->edges[best].prior;
+            else better = 0;
+            if (better) {
+                best = i;
+                best_visits = n;
+                best_value = mean;
+            }
+        }
+        if (best < 0 || best_visits == 0) {
+            status = GKO_BPUCT_LOGIC;
+            goto release;
+        }
+        info[0] = r->edges[best].move;
+        info[1] = (int32_t)sims;
+        info[2] = (int32_t)s->size;
+        info[3] = (int32_t)s->stats[OB_EVALS];
+        values[0] = root_sum / (double)sims;
+        values[1] = best_value;
+    }
+release:
+    free(pending);
+    free(weights);
+    free(leaf_values);
+failed:
+    if (status != 0) s->size = 0;
+    return status;
+}
+
+/* BatchedPUCT.cpp:290-326: keep and compact the played move's subtree. */
+int gko_bpuct_advance(void* h, int action) {
+    ob_search* s = (ob_search*)h;
+    ++s->stats[OB_ADVANCES];
+    if (!s->reuse || s->size == 0) {
+        s->size = 0;
+        return 0;
+    }
+    const ob_node* r = &s->tree[0];
+    int found = -1;
+    for (int i = 0; i < r->nedges; ++i)
+        if (r->edges[i].move == action) found = i;
+    if (found < 0 && !(action >= 0 && action < GK_ACTIONS && gko_legal(r->rec, action))) return 0;
+    if (found < 0 || r->edges[found].child < 0) {
+        s->size = 0;
+        return 0;
+    }
+    int64_t* order = (int64_t*)malloc((size_t)s->size * sizeof(int64_t));
+    int64_t* remap = (int64_t*)malloc((size_t)s->size * sizeof(int64_t));
+    ob_node* kept = (ob_node*)malloc((size_t)s->size * sizeof(ob_node));
+    if (!order || !remap || !kept) {
+        free(order);
+        free(remap);
+        free(kept);
+        s->size = 0;
+        return 0;
+    }
+    int64_t count = 0;
+    order[count++] = r->edges[found].child;
+    for (int64_t next = 0; next < count; ++next) {
+        const ob_node* n = &s->tree[order[next]];
+        for (int i = 0; i < n->nedges; ++i)
+            if (n->edges[i].child >= 0) order[count++] = n->edges[i].child;
+    }
+    for (int64_t i = 0; i < s->size; ++i) remap[i] = -1;
+    for (int64_t i = 0; i < count; ++i) remap[order[i]] = i;
+    for (int64_t i = 0; i < count; ++i) {
+        kept[i] = s->tree[order[i]];
+        for (int e = 0; e < kept[i].nedges; ++e)
+            if (kept[i].edges[e].child >= 0) kept[i].edges[e].child = remap[kept[i].edges[e].child];
+    }
+    memcpy(s->tree, kept, (size_t)count * sizeof(ob_node));
+    s->size = count;
+    free(order);
+    free(remap);
+    free(kept);
+    ++s->stats[OB_REUSE_HITS];
+    return 1;
+}

@@ -54,6 +54,28 @@ int gko_puct_search_tactics(const int32_t* rec, int simulations, double c_puct, 
 int gko_puct_search_batch(const int32_t* recs, int64_t n, int simulations, double c_puct, int32_t* visits,
                           int32_t* best, double* root_values, int threads);
 
+/* BatchedPUCT (mcts/src/BatchedPUCT.cpp): a persistent searcher with leaf
+ * batches under virtual loss and subtree reuse. `evaluator` picks the leaf
+ * evaluator (GKO_EVAL_*). stats = {network_evaluations, inference_batches,
+ * max_observed_batch_size, reused_nodes, inherited_visits, advance_calls,
+ * reuse_hits}. */
+#define GKO_BPUCT_STATS 7
+#define GKO_EVAL_HASH 0
+#define GKO_EVAL_UNIFORM 1
+#define GKO_EVAL_RAMP 2 /* tests/batched_puct_test.cpp:21-28 */
+#define GKO_BPUCT_BAD_VALUE (-2)   /* value not finite or outside [-1, 1] */
+#define GKO_BPUCT_BAD_POLICY (-3)  /* a weight not finite or negative */
+#define GKO_BPUCT_ZERO_POLICY (-4) /* no positive weight on a legal action */
+#define GKO_BPUCT_LOGIC (-5)
+void* gko_bpuct_new(int64_t simulations, double c_puct, int64_t leaf_batch, int reuse, int evaluator);
+void gko_bpuct_free(void* h);
+void gko_bpuct_clear(void* h);
+int64_t gko_bpuct_size(const void* h);
+void gko_bpuct_stats(const void* h, int64_t* out);
+int gko_bpuct_search(void* h, const int32_t* root, int32_t* visits, double* priors, double* move_values,
+                     uint8_t* legal, int32_t* info, double* values);
+int gko_bpuct_advance(void* h, int action);
+
 #ifdef __cplusplus
 }
 #endif

@@ -80,6 +80,11 @@ class Oracle:
         _bind(L, "gko_puct_search_batch", [_i32p, _i64, _int, ctypes.c_double, _i32p, _i32p, _f64p, _int], _int)
         _bind(L, "gko_root_tactics", [_i32p, _i8p, _u8p])
         _bind(L, "gko_puct_search_tactics", [_i32p, _int, ctypes.c_double, _int, _i32p, _f64p, _i32p, _f64p], _int)
+        _bind_batched(L, "gko")
+
+    def batched(self, simulations, c_puct=1.5, leaf_batch=8, reuse=True, evaluator="hash"):
+        """The restated BatchedPUCT searcher (oracle/gk_oracle.c)."""
+        return BatchedSearcher(self.lib, "gko", simulations, c_puct, leaf_batch, reuse, evaluator)
 
     def initial(self, n: int = 1, neutral: int = 40) -> np.ndarray:
         recs = np.zeros((n, STATE_WIDTH), dtype=np.int32)
@@ -159,6 +164,71 @@ class Oracle:
         return visits, best, roots
 
 
+EVALUATORS = {"hash": 0, "uniform": 1, "ramp": 2}
+BATCHED_STATS = ("network_evaluations", "inference_batches", "max_observed_batch_size", "reused_nodes",
+                 "inherited_visits", "advance_calls", "reuse_hits")
+
+
+def _bind_batched(lib, prefix):
+    vp = ctypes.c_void_p
+    _bind(lib, f"{prefix}_bpuct_new", [_i64, ctypes.c_double, _i64, _int, _int], vp)
+    _bind(lib, f"{prefix}_bpuct_free", [vp])
+    _bind(lib, f"{prefix}_bpuct_clear", [vp])
+    root = _i32p if prefix == "gko" else vp
+    _bind(lib, f"{prefix}_bpuct_search", [vp, root, _i32p, _f64p, _f64p, _u8p, _i32p, _f64p], _int)
+    _bind(lib, f"{prefix}_bpuct_advance", [vp, _int], _int)
+    _bind(lib, f"{prefix}_bpuct_stats", [vp, ctypes.POINTER(ctypes.c_int64)])
+
+
+class BatchedSearcher:
+    """One BatchedPUCT searcher (leaf batches, virtual loss, subtree reuse):
+    the plain-C restatement ("gko", searched from wire records) or the
+    reference engine ("gkr", searched from RefState handles)."""
+
+    def __init__(self, lib, prefix, simulations, c_puct, leaf_batch, reuse, evaluator):
+        self.lib, self.prefix = lib, prefix
+        self.h = getattr(lib, f"{prefix}_bpuct_new")(simulations, c_puct, leaf_batch, int(reuse),
+                                                      EVALUATORS[evaluator])
+        if not self.h:
+            raise ValueError("invalid BatchedPUCT options")
+
+    def __del__(self):
+        try:
+            getattr(self.lib, f"{self.prefix}_bpuct_free")(self.h)
+        except Exception:
+            pass
+
+    def clear(self):
+        getattr(self.lib, f"{self.prefix}_bpuct_clear")(self.h)
+
+    def search(self, root):
+        """root: a wire record (oracle) or a RefState (reference). Raises
+        ValueError with the failure code when the search fails."""
+        visits = np.zeros(ACTIONS, dtype=np.int32)
+        priors = np.zeros(ACTIONS, dtype=np.float64)
+        values = np.zeros(ACTIONS, dtype=np.float64)
+        legal = np.zeros(ACTIONS, dtype=np.uint8)
+        info = np.zeros(4, dtype=np.int32)
+        out = np.zeros(2, dtype=np.float64)
+        arg = root.h if isinstance(root, RefState) else np.ascontiguousarray(root, dtype=np.int32)
+        status = getattr(self.lib, f"{self.prefix}_bpuct_search")(self.h, arg, visits, priors, values, legal, info,
+                                                                  out)
+        if status != 0:
+            raise ValueError(f"BatchedPUCT search failed ({status})")
+        return dict(visits=visits, priors=priors, move_values=values, legal=legal.astype(bool), best=int(info[0]),
+                    simulations=int(info[1]), nodes=int(info[2]), evaluations=int(info[3]),
+                    root_value=float(out[0]), best_value=float(out[1]))
+
+    def advance(self, action):
+        return bool(getattr(self.lib, f"{self.prefix}_bpuct_advance")(self.h, int(action)))
+
+    @property
+    def stats(self):
+        out = (ctypes.c_int64 * len(BATCHED_STATS))()
+        getattr(self.lib, f"{self.prefix}_bpuct_stats")(self.h, out)
+        return dict(zip(BATCHED_STATS, (int(v) for v in out)))
+
+
 class Reference:
     """Driver for the reference C++ engine compiled from its own sources."""
 
@@ -184,6 +254,11 @@ class Reference:
         _bind(L, "gkr_encode_positions", [_u64, _u64, _i64, _int, _f32p, _u8p])
         _bind(L, "gkr_puct_search", [vp, _int, ctypes.c_double, _i32p, _f64p, _i32p, _f64p], _int)
         _bind(L, "gkr_puct_positions", [_u64, _u64, _i64, _int, ctypes.c_double, _int, _i32p, _i32p], _int)
+        _bind_batched(L, "gkr")
+
+    def batched(self, simulations, c_puct=1.5, leaf_batch=8, reuse=True, evaluator="hash"):
+        """The reference's own ``kingdom::BatchedPUCT`` (mcts/src/BatchedPUCT.cpp)."""
+        return BatchedSearcher(self.lib, "gkr", simulations, c_puct, leaf_batch, reuse, evaluator)
 
     def random_playouts(self, seed, n, first=0, neutral=40, fast=False, threads=1):
         boards = np.zeros((n, 81), dtype=np.int8)

@@ -9,11 +9,13 @@
 //   kingdom::State / play / legal_moves / score   engine/include/board/State.h:16-81
 //   kingdom::encode_puct_position                 mcts/include/BatchedPUCT.h:16
 //   kingdom::PUCT::search                         mcts/include/PUCT.h:60-73
+//   kingdom::BatchedPUCT search / advance / stats mcts/include/BatchedPUCT.h:38-60
 // Wire translation follows tests/gpu_rules_test.py:30-39 (cpu_record).
 #include "BatchedPUCT.h"
 #include "PUCT.h"
 #include "board/State.h"
 
+#include <cmath>
 #include <cstdint>
 #include <cstring>
 #include <exception>
@@ -155,6 +157,48 @@ void parallel_for(int64_t n, int threads, F&& body) {
     }
     for (auto& th : pool) th.join();
 }
+
+// ---- BatchedPUCT -----------------------------------------------------------
+// The batch callback sees only schema-1 positions, so the injected evaluator
+// rebuilds the wire record of a non-terminal position from its planes
+// (BatchedPUCT.cpp:25-50) before hashing it.
+kingdom::PUCTEvaluation encoded_eval(int kind, const kingdom::EncodedPUCTPosition& e) {
+    kingdom::PUCTEvaluation out;
+    const float* f = e.features.data();
+    if (kind == 1) {
+        out.policy.fill(1.0);
+        out.value = 0.0;
+        return out;
+    }
+    if (kind == 2) {  // tests/batched_puct_test.cpp:21-28
+        for (std::size_t i = 0; i < Board::kCellCount; ++i) out.policy[i] = static_cast<double>(i + 1) / 81.0;
+        out.value = f[405] != 0.0F ? 0.25 : -0.5;
+        return out;
+    }
+    int32_t rec[GK_STATE_WIDTH] = {};
+    const int actor = f[405] != 0.0F ? 1 : 2, enemy = 3 - actor;
+    for (int i = 0; i < GK_CELLS; ++i) {
+        rec[i] = f[i] != 0.0F ? actor : f[81 + i] != 0.0F ? enemy : f[162 + i] != 0.0F ? 3 : 0;
+        rec[GK_CELLS + i] = f[243 + i] != 0.0F ? actor : f[324 + i] != 0.0F ? enemy : 0;
+    }
+    const int own = static_cast<int>(std::lround(f[486] * 41.0)), other = static_cast<int>(std::lround(f[567] * 41.0));
+    rec[GK_ACTOR] = actor;
+    rec[GK_BLACK_STOCK] = actor == 1 ? own : other;
+    rec[GK_WHITE_STOCK] = actor == 1 ? other : own;
+    rec[GK_PASSES] = static_cast<int>(std::lround(f[648] * 2.0));
+    uint64_t words[GK_EVAL_WORDS];
+    gk_eval_words_from_record(rec, words);
+    const uint64_t h = gk_eval_hash_words(words);
+    for (int a = 0; a < GK_ACTIONS; ++a) out.policy[static_cast<std::size_t>(a)] = static_cast<double>(gk_eval_weight(h, a));
+    out.value = static_cast<double>(gk_eval_value(h));
+    return out;
+}
+
+struct BatchedHandle {
+    kingdom::BatchedPUCT search;
+    int evaluator;
+    int64_t max_rows = 0;
+};
 
 }  // namespace
 
@@ -308,4 +352,79 @@ int gkr_puct_search_cb(const void* h, int simulations, double c_puct, double alp
     }
 }
 
+// BatchedPUCT with one of the evaluators above (0 hash, 1 uniform, 2 the
+// reference tests' fixed evaluator). Same outputs as gko_bpuct_search.
+void* gkr_bpuct_new(int64_t simulations, double c_puct, int64_t leaf_batch, int reuse, int evaluator) {
+    try {
+        kingdom::PUCTOptions o;
+        o.simulations = static_cast<std::size_t>(simulations);
+        o.c_puct = c_puct;
+        o.dirichlet_epsilon = 0.0;
+        return new BatchedHandle{kingdom::BatchedPUCT(o, static_cast<std::size_t>(leaf_batch), reuse != 0), evaluator};
+    } catch (const std::exception&) {
+        return nullptr;
+    }
+}
+
+void gkr_bpuct_free(void* h) { delete static_cast<BatchedHandle*>(h); }
+
+void gkr_bpuct_clear(void* h) { static_cast<BatchedHandle*>(h)->search.clear(); }
+
+int gkr_bpuct_search(void* h, const void* state, int32_t* visits, double* priors, double* move_values,
+                     uint8_t* legal, int32_t* info, double* values) {
+    auto* b = static_cast<BatchedHandle*>(h);
+    for (int a = 0; a < GK_ACTIONS; ++a) {
+        visits[a] = 0;
+        priors[a] = 0.0;
+        move_values[a] = 0.0;
+        legal[a] = 0;
+    }
+    info[0] = -1;
+    info[1] = info[2] = info[3] = 0;
+    values[0] = values[1] = 0.0;
+    try {
+        const int kind = b->evaluator;
+        const auto r = b->search.search(*static_cast<const State*>(state),
+                                        [kind](const std::vector<kingdom::EncodedPUCTPosition>& positions) {
+                                            std::vector<kingdom::PUCTEvaluation> out;
+                                            out.reserve(positions.size());
+                                            for (const auto& p : positions) out.push_back(encoded_eval(kind, p));
+                                            return out;
+                                        });
+        for (const auto& m : r.moves) {
+            const int a = action_of(m.move);
+            visits[a] = static_cast<int32_t>(m.visits);
+            priors[a] = m.prior;
+            move_values[a] = m.value;
+            legal[a] = 1;
+        }
+        info[0] = r.best_move ? action_of(*r.best_move) : -1;
+        info[1] = static_cast<int32_t>(r.simulations);
+        info[2] = static_cast<int32_t>(r.nodes);
+        info[3] = static_cast<int32_t>(r.network_evaluations);
+        values[0] = r.root_value;
+        values[1] = r.best_value;
+        return 0;
+    } catch (const std::exception&) {
+        return -1;
+    }
+}
+
+int gkr_bpuct_advance(void* h, int action) {
+    auto* b = static_cast<BatchedHandle*>(h);
+    return b->search.advance(to_move(action)) ? 1 : 0;
+}
+
+void gkr_bpuct_stats(const void* h, int64_t* out) {
+    const auto& s = static_cast<const BatchedHandle*>(h)->search.stats();
+    out[0] = static_cast<int64_t>(s.network_evaluations);
+    out[1] = static_cast<int64_t>(s.inference_batches);
+    out[2] = static_cast<int64_t>(s.max_observed_batch_size);
+    out[3] = static_cast<int64_t>(s.reused_nodes);
+    out[4] = static_cast<int64_t>(s.inherited_visits);
+    out[5] = static_cast<int64_t>(s.advance_calls);
+    out[6] = static_cast<int64_t>(s.reuse_hits);
+}
+
 }  // extern "C"
+

@@ -24,7 +24,17 @@ Fixtures
                         reference engine (+1 win, -1 loss or a winning reply
                         for the opponent, 0 otherwise).
 
-Run with the argument ``tactics`` to write only tactics.npz.
+  batched.npz           evaluation games driven by the reference
+                        kingdom::BatchedPUCT (mcts/src/BatchedPUCT.cpp): one
+                        searcher per colour with subtree reuse, both advanced
+                        after every move as python/kingdom_ai/evaluation.py:
+                        174-231 does, under six (simulations, leaf batch,
+                        c_puct, evaluator, reuse) configurations; per search
+                        the root, every result field and the statistics, the
+                        move played, the advance results and an occasional
+                        illegal advance.
+
+Run with the argument ``tactics`` (or ``batched``) to write only that fixture.
 """
 
 from __future__ import annotations
@@ -178,6 +188,72 @@ def tactics_fixture(ref):
                 outcomes=outcomes)
 
 
+BATCHED_CONFIGS = (  # simulations, leaf batch, c_puct, evaluator (0 hash, 1 uniform, 2 ramp), reuse
+    (16, 4, 1.5, 2, 1),
+    (32, 8, 1.5, 0, 1),
+    (24, 1, 0.7, 0, 1),
+    (48, 16, 2.5, 1, 1),
+    (40, 8, 1.5, 0, 0),
+    (64, 64, 1.5, 0, 1),
+)
+BATCHED_GAMES = 6
+BATCHED_PLIES = 60
+
+
+def batched_fixture(ref):
+    from oracle.oracle import EVALUATORS
+    kinds = {v: k for k, v in EVALUATORS.items()}
+    rows = {k: [] for k in ("cfg", "game", "ply", "root", "visits", "priors", "move_values", "legal", "info",
+                            "values", "stats", "move", "advanced", "bad_action", "bad_advanced", "stats_after")}
+    for ci, (sims, leaf, c, kind, reuse) in enumerate(BATCHED_CONFIGS):
+        for g in range(BATCHED_GAMES):
+            rng = np.random.default_rng(1000 * ci + g)
+            searchers = [ref.batched(sims, c, leaf, bool(reuse), kinds[kind]) for _ in range(2)]
+            state = RefState.initial(ref, 40) if g % 2 == 0 else RefState.generated(ref, 31, 10 * ci + g)
+            for ply in range(BATCHED_PLIES):
+                root = state.record()
+                if root[166] != 0:
+                    break
+                who = 0 if root[162] == BLACK else 1
+                r = searchers[who].search(state)
+                stats = searchers[who].stats
+                legal = np.flatnonzero(r["legal"])
+                move = r["best"] if rng.random() < 0.7 else int(rng.choice(legal))
+                assert state.play(move)
+                advanced = [searchers[k].advance(move) for k in range(2)]
+                bad, bad_adv = -100, [False, False]
+                if rng.random() < 0.15:
+                    bad = int(rng.choice([-1, 82, 90, 40]))
+                    bad_adv = [searchers[k].advance(bad) for k in range(2)]
+                after = [searchers[k].stats for k in range(2)]
+                rows["cfg"].append(ci)
+                rows["game"].append(g)
+                rows["ply"].append(ply)
+                rows["root"].append(root)
+                for key in ("visits", "priors", "move_values", "legal"):
+                    rows[key].append(r[key])
+                rows["info"].append([r["best"], r["simulations"], r["nodes"], r["evaluations"]])
+                rows["values"].append([r["root_value"], r["best_value"]])
+                rows["stats"].append(list(stats.values()))
+                rows["move"].append(move)
+                rows["advanced"].append(advanced)
+                rows["bad_action"].append(bad)
+                rows["bad_advanced"].append(bad_adv)
+                rows["stats_after"].append([list(a.values()) for a in after])
+    out = {k: np.asarray(v) for k, v in rows.items()}
+    out["root"] = out["root"].astype(np.int32)
+    out["legal"] = out["legal"].astype(np.uint8)
+    out["visits"] = out["visits"].astype(np.int32)
+    for key in ("cfg", "game", "ply", "move", "bad_action"):
+        out[key] = out[key].astype(np.int32)
+    for key in ("info", "stats", "stats_after"):
+        out[key] = out[key].astype(np.int64)
+    out["advanced"] = out["advanced"].astype(np.uint8)
+    out["bad_advanced"] = out["bad_advanced"].astype(np.uint8)
+    out["configs"] = np.asarray(BATCHED_CONFIGS, dtype=np.float64)
+    return out
+
+
 def save(name, data):
     np.savez_compressed(HERE / name, **data)
     print(name, {k: v.shape for k, v in data.items()})
@@ -187,6 +263,9 @@ def main():
     ref = Reference()
     if len(sys.argv) > 1 and sys.argv[1] == "tactics":
         save("tactics.npz", tactics_fixture(ref))
+        return
+    if len(sys.argv) > 1 and sys.argv[1] == "batched":
+        save("batched.npz", batched_fixture(ref))
         return
     from_board = lambda cells, to_play: RefState.from_board(ref, cells, to_play)  # noqa: E731
 

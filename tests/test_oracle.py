@@ -194,3 +194,174 @@ def test_replay_checks_restatement_rejects_reference_cases(oracle):
         assert replay_violation(*replay_sample(oracle, index, white)) is None
     for message, row in replay_corruptions(oracle):
         assert replay_violation(**row) == message
+
+
+# ---- BatchedPUCT (mcts/src/BatchedPUCT.cpp) ------------------------------------------
+
+BATCHED_FIELDS = ("visits", "priors", "move_values", "legal")
+BATCHED_EVALUATORS = ("hash", "uniform", "ramp")
+
+
+def batched_games(golden):
+    """The golden evaluation games grouped by configuration: yields
+    (config index, (simulations, leaf, c_puct, evaluator, reuse), [row indices of each game])."""
+    g = golden("batched.npz")
+    for ci, (sims, leaf, c, kind, reuse) in enumerate(g["configs"]):
+        games = [np.flatnonzero((g["cfg"] == ci) & (g["game"] == game)) for game in np.unique(g["game"])]
+        yield g, ci, (int(sims), int(leaf), float(c), BATCHED_EVALUATORS[int(kind)], bool(reuse)), games
+
+
+def check_batched_row(g, i, result, stats):
+    """One search of a golden game against the reference's outputs."""
+    assert np.array_equal(np.asarray(result["visits"]), g["visits"][i])
+    assert np.array_equal(np.asarray(result["priors"]), g["priors"][i])
+    assert np.array_equal(np.asarray(result["move_values"]), g["move_values"][i])
+    assert np.array_equal(np.asarray(result["legal"]).astype(np.uint8), g["legal"][i])
+    info = [result["best"], result["simulations"], result["nodes"], result["evaluations"]]
+    assert info == g["info"][i].tolist()
+    assert [result["root_value"], result["best_value"]] == g["values"][i].tolist()
+    assert list(stats) == g["stats"][i].tolist()
+
+
+def test_oracle_batched_search_replays_reference_games(oracle, golden):
+    """The restated BatchedPUCT reproduces, bit for bit, evaluation games
+    played by the reference's own searcher (tests/golden/batched.npz)."""
+    searches = 0
+    for g, ci, (sims, leaf, c, kind, reuse), games in batched_games(golden):
+        for rows in games:
+            searchers = [oracle.batched(sims, c, leaf, reuse, kind) for _ in range(2)]
+            for i in rows:
+                root = g["root"][i]
+                who = 0 if root[162] == 1 else 1
+                result = searchers[who].search(root)
+                check_batched_row(g, i, result, searchers[who].stats.values())
+                searches += 1
+                move = int(g["move"][i])
+                assert [s.advance(move) for s in searchers] == g["advanced"][i].astype(bool).tolist()
+                if g["bad_action"][i] != -100:
+                    bad = int(g["bad_action"][i])
+                    assert [s.advance(bad) for s in searchers] == g["bad_advanced"][i].astype(bool).tolist()
+                assert [list(s.stats.values()) for s in searchers] == g["stats_after"][i].tolist()
+    assert searches == len(g["cfg"])
+
+
+def test_oracle_batched_search_matches_reference_engine_directly(oracle, reference):
+    """Fresh games against the reference searcher, where it is built here."""
+    from oracle.oracle import RefState
+    rng = np.random.default_rng(5)
+    for sims, leaf, c, kind in ((20, 5, 1.2, "hash"), (36, 12, 0.6, "hash"), (12, 2, 3.0, "ramp")):
+        ours = [oracle.batched(sims, c, leaf, True, kind) for _ in range(2)]
+        theirs = [reference.batched(sims, c, leaf, True, kind) for _ in range(2)]
+        state = RefState.generated(reference, 91, sims)
+        for _ in range(30):
+            rec = state.record()
+            if rec[166] != 0:
+                break
+            who = 0 if rec[162] == 1 else 1
+            a, b = ours[who].search(rec), theirs[who].search(state)
+            for key in BATCHED_FIELDS:
+                assert np.array_equal(a[key], b[key])
+            assert {k: a[k] for k in a if k not in BATCHED_FIELDS} == {k: b[k] for k in b if k not in BATCHED_FIELDS}
+            assert ours[who].stats == theirs[who].stats
+            move = a["best"] if rng.random() < 0.6 else int(rng.choice(np.flatnonzero(a["legal"])))
+            assert state.play(move)
+            assert [s.advance(move) for s in ours] == [s.advance(move) for s in theirs]
+
+
+def split_board_record(oracle, actor):
+    """tests/batched_puct_test.cpp:171-179: Black holds columns 0-3 and the top
+    of column 4, White the rest; (4, 4) is the only empty cell."""
+    rec = oracle.initial(1, -1)[0]
+    for row in range(9):
+        for col in range(9):
+            if col < 4 or (col == 4 and row < 4):
+                rec[row * 9 + col] = 1
+            elif col > 4 or (col == 4 and row > 4):
+                rec[row * 9 + col] = 2
+    rec[162] = actor
+    return rec
+
+
+def test_oracle_batched_search_known_answers(oracle):
+    """The assertions of the reference's tests/batched_puct_test.cpp on the
+    restatement, with the tests' own fixed evaluator ("ramp")."""
+    # :89-115 budgets, batch sizes and statistics
+    for count in (1, 7, 19, 301):
+        s = oracle.batched(count, 1.5, 8, False, "ramp")
+        r = s.search(oracle.initial(1)[0])
+        st = s.stats
+        assert r["simulations"] == count and r["visits"].sum() == count
+        assert r["evaluations"] == st["network_evaluations"] <= count + 1
+        assert r["nodes"] <= count + 1 and st["max_observed_batch_size"] <= 8
+        if count >= 8:
+            assert st["max_observed_batch_size"] == 8
+    # :117-150 subtree reuse and visits counted per search
+    s = oracle.batched(64, 1.5, 8, True, "ramp")
+    root = oracle.initial(1)[0]
+    first = s.search(root)
+    assert s.stats["reused_nodes"] == 0 and s.stats["inherited_visits"] == 0
+    repeated = s.search(root)
+    assert s.stats["reused_nodes"] == first["nodes"] and s.stats["inherited_visits"] == 64
+    assert repeated["simulations"] == 64 and repeated["visits"].sum() == 64 and repeated["evaluations"] <= 64
+    assert s.advance(repeated["best"])
+    root, _ = oracle.play(root[None].copy(), [repeated["best"]])
+    after = s.search(root[0])
+    assert s.stats["reused_nodes"] > 0 and s.stats["inherited_visits"] > 0
+    assert s.stats["advance_calls"] == 1 and s.stats["reuse_hits"] == 1
+    assert after["visits"].sum() == 64 and after["nodes"] < repeated["nodes"] + 65
+    assert not s.advance(40) and not s.advance(-1)
+    again = s.search(root[0])
+    assert s.stats["reused_nodes"] == after["nodes"] and again["visits"].sum() == 64
+    assert s.stats["advance_calls"] == 3 and s.stats["reuse_hits"] == 1
+    s.clear()
+    assert s.search(root[0])["evaluations"] > 0 and s.stats["reused_nodes"] == 0
+    # :152-169 a state that differs in any field starts a new tree
+    s = oracle.batched(16, 1.5, 4, True, "ramp")
+    start = oracle.initial(1)[0]
+    s.search(start)
+    passed, _ = oracle.play(start[None].copy(), [81])
+    assert s.search(passed[0])["simulations"] == 16 and s.stats["reused_nodes"] == 0
+    setup = passed[0].copy()
+    setup[165] = 0
+    assert s.search(setup)["simulations"] == 16 and s.stats["reused_nodes"] == 0
+    assert s.search(oracle.initial(1, -1)[0])["simulations"] == 16 and s.stats["reused_nodes"] == 0
+    # :171-209 capture values without the network, terminal roots
+    for actor in (1, 2):
+        s = oracle.batched(32, 1.5, 8, True, "ramp")
+        rec = split_board_record(oracle, actor)
+        r = s.search(rec)
+        assert r["best"] == 40 and r["best_value"] == 1.0 and r["visits"].sum() == 32
+        assert r["evaluations"] == 1 and s.stats["inference_batches"] == 1
+        assert s.advance(40)
+        done, _ = oracle.play(rec[None].copy(), [40])
+        assert done[0][166] == 1  # capture
+        t = s.search(done[0])
+        assert t["root_value"] == -1.0 and s.stats["network_evaluations"] == 0 and t["best"] == -1
+    two = oracle.initial(1)
+    oracle.play(two, [81])
+    oracle.play(two, [81])
+    t = oracle.batched(8, 1.5, 8, True, "ramp").search(two[0])
+    assert t["best"] == -1 and t["simulations"] == 0 and not t["legal"].any() and t["root_value"] == -1.0
+    # :262-280 a whole game with two searchers that advance after every move
+    rec = oracle.initial(1)[0]
+    black, white = oracle.batched(16, 1.5, 4, True, "ramp"), oracle.batched(16, 1.5, 4, True, "ramp")
+    plies = 0
+    while rec[166] == 0 and plies < 164:
+        r = (black if rec[162] == 1 else white).search(rec)
+        assert r["visits"].sum() == 16
+        nxt, ok = oracle.play(rec[None].copy(), [r["best"]])
+        assert ok[0]
+        rec = nxt[0]
+        black.advance(r["best"])
+        white.advance(r["best"])
+        plies += 1
+    assert rec[166] != 0
+    # :57-87 one leaf per batch without reuse is the legacy search
+    start, _ = oracle.play(oracle.initial(1), [0])
+    start, _ = oracle.play(start, [81])
+    for count in (1, 31, 300):
+        legacy = oracle.puct(start[0], count)
+        r = oracle.batched(count, 1.5, 1, False, "hash").search(start[0])
+        assert np.array_equal(r["visits"], legacy["visits"]) and np.array_equal(r["priors"], legacy["priors"])
+        assert (r["best"], r["nodes"], r["evaluations"]) == (legacy["best"], legacy["nodes"], legacy["evaluations"])
+        assert (r["root_value"], r["best_value"]) == (legacy["root_value"], legacy["best_value"])
