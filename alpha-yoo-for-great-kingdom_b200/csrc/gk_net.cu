@@ -820,7 +820,7 @@ struct HeadOut {
     float* leaf_value;   // search mode: [B]
     const gk_bits* states;  // search mode: leaf states for the legal mask
     const int32_t* leaf;    // search mode: [B] leaf node (0: the root, masked by root_allow too)
-    const uint32_t* root_allow;  // search mode: [B][3] root candidates
+    const uint32_t* root_allow;  // search mode: [B][3] root candidates, or null (no root narrowing)
 };
 
 constexpr int kPolStride = 163;  // odd row stride: conflict-free lane-per-row reads
@@ -941,7 +941,8 @@ __global__ void __launch_bounds__(32 * kHeadWarps) net_heads_kernel(NetParams p,
                 for (int k = 0; k < 3; ++k) {
                     const int a = lane + 32 * k;
                     legal[k] = a < GK_ACTIONS && (a == GK_PASS ? true : gk_test(placements, a + a / 9) != 0) &&
-                               (out.leaf[tree] != 0 || ((out.root_allow[tree * 3 + k] >> lane) & 1u) != 0u);
+                               (out.root_allow == nullptr || out.leaf[tree] != 0 ||
+                                ((out.root_allow[tree * 3 + k] >> lane) & 1u) != 0u);
                     if (legal[k]) mx = fmaxf(mx, logit[k]);
                 }
 #pragma unroll
@@ -1145,6 +1146,18 @@ int gk_net_forward(const gk_net_t* net, const uint32_t* states, const float* fea
 int gk_net_evaluate_puct(const gk_net_t* net, void* ws, int64_t batch, int capacity, float* headfeat,
                          uint32_t* status, void* stream) {
     return net_evaluate(net, ws, batch, capacity, headfeat, status, as_stream(stream), nullptr, nullptr);
+}
+
+int gk_net_evaluate_states(const gk_net_t* net, const uint32_t* states, const int32_t* active,
+                           const int32_t* active_count, int64_t n, float* policy, float* value, float* headfeat,
+                           uint32_t* status, void* stream) {
+    if (!valid_net(net) || states == nullptr || active == nullptr || active_count == nullptr || n <= 0 ||
+        policy == nullptr || value == nullptr || headfeat == nullptr || status == nullptr)
+        return GK_EINVAL;
+    const gk_bits* bits = reinterpret_cast<const gk_bits*>(states);
+    NetInput in{bits, nullptr, active, active_count, n};
+    HeadOut out{nullptr, nullptr, policy, value, bits, nullptr, nullptr};
+    return run_forward(net, in, headfeat, out, status, as_stream(stream));
 }
 
 }  // extern "C"

@@ -13,3 +13,4 @@ from .gpu_rules import (  # noqa: F401
 from .gpu_puct import GpuPUCT, GpuPUCTOptions, GpuSearchResult, HashEvaluator  # noqa: F401
 from .training import Cell, EndReason, GameData, TrainingBatch, TrainingSample, collect_gpu_puct_games  # noqa: F401
 from .replay import DeviceReplayBuffer, validate_rows  # noqa: F401
+from .batched_puct import BatchedSearchResult, GpuBatchedPUCT, PUCTOptions  # noqa: F401

@@ -5,6 +5,7 @@
     encode   observation planes + legal masks for 65,536 and 2^20 generated positions
     puct     1024 trees x 800 simulations with the injected evaluator
     replay   replay-row checks of DeviceReplayBuffer ingest on 2^20 rows (3.66 GB)
+    batched  the evaluation searcher (BatchedPUCT) for 4096 games x 128 simulations, leaf batch 8
 
 Every timed launch is bracketed by CUDA events on the launching stream; an L2
 flush (a 256 MB write) separates timed launches so each one reads its inputs
@@ -216,4 +217,63 @@ def bench_replay(args, peaks):
           "metric": "rows/s", "value": n / (ms / 1e3), "unit": "rows/s", "ms": ms, "dtype": "f32",
           "roofline": {"bound": "hbm", "kernel": "replay_validate_kernel", "achieved": gbs, "peak": peaks[1],
                        "unit": "GB/s", "frac": gbs / peaks[1], "bytes_per_row": row_bytes},
+          "cpu_baseline": cpu})
+
+
+def bench_batched(args, peaks):
+    """The evaluation searcher (kingdom::BatchedPUCT, mcts/src/BatchedPUCT.cpp)
+    for `--searchers` games at once: `--sims` simulations in leaf batches of
+    `--leaf`, from generated positions, new trees every search. Two evaluators:
+    the injected one (the whole search is one launch) and the native 64ch x 6
+    block network (one network batch per wave over every game). CPU baseline:
+    the reference's own BatchedPUCT (oracle/_ref) with the injected evaluator
+    on a bounded sample, one thread."""
+    import time
+
+    from kingdom_ai import HashEvaluator
+    from kingdom_ai.batched_puct import GpuBatchedPUCT, PUCTOptions
+    from kingdom_ai.model import random_network
+
+    device = torch.device("cuda", 0)
+    flush = Flusher(device)
+    T, S, L = args.searchers, args.sims_batched, args.leaf
+    bits = positions(T, 4343, device)
+    search = GpuBatchedPUCT(T, PUCTOptions(simulations=S), L, reuse_tree=False)
+    hold = {}
+
+    def run(evaluator):
+        hold["r"] = search.search(bits, evaluator)
+
+    ms_hash = timed(lambda: run(HashEvaluator()), args.steps, args.warmup, flush)
+    r = hold["r"]
+    assert int(r.simulations.sum().item()) == T * S
+    nodes = float(r.nodes.float().mean().item())
+    net = random_network(64, 6, 1)
+    ms_net = timed(lambda: run(net), max(1, args.steps // 2), 1, flush)
+    r = hold["r"]
+    assert int(r.simulations.sum().item()) == T * S
+    batches = float(search.stats["inference_batches"].float().mean().item())
+    cpu = None
+    try:
+        from oracle.oracle import Reference, RefState
+        ref = Reference()
+        searcher = ref.batched(S, 1.5, L, False, "hash")
+        start, done = time.perf_counter(), 0
+        while time.perf_counter() - start < 10.0:
+            searcher.search(RefState.generated(ref, 4343, done))
+            done += 1
+        elapsed = time.perf_counter() - start
+        cpu = {"value": done * S / elapsed, "unit": "simulations/s", "cores": 1, "kind": "reference",
+               "sample": f"{done} searches of {S} simulations, leaf batch {L}, injected evaluator, "
+                         f"reference kingdom::BatchedPUCT, {elapsed:.1f} s"}
+    except Exception as exc:  # noqa: BLE001 - reported, not fatal
+        cpu = {"value": None, "unavailable": str(exc)}
+    emit({"workload": f"batched evaluation search: {T} games x {S} simulations, leaf batch {L}, c_puct 1.5, "
+                      "generated positions, new trees every search",
+          "metric": "simulations/s", "unit": "simulations/s",
+          "value": T * S / (ms_hash / 1e3), "ms_per_search": ms_hash, "evaluator": "injected (one launch)",
+          "nodes_mean": nodes,
+          "network": {"value": T * S / (ms_net / 1e3), "ms_per_search": ms_net,
+                      "evaluator": "native 64ch x 6-block bf16 network, one batch per wave",
+                      "waves_per_search": batches},
           "cpu_baseline": cpu})

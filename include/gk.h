@@ -274,6 +274,16 @@ GK_API int gk_net_forward(const gk_net_t* net, const uint32_t* states, const flo
 GK_API int gk_net_evaluate_puct(const gk_net_t* net, void* ws, int64_t batch, int capacity, float* headfeat,
                                 uint32_t* status, void* stream);
 
+/* Network evaluation of a gathered set of packed states: for i <
+ * *active_count, state active[i] (uint32[16] each) is evaluated and its masked
+ * softmax policy over legal actions and its value are written to row
+ * active[i] of policy fp32[n,82] and value fp32[n]. Used by the batched
+ * evaluation search (gk_bpuct_*) for its leaf slots; the reference calls the
+ * model through EncodedBatchedEvaluator (python/kingdom_ai/encoded_batching.py:71-95). */
+GK_API int gk_net_evaluate_states(const gk_net_t* net, const uint32_t* states, const int32_t* active,
+                                  const int32_t* active_count, int64_t n, float* policy, float* value,
+                                  float* headfeat, uint32_t* status, void* stream);
+
 /* ------------------------------------------------------------ self-play */
 
 /* Per-ply self-play parameters (GpuPUCTOptions plus the temperature schedule
@@ -340,6 +350,114 @@ GK_API int gk_selfplay_buffers(void* ws, int64_t lanes, gk_selfplay_buffers_t* o
 GK_API int gk_selfplay_ply(void* sp_ws, void* puct_ws, int64_t lanes, const gk_net_t* net,
                            const gk_selfplay_params_t* params, const gk_replay_t* replay, float* headfeat,
                            uint32_t* status, void* timer, void* stream);
+
+/* ------------------------------------------------------ batched search */
+
+/* kingdom::BatchedPUCT (mcts/include/BatchedPUCT.h:38-60,
+ * mcts/src/BatchedPUCT.cpp) for many searchers at once: one workspace holds
+ * `trees` trees of at most `capacity` nodes, and each search runs in waves
+ * that collect up to `leaf_batch` pending leaves per tree under a virtual
+ * loss of one, evaluate them together and back them up in collection order.
+ * Trees persist between searches; gk_bpuct_advance keeps the played move's
+ * subtree (reuse). A search adds at most `simulations` nodes to a tree, so a
+ * caller keeps capacity >= nodes held + simulations + 1 (gk_bpuct_grow).
+ * Per-tree statistics, GK_BPUCT_STAT_* order (BatchedPUCTStatistics,
+ * BatchedPUCT.h:21-31): */
+#define GK_BPUCT_STAT_EVALS 0        /* network evaluations of the last search */
+#define GK_BPUCT_STAT_BATCHES 1      /* inference batches of the last search */
+#define GK_BPUCT_STAT_MAX_BATCH 2    /* largest batch of the last search */
+#define GK_BPUCT_STAT_REUSED 3       /* nodes held when the last search began */
+#define GK_BPUCT_STAT_INHERITED 4    /* root visits when the last search began */
+#define GK_BPUCT_STAT_ADVANCES 5     /* advance calls (cumulative) */
+#define GK_BPUCT_STAT_REUSE_HITS 6   /* advances that kept a subtree (cumulative) */
+#define GK_BPUCT_STATS 7
+/* Evaluation failures of a batched search, besides GK_ERR_BAD_EVAL (a value
+ * not finite or outside [-1, 1], BatchedPUCT.cpp:73-75): */
+#define GK_BPUCT_ERR_POLICY (1u << 4)    /* a weight not finite or negative (BatchedPUCT.cpp:76-80) */
+#define GK_BPUCT_ERR_NO_WEIGHT (1u << 5) /* no positive weight on a legal action (BatchedPUCT.cpp:233-236) */
+
+typedef struct {
+    int64_t* actions;      /* [T] best action (BatchedPUCT.cpp:118-123), -1 when none */
+    int32_t* visits;       /* [T,82] visits gained in this search */
+    double* priors;        /* [T,82] root edge priors */
+    double* move_values;   /* [T,82] mean value gained in this search */
+    uint8_t* legal;        /* [T,82] the root's edges (its legal actions) */
+    int32_t* simulations;  /* [T] */
+    int32_t* nodes;        /* [T] tree size after the search */
+    double* root_values;   /* [T] */
+    double* best_values;   /* [T] */
+    int32_t* stats;        /* [T,GK_BPUCT_STATS] */
+    uint32_t* errors;      /* [T] GK_ERR_* of this search; a failed tree is cleared */
+    uint32_t* status;      /* [1] OR of errors, or NULL */
+} gk_bpuct_results_t;
+
+typedef struct {
+    uint8_t* needs_eval;   /* [T*L] slot holds a leaf to evaluate */
+    uint32_t* leaf_bits;   /* [T*L,16] packed leaf states */
+    double* policy;        /* [T*L,82] evaluator weights (read unless float_eval) */
+    double* value;         /* [T*L] */
+    float* policy_f;       /* [T*L,82] fp32 evaluator output (float_eval) */
+    float* value_f;        /* [T*L] */
+    int32_t* active;       /* [T*L] slots compacted by gk_bpuct_compact */
+    int32_t* active_count; /* [1] */
+    int32_t* pending;      /* [T] leaves of the current wave */
+    int32_t* node_count;   /* [T] nodes held */
+    int32_t* remaining;    /* [1] max over trees of simulations left after the last wave */
+    int32_t* stats;        /* [T,GK_BPUCT_STATS] current statistics */
+} gk_bpuct_buffers_t;
+
+/* Bytes of a batched-search workspace (0 for invalid sizes). Stands in for
+ * the per-searcher node vectors of BatchedPUCT::Impl (BatchedPUCT.cpp:134-140). */
+GK_API size_t gk_bpuct_workspace_bytes(int64_t trees, int capacity, int leaf_batch);
+/* Device pointers of the workspace's evaluator interface and counters. */
+GK_API int gk_bpuct_buffers(void* ws, int64_t trees, int capacity, int leaf_batch, gk_bpuct_buffers_t* out);
+/* Empty trees and zero counters (once, after allocating the workspace). */
+GK_API int gk_bpuct_init(void* ws, int64_t trees, int capacity, int leaf_batch, void* stream);
+/* BatchedPUCT::clear (BatchedPUCT.cpp:286) of the trees with mask[t] != 0 (NULL: all). */
+GK_API int gk_bpuct_clear(void* ws, int64_t trees, int capacity, int leaf_batch, const uint8_t* mask,
+                          void* stream);
+/* Start a search of the trees with mask[t] != 0 (NULL: all) from packed roots
+ * (BatchedPUCT.cpp:339-367): a tree that does not continue from its root, or
+ * any tree when reuse is 0, is cleared; a finished root clears the tree and
+ * gives its terminal value; an unexpanded root is queued in slot 0. */
+GK_API int gk_bpuct_begin(void* ws, int64_t trees, int capacity, int leaf_batch, const uint32_t* roots,
+                          const uint8_t* mask, int simulations, int reuse, void* stream);
+/* Expand the queued roots from their evaluations (one batch of one each,
+ * BatchedPUCT.cpp:361-365) and record the root edges results are measured from. */
+GK_API int gk_bpuct_root_expand(void* ws, int64_t trees, int capacity, int leaf_batch, int float_eval,
+                                void* stream);
+/* One wave's selection (BatchedPUCT.cpp:377-404): per tree, leaves until the
+ * wave holds min(simulations left, leaf_batch); finished leaves are backed up
+ * at once. Also zeroes *remaining. */
+GK_API int gk_bpuct_collect(void* ws, int64_t trees, int capacity, int leaf_batch, double c_puct, void* stream);
+/* The injected evaluator (include/gk_common.h) on every slot that needs one;
+ * stands in for the reference's batch callback (BatchedPUCT.cpp:252-268). */
+GK_API int gk_bpuct_hash_eval(void* ws, int64_t trees, int capacity, int leaf_batch, void* stream);
+/* Device-side list of the slots that need an evaluation (active, active_count):
+ * the positions vector of BatchedPUCT.cpp:381-401, without a host round trip. */
+GK_API int gk_bpuct_compact(void* ws, int64_t trees, int capacity, int leaf_batch, void* stream);
+/* One wave's expansion, release and backup in collection order
+ * (BatchedPUCT.cpp:405-413); a rejected evaluation (BatchedPUCT.cpp:72-81,
+ * 233-236) sets GK_ERR_BAD_EVAL, GK_BPUCT_ERR_POLICY or GK_BPUCT_ERR_NO_WEIGHT
+ * on its tree. */
+GK_API int gk_bpuct_expand(void* ws, int64_t trees, int capacity, int leaf_batch, int float_eval, void* stream);
+/* Results of the search (BatchedPUCT.cpp:415-434); failed trees are cleared. */
+GK_API int gk_bpuct_finish(void* ws, int64_t trees, int capacity, int leaf_batch, const gk_bpuct_results_t* out,
+                           void* stream);
+/* BatchedPUCT::advance (BatchedPUCT.cpp:290-326) of the trees with mask[t] != 0
+ * by actions[t]: advanced[t] = 1 when the subtree was kept; an illegal action
+ * leaves the tree as it is; a legal one without a child clears it. */
+GK_API int gk_bpuct_advance(void* ws, int64_t trees, int capacity, int leaf_batch, const int32_t* actions,
+                            const uint8_t* mask, int reuse, uint8_t* advanced, void* stream);
+/* A whole search with the injected evaluator in one launch (begin, waves,
+ * finish): BatchedPUCT::search (BatchedPUCT.cpp:328-442) with the callback on the device. */
+GK_API int gk_bpuct_search_hash(void* ws, int64_t trees, int capacity, int leaf_batch, const uint32_t* roots,
+                                const uint8_t* mask, int simulations, int reuse, double c_puct,
+                                const gk_bpuct_results_t* out, void* stream);
+/* Copy every tree into a workspace with more nodes per tree (the reference's
+ * node vector grows on demand, BatchedPUCT.cpp:183-185). */
+GK_API int gk_bpuct_grow(const void* src, int capacity, void* dst, int new_capacity, int64_t trees,
+                         int leaf_batch, void* stream);
 
 /* --------------------------------------------------------------- replay */
 
