@@ -298,6 +298,9 @@ class GpuBatchedPUCT:
         return mask.to(torch.uint8).contiguous()
 
     def _ensure_capacity(self, stream):
+        if not self._reuse:
+            # every searched tree starts empty (BatchedPUCT.cpp:346)
+            self._node_bound = 0
         need = self._node_bound + self._options.simulations + 1
         if need <= self._ws.capacity:
             return
@@ -333,14 +336,22 @@ class GpuBatchedPUCT:
         raise TypeError("PUCT requires a policy/value evaluator")
 
     def _results(self):
-        T, dev = self.trees, self.device
-        z = lambda shape, dtype: torch.zeros(shape, dtype=dtype, device=dev)  # noqa: E731
-        out = dict(actions=torch.full((T,), -1, dtype=torch.int64, device=dev),
-                   visits=z((T, ACTION_SIZE), torch.int32), priors=z((T, ACTION_SIZE), torch.float64),
-                   move_values=z((T, ACTION_SIZE), torch.float64), legal=z((T, ACTION_SIZE), torch.uint8),
-                   simulations=z((T,), torch.int32), nodes=z((T,), torch.int32), root_values=z((T,), torch.float64),
-                   best_values=z((T,), torch.float64), stats=z((T, len(STAT_NAMES)), torch.int32),
-                   errors=z((T,), torch.int32), status=z((1,), torch.int32))
+        """Result tensors carved from one allocation. The finish kernel writes
+        every field of every tree, so nothing needs clearing first."""
+        T = self.trees
+        fields = (("actions", (T,), torch.int64), ("priors", (T, ACTION_SIZE), torch.float64),
+                  ("move_values", (T, ACTION_SIZE), torch.float64), ("root_values", (T,), torch.float64),
+                  ("best_values", (T,), torch.float64), ("visits", (T, ACTION_SIZE), torch.int32),
+                  ("simulations", (T,), torch.int32), ("nodes", (T,), torch.int32),
+                  ("stats", (T, len(STAT_NAMES)), torch.int32), ("errors", (T,), torch.int32),
+                  ("status", (1,), torch.int32), ("legal", (T, ACTION_SIZE), torch.uint8))
+        sizes = [math.prod(shape) * torch.empty((), dtype=dtype).element_size() for _, shape, dtype in fields]
+        padded = [(n + 255) // 256 * 256 for n in sizes]
+        storage = torch.empty(sum(padded), dtype=torch.uint8, device=self.device)
+        out, offset = {}, 0
+        for (name, shape, dtype), n, step in zip(fields, sizes, padded):
+            out[name] = storage[offset:offset + n].view(dtype).view(shape)
+            offset += step
         struct = _Results(*(out[name].data_ptr() for name, _ in _Results._fields_))
         return out, struct
 
