@@ -46,9 +46,9 @@ namespace gk {
 
 template <int C>
 struct NetCfg {
-    static_assert(C == 64 || C == 128, "channels must be 64 or 128");
-    static constexpr int G = C == 64 ? 5 : 2;    // images per group
-    static constexpr int T = C == 64 ? 4 : 2;    // 128-row tiles per group (>= 100*G rows)
+    static_assert(C == 32 || C == 64 || C == 128, "channels must be 32, 64 or 128");
+    static constexpr int G = C == 32 ? 10 : C == 64 ? 5 : 2;  // images per group
+    static constexpr int T = C == 32 ? 8 : C == 64 ? 4 : 2;   // 128-row tiles per group (>= 100*G rows)
     static constexpr int HALO = 11;              // max |tap row shift| = 10 + 1
     // Rows a kept output reads: the group's G*100 rows and a zero halo either
     // side. The tail of the last tile (rows G*100 .. T*128-1) is computed but
@@ -59,13 +59,17 @@ struct NetCfg {
     static constexpr int CHUNK = ROWS * 16;      // bytes between 8-channel chunks
     static constexpr int ACT = (C / 8) * CHUNK;  // one activation buffer
     static constexpr int SLOT = C * C * 2;       // one tap of weights (bf16)
-    static constexpr int NSLOT = C == 64 ? 11 : 3;
-    static constexpr bool TILE_OUTER = C == 64;  // all 9 taps resident: tile-major issue order
+    static constexpr int NSLOT = C <= 64 ? 11 : 3;
+    static constexpr bool TILE_OUTER = C <= 64;  // all 9 taps resident: tile-major issue order
     static constexpr int EPI_WARPS = 8;          // two per TMEM lane quadrant, each half the channels
+    static constexpr int HALF = C / 2;           // channels of one epilogue warp
+    static constexpr int W = HALF < 32 ? HALF : 32;  // TMEM columns per load
+    // GroupNorm partial sums: [image][group][32-row chunk of the image, <= 5]
+    static constexpr int GN_PARTS = G * 8 * 5;
     static constexpr int THREADS = 64 + 32 * EPI_WARPS;
-    static constexpr int NBARS = 2 * NSLOT + 2 * T + 2;  // + mma_idle, heads_ready
+    static constexpr int NBARS = 2 * NSLOT + 2 * T + 3;  // + mma_idle, heads_ready, gn_ready
     static constexpr int HEADW = (3 * C + 3 + 3) / 4 * 4;  // head 1x1 weights + biases (floats)
-    static constexpr int SMEM = 2 * ACT + NSLOT * SLOT + NBARS * 8 + 16 + HEADW * 4;
+    static constexpr int SMEM = 2 * ACT + NSLOT * SLOT + NBARS * 8 + 16 + HEADW * 4 + 2 * GN_PARTS * 4;
     static constexpr uint32_t IDESC = tc::idesc_bf16(128, C);
     static_assert(2 * T * C <= 512, "two layers of accumulators must fit in TMEM");
     static_assert(TAIL >= 0 && TAIL * 16 <= NSLOT * SLOT, "tail reads stay inside the shared-memory allocation");
@@ -74,15 +78,19 @@ struct NetCfg {
 
 struct NetParams {
     int channels, blocks;
+    int norm;               // 0 batch norm folded, 1 GroupNorm (include/gk.h, gk_net_t)
+    const float* norm_w;    // [layers][C] GroupNorm weight (norm 1)
+    const float* norm_b;    // [layers][C] GroupNorm bias (norm 1)
+    const float* head_norm; // [6] head GroupNorm weights and biases (norm 1)
     const uint8_t* conv_w;  // per layer, per tap: [Cin/8][Cout][8] bf16 (stem Cin padded to 16)
     const float* conv_b;    // [layers][C]
     const float* head_w;    // [3][C]: policy 1x1 (2 rows) then value 1x1 (BN folded)
     const float* head_b;    // [3]
     const float* pol_w;     // [82][162]
     const float* pol_b;     // [82]
-    const float* val_w1;    // [64][81]
-    const float* val_b1;    // [64]
-    const float* val_w2;    // [64]
+    const float* val_w1;    // [H][81], H = 64 (norm 0) or C (norm 1)
+    const float* val_b1;    // [H]
+    const float* val_w2;    // [H]
     const float* val_b2;    // [1]
 };
 
@@ -247,7 +255,83 @@ __device__ __forceinline__ bool issue_layer(uint32_t tmem_d, uint32_t a_lo, uint
     return true;
 }
 
+// W TMEM columns (16 or 32) of this thread's lane.
+template <int W>
+__device__ __forceinline__ void tmem_ldw(uint32_t taddr, float (&v)[W]) {
+    if constexpr (W == 16) tc::tmem_ld16(taddr, v);
+    else tc::tmem_ld32(taddr, v);
+}
+
+// GroupNorm statistics of the reference network (GroupNorm(gcd(8, C), C),
+// python/kingdom_ai/model.py:17-23, 46-47): per image and group of C/8
+// channels, over the 81 cells. A 32-row chunk k of a group's rows meets at
+// most two images; image `img` spans chunks gn_first(img) .. gn_last(img),
+// at most five, and each chunk's warp stores its partial sums in slot
+// [img][group][k - gn_first(img)], so the combine below adds them in a fixed
+// order and the statistics do not depend on warp timing.
+__device__ __forceinline__ int gn_first(int img) { return img * 100 / 32; }
+__device__ __forceinline__ int gn_last(int img) { return (img * 100 + 99) / 32; }
+
+__device__ __forceinline__ float gn_total(const float* parts, int img, int grp) {
+    const float* p = parts + (img * 8 + grp) * 5;
+    float s = 0.0f;
+    for (int j = 0, n = gn_last(img) - gn_first(img); j <= n; ++j) s += p[j];
+    return s;
+}
+
+// One pass of this warp over the accumulator of tile t: per group of the
+// warp's half (four groups), the sum over valid cells of x (centred == false)
+// or of (x - mean)^2 (centred == true, means from `sums`), reduced over the
+// warp separately for the two images a chunk can meet, into `parts`.
 template <int C>
+__device__ __forceinline__ void gn_partials(uint32_t tacc, int t, int q, int lane, int col0, int nimg, bool centred,
+                                            const float* sums, float* parts) {
+    using K = NetCfg<C>;
+    constexpr int W = K::W, CG = C / 8;
+    const int m0 = t * 128 + q * 32, m = m0 + lane;
+    const int img = m / 100, pos = m - img * 100, r = pos / 10, cc = pos - r * 10;
+    const bool valid = img < nimg && r < 9 && cc < 9;
+    const int g0 = col0 / CG;
+    float mu[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+    if (centred && valid) {
+#pragma unroll
+        for (int gi = 0; gi < 4; ++gi) mu[gi] = gn_total(sums, img, g0 + gi) / (float)(81 * CG);
+    }
+    float acc[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+#pragma unroll
+    for (int cb = 0; cb < K::HALF / W; ++cb) {
+        float v[W];
+        tmem_ldw<W>(tacc + (uint32_t)(col0 + cb * W), v);
+#pragma unroll
+        for (int j = 0; j < W; ++j) {
+            const int gi = (cb * W + j) / CG;
+            const float d = v[j] - mu[gi];
+            acc[gi] += valid ? (centred ? d * d : v[j]) : 0.0f;
+        }
+    }
+    const int img0 = m0 / 100;
+    const bool second = img != img0;
+#pragma unroll
+    for (int gi = 0; gi < 4; ++gi) {
+        float a = second ? 0.0f : acc[gi], b = second ? acc[gi] : 0.0f;
+#pragma unroll
+        for (int off = 16; off; off >>= 1) {
+            a += __shfl_xor_sync(0xffffffffu, a, off);
+            b += __shfl_xor_sync(0xffffffffu, b, off);
+        }
+        if (lane == 0) {
+            const int k = t * 4 + q;
+            if (img0 < K::G) parts[(img0 * 8 + g0 + gi) * 5 + (k - gn_first(img0))] = a;
+            if (img0 + 1 < K::G && (m0 + 31) / 100 == img0 + 1)
+                parts[((img0 + 1) * 8 + g0 + gi) * 5 + (k - gn_first(img0 + 1))] = b;
+        }
+    }
+}
+
+// GN: the reference's GroupNorm network (p.norm == 1); otherwise batch norm
+// folded into conv_b. Two instantiations keep the batch-norm epilogue free of
+// the GroupNorm passes.
+template <int C, bool GN>
 __global__ void __launch_bounds__(NetCfg<C>::THREADS, 1)
     net_tower_kernel(NetParams p, NetInput in, float* headfeat, uint32_t* status) {
     using K = NetCfg<C>;
@@ -258,12 +342,15 @@ __global__ void __launch_bounds__(NetCfg<C>::THREADS, 1)
     uint64_t* const bars = reinterpret_cast<uint64_t*>(slots + K::NSLOT * K::SLOT);
     uint32_t* const tmem_holder = reinterpret_cast<uint32_t*>(bars + K::NBARS);
     float* const headw = reinterpret_cast<float*>(tmem_holder + 4);  // [3][C] then [3] biases
+    float* const gn_sum = headw + K::HEADW;    // GroupNorm partial sums (norm 1)
+    float* const gn_sq = gn_sum + K::GN_PARTS;  // and centred squares
     const uint32_t slot_full = tc::smem_u32(bars);
     const uint32_t slot_free = slot_full + 8 * K::NSLOT;
     const uint32_t acc_full = slot_free + 8 * K::NSLOT;
     const uint32_t epi_done = acc_full + 8 * K::T;
     const uint32_t mma_idle = epi_done + 8 * K::T;
     const uint32_t heads_ready = mma_idle + 8;
+    const uint32_t gn_ready = heads_ready + 8;
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int NL = 1 + 2 * p.blocks;  // MMA layers per group
@@ -274,13 +361,13 @@ __global__ void __launch_bounds__(NetCfg<C>::THREADS, 1)
     for (int i = threadIdx.x; i < 2 * K::ACT / 16; i += blockDim.x)
         reinterpret_cast<uint4*>(smem)[i] = make_uint4(0, 0, 0, 0);
     for (int i = threadIdx.x; i < 3 * C; i += blockDim.x) headw[i] = p.head_w[i];
-    if (threadIdx.x < 3) headw[3 * C + threadIdx.x] = p.head_b[threadIdx.x];
+    if (threadIdx.x < 3) headw[3 * C + threadIdx.x] = p.norm ? 0.0f : p.head_b[threadIdx.x];
     tc::fence_proxy_async_smem();
     if (threadIdx.x == 0) {
         // epi_done and heads_ready complete when every epilogue warp has arrived.
         for (int b = 0; b < K::NBARS; ++b) {
             const uint32_t bar = slot_full + 8 * b;
-            const bool per_warp = (bar >= epi_done && bar < mma_idle) || bar == heads_ready;
+            const bool per_warp = (bar >= epi_done && bar < mma_idle) || bar == heads_ready || bar == gn_ready;
             tc::mbar_init(bar, per_warp ? (uint32_t)K::EPI_WARPS : 1u);
         }
         tc::fence_mbar_init();
@@ -337,11 +424,13 @@ __global__ void __launch_bounds__(NetCfg<C>::THREADS, 1)
         __syncwarp();
     } else if (warp >= 2) {
         // ------- epilogue: 8 warps; warp -> (TMEM lane quadrant, half of the channels) -------
-        constexpr int HALF = C / 2;
+        constexpr int HALF = K::HALF, W = K::W, CG = C / 8;
         const int e = warp - 2;
         const int q = warp & 3;          // TMEM lanes 32q..32q+31 = tile rows
         const int col0 = (e >> 2) * HALF; // this warp's channels [col0, col0 + C/2)
         const int etid = threadIdx.x - 64;
+        constexpr bool gn = GN;
+        uint32_t gn_phase = 0;
         int i = 0;
         for (int g = blockIdx.x; g < groups; g += gridDim.x, ++i) {
             const int base_img = g * K::G;
@@ -355,34 +444,73 @@ __global__ void __launch_bounds__(NetCfg<C>::THREADS, 1)
             for (int l = 0; l < NL; ++l) {
                 const int a = i * NL + l;
                 const uint32_t colbase = (uint32_t)((a & 1) * K::T * C);
+                const uint32_t tq = tmem + ((uint32_t)(q * 32) << 16) + colbase;  // this quadrant's accumulators
                 uint8_t* const out = l % 2 == 0 ? bufP : bufQ;
                 const bool residual = l >= 2 && l % 2 == 0;
                 const bool last = l == NL - 1;
-                float bias[HALF];
+                float bias[GN ? 1 : HALF];
+                if constexpr (!GN) {
 #pragma unroll
-                for (int j = 0; j < HALF; ++j) bias[j] = __ldg(p.conv_b + l * C + col0 + j);
+                    for (int j = 0; j < HALF; ++j) bias[j] = __ldg(p.conv_b + l * C + col0 + j);
+                }
+                if constexpr (GN) {
+                    // GroupNorm statistics: sums, then centred squares, each
+                    // followed by a bounded barrier of the eight warps.
+                    for (int t = 0; t < K::T; ++t) {
+                        if (!warp_wait(acc_full + 8 * t, (uint32_t)a & 1u, status, lane == 0)) goto epi_done_label;
+                        tc::tc_fence_after();
+                        gn_partials<C>(tq + t * C, t, q, lane, col0, nimg, false, gn_sum, gn_sum);
+                    }
+                    for (int pass = 0; pass < 2; ++pass) {
+                        if (pass == 1) {
+                            for (int t = 0; t < K::T; ++t) gn_partials<C>(tq + t * C, t, q, lane, col0, nimg, true, gn_sum, gn_sq);
+                        }
+                        __syncwarp();
+                        if (lane == 0) tc::mbar_arrive(gn_ready);
+                        if (!warp_wait(gn_ready, gn_phase & 1u, status, lane == 0)) goto epi_done_label;
+                        ++gn_phase;
+                        __threadfence_block();
+                    }
+                }
                 for (int t = 0; t < K::T; ++t) {
-                    if (!warp_wait(acc_full + 8 * t, (uint32_t)a & 1u, status, lane == 0)) goto epi_done_label;
+                    if (!gn && !warp_wait(acc_full + 8 * t, (uint32_t)a & 1u, status, lane == 0)) goto epi_done_label;
                     tc::tc_fence_after();
                     const int m = t * 128 + q * 32 + lane;
                     const int img = m / 100, pos = m - img * 100, r = pos / 10, cc = pos - r * 10;
                     const bool valid = img < nimg && r < 9 && cc < 9;
                     const bool stored = m < K::G * 100;  // tail rows of the last tile are dropped
                     uint8_t* const row = out + (K::HALO + m) * 16;
+                    float mean[4] = {0.0f, 0.0f, 0.0f, 0.0f}, rstd[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+                    if (gn && valid) {
 #pragma unroll
-                    for (int cb = 0; cb < HALF / 32; ++cb) {
-                        const int ch0 = col0 + cb * 32;
-                        float v[32];
-                        tc::tmem_ld32(tmem + ((uint32_t)(q * 32) << 16) + colbase + t * C + ch0, v);
-                        uint4 res[4];
+                        for (int gi = 0; gi < 4; ++gi) {
+                            const int grp = col0 / CG + gi;
+                            mean[gi] = gn_total(gn_sum, img, grp) / (float)(81 * CG);
+                            rstd[gi] = 1.0f / sqrtf(gn_total(gn_sq, img, grp) / (float)(81 * CG) + 1e-5f);
+                        }
+                    }
+#pragma unroll
+                    for (int cb = 0; cb < HALF / W; ++cb) {
+                        const int ch0 = col0 + cb * W;
+                        float v[W];
+                        tmem_ldw<W>(tq + t * C + ch0, v);
+                        uint4 res[W / 8];
                         if (residual && stored) {
 #pragma unroll
-                            for (int k = 0; k < 4; ++k)
+                            for (int k = 0; k < W / 8; ++k)
                                 res[k] = *reinterpret_cast<const uint4*>(row + (ch0 / 8 + k) * K::CHUNK);
                         }
 #pragma unroll
-                        for (int j = 0; j < 32; ++j) {
-                            float x = v[j] + bias[cb * 32 + j];
+                        for (int j = 0; j < W; ++j) {
+                            float x;
+                            if constexpr (GN) {
+                                // torch's fused GroupNorm form: y = a x + b, a = rstd w, b = bias - a mean
+                                const int gi = (cb * W + j) / CG;
+                                const float sa = rstd[gi] * __ldg(p.norm_w + l * C + ch0 + j);
+                                x = sa * v[j] + (__ldg(p.norm_b + l * C + ch0 + j) - sa * mean[gi]);
+                            } else {
+                                x = v[j] + bias[cb * W + j];
+                            }
                             if (residual) {
                                 const uint4 rv = res[j >> 3];
                                 const uint32_t w = (j & 7) < 2 ? rv.x : (j & 7) < 4 ? rv.y : (j & 7) < 6 ? rv.z : rv.w;
@@ -391,7 +519,7 @@ __global__ void __launch_bounds__(NetCfg<C>::THREADS, 1)
                             v[j] = valid ? fmaxf(x, 0.0f) : 0.0f;
                         }
 #pragma unroll
-                        for (int k = 0; k < 4 && stored; ++k) {
+                        for (int k = 0; k < W / 8 && stored; ++k) {
                             const uint4 o = make_uint4(pack_bf16x2(v[8 * k], v[8 * k + 1]),
                                                        pack_bf16x2(v[8 * k + 2], v[8 * k + 3]),
                                                        pack_bf16x2(v[8 * k + 4], v[8 * k + 5]),
@@ -431,9 +559,10 @@ __global__ void __launch_bounds__(NetCfg<C>::THREADS, 1)
                     }
                 }
                 float* hf = headfeat + (int64_t)(base_img + img) * 243 + r * 9 + cc;
-                hf[0] = fmaxf(h0, 0.0f);
-                hf[81] = fmaxf(h1, 0.0f);
-                hf[162] = fmaxf(h2, 0.0f);
+                // With GroupNorm the heads kernel normalises the raw outputs first.
+                hf[0] = gn ? h0 : fmaxf(h0, 0.0f);
+                hf[81] = gn ? h1 : fmaxf(h1, 0.0f);
+                hf[162] = gn ? h2 : fmaxf(h2, 0.0f);
             }
         }
     epi_done_label:;
@@ -827,8 +956,10 @@ constexpr int kPolStride = 163;  // odd row stride: conflict-free lane-per-row r
 constexpr int kValStride = 81;
 constexpr int kHeadWarps = 8;   // per block
 constexpr int kHeadPos = 4;     // positions per warp: each weight read from shared memory feeds four
-constexpr size_t kHeadSmem =
-    (size_t)(82 * kPolStride + 64 * kValStride + kHeadWarps * kHeadPos * 244) * sizeof(float);
+// Shared memory of the heads kernel for a value head of H hidden units.
+constexpr size_t head_smem(int H) {
+    return (size_t)(82 * kPolStride + H * kValStride + kHeadWarps * kHeadPos * 244) * sizeof(float);
+}
 
 // Copies an N-float row-major matrix of COLS columns into shared memory with
 // row stride STRIDE, as 4-byte asynchronous copies: every copy of the block
@@ -842,14 +973,18 @@ __device__ __forceinline__ void stage_matrix(float* dst, const float* src) {
     }
 }
 
+// H = value-head hidden units: 64 for the batch-norm layout, C for the
+// reference's GroupNorm network (python/kingdom_ai/model.py:58-66).
+template <int H>
 __global__ void __launch_bounds__(32 * kHeadWarps) net_heads_kernel(NetParams p, const float* headfeat, NetInput in,
                                                                HeadOut out) {
+    constexpr int HU = H / 32;  // hidden units per lane
     extern __shared__ float hs[];
     float* wp = hs;
     float* w1 = wp + 82 * kPolStride;
-    float* feat_all = w1 + 64 * kValStride;
+    float* feat_all = w1 + H * kValStride;
     stage_matrix<82 * 162, 162, kPolStride>(wp, p.pol_w);
-    stage_matrix<64 * 81, 81, kValStride>(w1, p.val_w1);
+    stage_matrix<H * 81, 81, kValStride>(w1, p.val_w1);
     asm volatile("cp.async.wait_all;" ::: "memory");
     __syncthreads();
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -862,8 +997,7 @@ __global__ void __launch_bounds__(32 * kHeadWarps) net_heads_kernel(NetParams p,
     const float* wa = wp + lane * kPolStride;
     const float* wb = wp + (lane + 32) * kPolStride;
     const float* wc = wp + (lane + 64 < GK_ACTIONS ? lane + 64 : GK_ACTIONS - 1) * kPolStride;
-    const float* va = w1 + lane * kValStride;
-    const float* vb = w1 + (lane + 32) * kValStride;
+    const bool gn = p.norm != 0;
     for (int img0 = (blockIdx.x * kHeadWarps + warp) * kHeadPos; img0 < count;
          img0 += gridDim.x * kHeadWarps * kHeadPos) {
 #pragma unroll
@@ -873,6 +1007,47 @@ __global__ void __launch_bounds__(32 * kHeadWarps) net_heads_kernel(NetParams p,
             float fv[8];
 #pragma unroll
             for (int v = 0; v < 8; ++v) fv[v] = img < count && lane + 32 * v < 243 ? __ldg(hf + lane + 32 * v) : 0.f;
+            if (gn) {
+                // GroupNorm(1, 2) over the 162 policy features and
+                // GroupNorm(1, 1) over the 81 value features, then ReLU
+                // (python/kingdom_ai/model.py:51-63; eps 1e-5).
+                float sp = 0.f, sv = 0.f;
+#pragma unroll
+                for (int v = 0; v < 8; ++v) {
+                    const int idx = lane + 32 * v;
+                    if (idx < 162) sp += fv[v];
+                    else if (idx < 243) sv += fv[v];
+                }
+#pragma unroll
+                for (int off = 16; off; off >>= 1) {
+                    sp += __shfl_xor_sync(0xffffffffu, sp, off);
+                    sv += __shfl_xor_sync(0xffffffffu, sv, off);
+                }
+                const float mp = sp / 162.f, mv = sv / 81.f;
+                float qp = 0.f, qv = 0.f;
+#pragma unroll
+                for (int v = 0; v < 8; ++v) {
+                    const int idx = lane + 32 * v;
+                    if (idx < 162) qp += (fv[v] - mp) * (fv[v] - mp);
+                    else if (idx < 243) qv += (fv[v] - mv) * (fv[v] - mv);
+                }
+#pragma unroll
+                for (int off = 16; off; off >>= 1) {
+                    qp += __shfl_xor_sync(0xffffffffu, qp, off);
+                    qv += __shfl_xor_sync(0xffffffffu, qv, off);
+                }
+                const float rp = 1.0f / sqrtf(qp / 162.f + 1e-5f), rv = 1.0f / sqrtf(qv / 81.f + 1e-5f);
+#pragma unroll
+                for (int v = 0; v < 8; ++v) {
+                    const int idx = lane + 32 * v;
+                    if (idx >= 243) continue;
+                    const int ch = idx < 81 ? 0 : idx < 162 ? 1 : 2;
+                    const float w = __ldg(p.head_norm + (ch < 2 ? ch : 4)), b = __ldg(p.head_norm + (ch < 2 ? 2 + ch : 5));
+                    const float mean = ch < 2 ? mp : mv, rstd = ch < 2 ? rp : rv;
+                    const float a = rstd * w;
+                    fv[v] = fmaxf(a * fv[v] + (b - a * mean), 0.f);
+                }
+            }
 #pragma unroll
             for (int v = 0; v < 8; ++v)
                 if (lane + 32 * v < 243) feat[u * 244 + lane + 32 * v] = fv[v];
@@ -892,26 +1067,31 @@ __global__ void __launch_bounds__(32 * kHeadWarps) net_heads_kernel(NetParams p,
                 lc[u] = fmaf(xc, f, lc[u]);
             }
         }
-        float ha[kHeadPos], hb[kHeadPos];
-        const float ba = __ldg(p.val_b1 + lane), bb = __ldg(p.val_b1 + lane + 32);
+        float hv[HU][kHeadPos];
 #pragma unroll
-        for (int u = 0; u < kHeadPos; ++u) {
-            ha[u] = ba;
-            hb[u] = bb;
+        for (int k = 0; k < HU; ++k) {
+            const float b = __ldg(p.val_b1 + lane + 32 * k);
+#pragma unroll
+            for (int u = 0; u < kHeadPos; ++u) hv[k][u] = b;
         }
 #pragma unroll 3
         for (int j = 0; j < 81; ++j) {
-            const float xa = va[j], xb = vb[j];
+            float x[HU];
+#pragma unroll
+            for (int k = 0; k < HU; ++k) x[k] = w1[(lane + 32 * k) * kValStride + j];
 #pragma unroll
             for (int u = 0; u < kHeadPos; ++u) {
                 const float f = feat[u * 244 + 162 + j];
-                ha[u] = fmaf(xa, f, ha[u]);
-                hb[u] = fmaf(xb, f, hb[u]);
+#pragma unroll
+                for (int k = 0; k < HU; ++k) hv[k][u] = fmaf(x[k], f, hv[k][u]);
             }
         }
         const float pa = __ldg(p.pol_b + lane), pb = __ldg(p.pol_b + lane + 32);
         const float pc = lane + 64 < GK_ACTIONS ? __ldg(p.pol_b + lane + 64) : 0.f;
-        const float w2a = __ldg(p.val_w2 + lane), w2b = __ldg(p.val_w2 + lane + 32), b2 = __ldg(p.val_b2);
+        float w2[HU];
+#pragma unroll
+        for (int k = 0; k < HU; ++k) w2[k] = __ldg(p.val_w2 + lane + 32 * k);
+        const float b2 = __ldg(p.val_b2);
 #pragma unroll
         for (int u = 0; u < kHeadPos; ++u) {
             const int img = img0 + u;
@@ -920,8 +1100,9 @@ __global__ void __launch_bounds__(32 * kHeadWarps) net_heads_kernel(NetParams p,
             logit[0] = la[u] + pa;
             logit[1] = lb[u] + pb;
             logit[2] = lane + 64 < GK_ACTIONS ? lc[u] + pc : 0.f;
-            float vpart = fmaf(fmaxf(ha[u], 0.f), w2a, 0.f);
-            vpart = fmaf(fmaxf(hb[u], 0.f), w2b, vpart);
+            float vpart = 0.f;
+#pragma unroll
+            for (int k = 0; k < HU; ++k) vpart = fmaf(fmaxf(hv[k][u], 0.f), w2[k], vpart);
 #pragma unroll
             for (int off = 16; off; off >>= 1) vpart += __shfl_xor_sync(0xffffffffu, vpart, off);
             const float value = tanhf(vpart + b2);
@@ -1045,50 +1226,78 @@ inline NetParams make_params(const gk_net_t* net) {
     p.val_b1 = net->val_b1;
     p.val_w2 = net->val_w2;
     p.val_b2 = net->val_b2;
+    p.norm = net->norm;
+    p.norm_w = net->norm_w;
+    p.norm_b = net->norm_b;
+    p.head_norm = net->head_norm;
     return p;
 }
 
-template <int C>
+template <int C, bool GN>
 int launch_tower(const NetParams& p, const NetInput& in, float* headfeat, uint32_t* status, cudaStream_t stream) {
     using K = NetCfg<C>;
     static bool done[64] = {};
     if (!once_per_device(done, [] {
-            return cudaFuncSetAttribute(net_tower_kernel<C>, cudaFuncAttributeMaxDynamicSharedMemorySize, K::SMEM) ==
-                   cudaSuccess;
+            return cudaFuncSetAttribute(net_tower_kernel<C, GN>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                        K::SMEM) == cudaSuccess;
         }))
         return launch_status();
     const int64_t groups = (in.n + K::G - 1) / K::G;
     const int grid = (int)(groups < kSmCount ? groups : kSmCount);
-    net_tower_kernel<C><<<grid < 1 ? 1 : grid, K::THREADS, K::SMEM, stream>>>(p, in, headfeat, status);
+    net_tower_kernel<C, GN><<<grid < 1 ? 1 : grid, K::THREADS, K::SMEM, stream>>>(p, in, headfeat, status);
+    return launch_status();
+}
+
+template <int H>
+int launch_heads_h(const NetParams& p, const float* headfeat, const NetInput& in, const HeadOut& out,
+                   cudaStream_t stream) {
+    static bool done[64] = {};
+    if (!once_per_device(done, [] {
+            return cudaFuncSetAttribute(net_heads_kernel<H>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                        (int)head_smem(H)) == cudaSuccess;
+        }))
+        return launch_status();
+    int64_t blocks = (in.n + kHeadWarps * kHeadPos - 1) / (kHeadWarps * kHeadPos);
+    if (blocks > 2 * kSmCount) blocks = 2 * kSmCount;
+    net_heads_kernel<H><<<(int)(blocks < 1 ? 1 : blocks), 32 * kHeadWarps, head_smem(H), stream>>>(p, headfeat, in,
+                                                                                                   out);
     return launch_status();
 }
 
 int launch_heads(const NetParams& p, const float* headfeat, const NetInput& in, const HeadOut& out,
                  cudaStream_t stream) {
-    static bool done[64] = {};
-    if (!once_per_device(done, [] {
-            return cudaFuncSetAttribute(net_heads_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                        (int)kHeadSmem) == cudaSuccess;
-        }))
-        return launch_status();
-    int64_t blocks = (in.n + kHeadWarps * kHeadPos - 1) / (kHeadWarps * kHeadPos);
-    if (blocks > 2 * kSmCount) blocks = 2 * kSmCount;
-    net_heads_kernel<<<(int)(blocks < 1 ? 1 : blocks), 32 * kHeadWarps, kHeadSmem, stream>>>(p, headfeat, in, out);
-    return launch_status();
+    const int hidden = p.norm ? p.channels : 64;
+    return hidden == 32    ? launch_heads_h<32>(p, headfeat, in, out, stream)
+           : hidden == 128 ? launch_heads_h<128>(p, headfeat, in, out, stream)
+                           : launch_heads_h<64>(p, headfeat, in, out, stream);
 }
 
 inline bool valid_net(const gk_net_t* net) {
-    return net && (net->channels == 64 || net->channels == 128) && net->blocks >= 0 && net->blocks <= 64 &&
-           net->conv_w && net->conv_b && net->head_w && net->head_b && net->pol_w && net->pol_b && net->val_w1 &&
-           net->val_b1 && net->val_w2 && net->val_b2 && aligned16(net->conv_w);
+    if (!net || (net->channels != 32 && net->channels != 64 && net->channels != 128) || net->blocks < 0 ||
+        net->blocks > 64 || !net->conv_w || !net->head_w || !net->pol_w || !net->pol_b || !net->val_w1 ||
+        !net->val_b1 || !net->val_w2 || !net->val_b2 || !aligned16(net->conv_w))
+        return false;
+    if (net->norm == 0) return net->conv_b && net->head_b;
+    return net->norm == 1 && net->norm_w && net->norm_b && net->head_norm;
 }
 
 int run_forward(const gk_net_t* net, const NetInput& in, float* headfeat, const HeadOut& out, uint32_t* status,
                 cudaStream_t stream, cudaEvent_t tower_start = nullptr, cudaEvent_t tower_stop = nullptr) {
     const NetParams p = make_params(net);
     if (tower_start) cudaEventRecord(tower_start, stream);
-    const int s = net->channels == 64 ? launch_tower_cols(p, in, headfeat, status, stream)
-                                      : launch_tower<128>(p, in, headfeat, status, stream);
+    // The column-fused kernel serves the 64-channel batch-norm layout; GroupNorm
+    // needs whole-image statistics between layers, which the templated tower
+    // gathers (its conv_w is per tap for every width).
+    int s;
+    if (net->norm == 0) {
+        s = net->channels == 64   ? launch_tower_cols(p, in, headfeat, status, stream)
+            : net->channels == 32 ? launch_tower<32, false>(p, in, headfeat, status, stream)
+                                  : launch_tower<128, false>(p, in, headfeat, status, stream);
+    } else {
+        s = net->channels == 32   ? launch_tower<32, true>(p, in, headfeat, status, stream)
+            : net->channels == 64 ? launch_tower<64, true>(p, in, headfeat, status, stream)
+                                  : launch_tower<128, true>(p, in, headfeat, status, stream);
+    }
     if (tower_stop) cudaEventRecord(tower_stop, stream);
     if (s) return s;
     return launch_heads(p, headfeat, in, out, stream);
@@ -1114,7 +1323,7 @@ using namespace gk;
 extern "C" {
 
 size_t gk_net_weight_bytes(int channels, int blocks) {
-    if ((channels != 64 && channels != 128) || blocks < 0) return 0;
+    if ((channels != 32 && channels != 64 && channels != 128) || blocks < 0) return 0;
     return (size_t)9 * 16 * channels * 2 + (size_t)blocks * 2 * 9 * channels * channels * 2;
 }
 

@@ -46,7 +46,8 @@ class PuctResults(ctypes.Structure):
 class NetStruct(ctypes.Structure):
     _fields_ = [("channels", c_int), ("blocks", c_int), ("conv_w", c_void_p), ("conv_b", c_void_p),
                 ("head_w", c_void_p), ("head_b", c_void_p), ("pol_w", c_void_p), ("pol_b", c_void_p),
-                ("val_w1", c_void_p), ("val_b1", c_void_p), ("val_w2", c_void_p), ("val_b2", c_void_p)]
+                ("val_w1", c_void_p), ("val_b1", c_void_p), ("val_w2", c_void_p), ("val_b2", c_void_p),
+                ("norm", c_int), ("norm_w", c_void_p), ("norm_b", c_void_p), ("head_norm", c_void_p)]
 
 
 _SIGNATURES = {

@@ -316,12 +316,12 @@ class GpuBatchedPUCT:
         self._ws = grown
 
     def _kind(self, evaluator):
-        from .model import NativePolicyValueNet, PolicyValueNet
+        from .model import NativePolicyValueNet, native_supported
         if isinstance(evaluator, HashEvaluator):
             return "hash", None
         if isinstance(evaluator, NativePolicyValueNet):
             return "native", evaluator
-        if type(evaluator) is PolicyValueNet and evaluator.channels in (64, 128):
+        if native_supported(evaluator):
             # Packed once per model and weight version: any in-place update of
             # a parameter or buffer bumps its version counter.
             key = (id(evaluator), tuple((t.data_ptr(), t._version)

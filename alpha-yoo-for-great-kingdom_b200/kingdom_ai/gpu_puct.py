@@ -168,8 +168,8 @@ class GpuPUCT:
         elif isinstance(model, nn.Module):
             self.model = copy.deepcopy(model).to(device=self.device, dtype=torch.float32).eval()
             self._kind = "module"
-            from .model import NativePolicyValueNet, PolicyValueNet
-            if type(self.model) is PolicyValueNet and self.model.channels in (64, 128):
+            from .model import NativePolicyValueNet, native_supported
+            if native_supported(self.model):
                 self._native_net = NativePolicyValueNet(self.model.cpu(), device=self.device)
                 self._kind = "native"
         else:

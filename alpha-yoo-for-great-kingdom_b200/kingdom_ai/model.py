@@ -9,12 +9,17 @@ value head's hidden width fixed at 64):
     value  conv1x1(C -> 1) + BN + ReLU -> flatten(81) -> Linear(81 -> 64) -> ReLU
            -> Linear(64 -> 1) -> tanh
 
+``GroupNormPolicyValueNet`` is the reference's own network (GroupNorm
+everywhere, value hidden width C), which the native kernels also run.
+
 This module is the fp32 reference the native bf16 kernels are judged
 against; ``fold`` turns its eval-mode batch norms into per-channel scale and
 bias, which is what the native network consumes.
 """
 
 from __future__ import annotations
+
+import math
 
 import torch
 from torch import nn
@@ -123,6 +128,99 @@ def fold(conv: nn.Conv2d, bn: nn.BatchNorm2d):
     return weight.detach().float(), bias.detach().float()
 
 
+class _GroupNormBlock(nn.Module):
+    """Residual block of the reference network: conv, GroupNorm, ReLU, conv,
+    GroupNorm, added to the input, ReLU (python/kingdom_ai/model.py:13-27)."""
+
+    def __init__(self, channels):
+        super().__init__()
+        groups = math.gcd(8, channels)
+        self.layers = nn.Sequential(
+            nn.Conv2d(channels, channels, 3, padding=1, bias=False),
+            nn.GroupNorm(groups, channels),
+            nn.ReLU(),
+            nn.Conv2d(channels, channels, 3, padding=1, bias=False),
+            nn.GroupNorm(groups, channels),
+        )
+        self.activation = nn.ReLU()
+
+    def forward(self, x):
+        return self.activation(x + self.layers(x))
+
+
+class GroupNormPolicyValueNet(nn.Module):
+    """The reference's PolicyValueNet (python/kingdom_ai/model.py:30-84):
+    GroupNorm(gcd(8, C), C) after every trunk convolution, GroupNorm(1, 2) and
+    GroupNorm(1, 1) in the heads, and a value head of C hidden units. Module
+    names and parameter shapes are the reference's, so its checkpoints'
+    state_dicts load unchanged (checkpoint.py:86-89 stores ``model_config``
+    {channels, residual_blocks} beside them)."""
+
+    def __init__(self, channels: int = 32, residual_blocks: int = 2):
+        super().__init__()
+        if type(channels) is not int or channels < 1:
+            raise ValueError("channels must be a positive integer")
+        if type(residual_blocks) is not int or residual_blocks < 0:
+            raise ValueError("residual_blocks must be a non-negative integer")
+        self.channels = channels
+        self.residual_blocks = residual_blocks
+        self.trunk = nn.Sequential(
+            nn.Conv2d(INPUT_CHANNELS, channels, 3, padding=1, bias=False),
+            nn.GroupNorm(math.gcd(8, channels), channels),
+            nn.ReLU(),
+            *[_GroupNormBlock(channels) for _ in range(residual_blocks)],
+        )
+        self.policy_head = nn.Sequential(
+            nn.Conv2d(channels, 2, 1, bias=False),
+            nn.GroupNorm(1, 2),
+            nn.ReLU(),
+            nn.Flatten(),
+            nn.Linear(2 * BOARD * BOARD, ACTION_SIZE),
+        )
+        self.value_head = nn.Sequential(
+            nn.Conv2d(channels, 1, 1, bias=False),
+            nn.GroupNorm(1, 1),
+            nn.ReLU(),
+            nn.Flatten(),
+            nn.Linear(BOARD * BOARD, channels),
+            nn.ReLU(),
+            nn.Linear(channels, 1),
+            nn.Tanh(),
+        )
+
+    @property
+    def model_config(self) -> dict:
+        return {"channels": self.channels, "residual_blocks": self.residual_blocks}
+
+    def forward(self, features: torch.Tensor):
+        shared = self.trunk(features)
+        return self.policy_head(shared), self.value_head(shared).squeeze(-1)
+
+
+def random_groupnorm_network(channels: int, blocks: int, seed: int) -> GroupNormPolicyValueNet:
+    """Kaiming-normal weights and randomised GroupNorm affine parameters from `seed`."""
+    g = torch.Generator().manual_seed(seed)
+    net = GroupNormPolicyValueNet(channels, blocks)
+    with torch.no_grad():
+        for module in net.modules():
+            if isinstance(module, (nn.Conv2d, nn.Linear)):
+                fan_in = module.weight[0].numel()
+                module.weight.copy_(torch.randn(module.weight.shape, generator=g) * (2.0 / fan_in) ** 0.5)
+                if module.bias is not None:
+                    module.bias.copy_(torch.randn(module.bias.shape, generator=g) * 0.05)
+            elif isinstance(module, nn.GroupNorm):
+                n = module.num_channels
+                module.weight.copy_(1.0 + 0.1 * torch.randn(n, generator=g))
+                module.bias.copy_(0.1 * torch.randn(n, generator=g))
+    return net.eval()
+
+
+def native_supported(model) -> bool:
+    """Whether the native kernels can evaluate this module as it is."""
+    return ((type(model) is PolicyValueNet and model.channels in (32, 64, 128))
+            or (type(model) is GroupNormPolicyValueNet and model.channels in (32, 64, 128)))
+
+
 # ---------------------------------------------------------------------------
 # Native (sm_100a) network
 # ---------------------------------------------------------------------------
@@ -147,7 +245,8 @@ def _pack_conv(weight: torch.Tensor, cin_pad: int, column_fused: bool) -> torch.
 
 
 class NativePolicyValueNet:
-    """A PolicyValueNet packed for the tcgen05 kernels (BN folded, bf16 convs).
+    """A PolicyValueNet (BN folded) or GroupNormPolicyValueNet packed for the
+    tcgen05 kernels (bf16 convolutions).
 
     ``forward_states`` / ``forward_features`` return raw logits [N,82] and
     values [N] (fp32); ``evaluate_workspace`` is the in-search leaf evaluator.
@@ -155,47 +254,82 @@ class NativePolicyValueNet:
     and the fully connected heads run in fp32.
     """
 
-    def __init__(self, model: PolicyValueNet, device="cuda"):
+    def __init__(self, model, device="cuda"):
         from . import _native as native
         self.native = native
         self.device = torch.device(device)
-        if model.channels not in (64, 128):
-            raise ValueError("the native network supports 64 or 128 channels")
+        if not native_supported(model):
+            raise ValueError("the native network supports PolicyValueNet or GroupNormPolicyValueNet "
+                             "with 32, 64 or 128 channels")
         self.channels, self.blocks = model.channels, model.residual_blocks
+        self.norm = 1 if isinstance(model, GroupNormPolicyValueNet) else 0
         model = model.eval()
         with torch.no_grad():
-            convs = [fold(model.stem, model.stem_bn)]
-            for block in model.blocks:
-                convs.append(fold(block.conv1, block.bn1))
-                convs.append(fold(block.conv2, block.bn2))
-            fused = self.channels == 64
-            packed = [_pack_conv(convs[0][0].cpu(), 16, fused)] + [_pack_conv(w.cpu(), self.channels, fused)
-                                                                    for w, _ in convs[1:]]
-            conv_w = torch.cat([p.reshape(-1) for p in packed])
-            pw, pb = fold(model.policy_conv, model.policy_bn)
-            vw, vb = fold(model.value_conv, model.value_bn)
-            head_w = torch.cat([pw.reshape(2, -1), vw.reshape(1, -1)]).float()
-            head_b = torch.cat([pb, vb]).float()
-            tensors = {
-                "conv_w": conv_w,
-                "conv_b": torch.stack([b for _, b in convs]).float(),
-                "head_w": head_w, "head_b": head_b,
-                "pol_w": model.policy_fc.weight.detach().float(), "pol_b": model.policy_fc.bias.detach().float(),
-                "val_w1": model.value_fc1.weight.detach().float(), "val_b1": model.value_fc1.bias.detach().float(),
-                "val_w2": model.value_fc2.weight.detach().float().reshape(-1),
-                "val_b2": model.value_fc2.bias.detach().float().reshape(-1),
-            }
+            if self.norm:
+                tensors = self._groupnorm_tensors(model)
+            else:
+                tensors = self._batchnorm_tensors(model)
         expected = native.library().gk_net_weight_bytes(self.channels, self.blocks)
-        if conv_w.numel() * 2 != expected:
+        if tensors["conv_w"].numel() * 2 != expected:
             raise RuntimeError("packed weight size mismatch")
         self.tensors = {k: v.to(self.device).contiguous() for k, v in tensors.items()}
         t = self.tensors
+        ptr = lambda name: t[name].data_ptr() if name in t else None  # noqa: E731
         self.struct = native.NetStruct(
-            self.channels, self.blocks, t["conv_w"].data_ptr(), t["conv_b"].data_ptr(), t["head_w"].data_ptr(),
-            t["head_b"].data_ptr(), t["pol_w"].data_ptr(), t["pol_b"].data_ptr(), t["val_w1"].data_ptr(),
-            t["val_b1"].data_ptr(), t["val_w2"].data_ptr(), t["val_b2"].data_ptr())
+            self.channels, self.blocks, ptr("conv_w"), ptr("conv_b"), ptr("head_w"), ptr("head_b"), ptr("pol_w"),
+            ptr("pol_b"), ptr("val_w1"), ptr("val_b1"), ptr("val_w2"), ptr("val_b2"), self.norm, ptr("norm_w"),
+            ptr("norm_b"), ptr("head_norm"))
         self._headfeat = None
         self.status = torch.zeros(2, dtype=torch.int32, device=self.device)
+
+    def _batchnorm_tensors(self, model):
+        convs = [fold(model.stem, model.stem_bn)]
+        for block in model.blocks:
+            convs.append(fold(block.conv1, block.bn1))
+            convs.append(fold(block.conv2, block.bn2))
+        fused = self.channels == 64
+        packed = [_pack_conv(convs[0][0].cpu(), 16, fused)] + [_pack_conv(w.cpu(), self.channels, fused)
+                                                                for w, _ in convs[1:]]
+        pw, pb = fold(model.policy_conv, model.policy_bn)
+        vw, vb = fold(model.value_conv, model.value_bn)
+        return {
+            "conv_w": torch.cat([p.reshape(-1) for p in packed]),
+            "conv_b": torch.stack([b for _, b in convs]).float(),
+            "head_w": torch.cat([pw.reshape(2, -1), vw.reshape(1, -1)]).float(),
+            "head_b": torch.cat([pb, vb]).float(),
+            "pol_w": model.policy_fc.weight.detach().float(), "pol_b": model.policy_fc.bias.detach().float(),
+            "val_w1": model.value_fc1.weight.detach().float(), "val_b1": model.value_fc1.bias.detach().float(),
+            "val_w2": model.value_fc2.weight.detach().float().reshape(-1),
+            "val_b2": model.value_fc2.bias.detach().float().reshape(-1),
+        }
+
+    def _groupnorm_tensors(self, model):
+        """The reference layout (python/kingdom_ai/model.py:13-84): bias-free
+        convolutions in the per-tap bf16 layout and each GroupNorm's affine
+        parameters (include/gk.h, gk_net_t, norm 1)."""
+        convs, norms = [(model.trunk[0], model.trunk[1])], []
+        for block in list(model.trunk)[3:]:
+            convs.append((block.layers[0], block.layers[1]))
+            convs.append((block.layers[3], block.layers[4]))
+        packed = [_pack_conv(convs[0][0].weight.detach().float().cpu(), 16, False)]
+        packed += [_pack_conv(c.weight.detach().float().cpu(), self.channels, False) for c, _ in convs[1:]]
+        for _, gn in convs:
+            if gn.num_groups != 8 or abs(gn.eps - 1e-5) > 1e-12:
+                raise ValueError("the native network expects GroupNorm(8, C) with eps 1e-5")
+            norms.append(gn)
+        ph, vh = model.policy_head, model.value_head
+        return {
+            "conv_w": torch.cat([p.reshape(-1) for p in packed]),
+            "norm_w": torch.stack([g.weight.detach().float() for g in norms]),
+            "norm_b": torch.stack([g.bias.detach().float() for g in norms]),
+            "head_w": torch.cat([ph[0].weight.detach().float().reshape(2, -1),
+                                 vh[0].weight.detach().float().reshape(1, -1)]),
+            "head_norm": torch.cat([ph[1].weight.detach().float(), ph[1].bias.detach().float(),
+                                    vh[1].weight.detach().float(), vh[1].bias.detach().float()]),
+            "pol_w": ph[4].weight.detach().float(), "pol_b": ph[4].bias.detach().float(),
+            "val_w1": vh[4].weight.detach().float(), "val_b1": vh[4].bias.detach().float(),
+            "val_w2": vh[6].weight.detach().float().reshape(-1), "val_b2": vh[6].bias.detach().float().reshape(-1),
+        }
 
     def _workspace(self, n):
         if self._headfeat is None or self._headfeat.shape[0] < n:

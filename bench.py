@@ -271,6 +271,8 @@ def main():
                         default="selfplay",
                         help="selfplay is the headline; the others time one kernel family each")
     parser.add_argument("--net", default="128x10", help="network workload: CHANNELSxBLOCKS")
+    parser.add_argument("--norm", choices=["batch", "group"], default="batch",
+                        help="network workload: batch norm folded, or the reference's GroupNorm network")
     parser.add_argument("--batch", type=int, default=8192, help="network workload batch")
     parser.add_argument("--states", type=int, default=1 << 22, help="rules workload: states per play launch")
     parser.add_argument("--positions", type=int, default=65536, help="encode workload: positions")

@@ -59,27 +59,32 @@ def emit(line):
 
 def bench_network(args, peaks):
     from kingdom_ai.gpu_puct import encode_packed
-    from kingdom_ai.model import NativePolicyValueNet, calibrate_batchnorm, random_network
+    from kingdom_ai.model import (NativePolicyValueNet, calibrate_batchnorm, random_groupnorm_network,
+                                  random_network)
 
     device = torch.device("cuda", 0)
     channels, blocks = (int(x) for x in args.net.split("x"))
     n = args.batch
-    model = random_network(channels, blocks, 1234).to(device)
+    group = args.norm == "group"
+    model = (random_groupnorm_network if group else random_network)(channels, blocks, 1234).to(device)
     bits = positions(n, 4321, device)
     features, _ = encode_packed(bits)
-    calibrate_batchnorm(model, features)
+    if not group:
+        calibrate_batchnorm(model, features)
     net = NativePolicyValueNet(model.cpu(), device)
     flush = Flusher(device)
     ms = timed(lambda: net.forward_states(bits), args.steps, args.warmup, flush)
     net.check()
+    hidden = channels if group else 64
     flops = 2 * 81 * 9 * 10 * channels + 2 * blocks * 2 * 81 * 9 * channels * channels + 2 * 81 * (
-        channels * 3 + 162 * 82 + 81 * 64 + 64)
+        channels * 3 + 162 * 82 + 81 * hidden + hidden)
     tflops = n * flops / (ms / 1e3) / 1e12
     with torch.no_grad():
         t_ref = timed(lambda: model.to(device)(features), max(1, args.steps // 2), 1, flush)
         with torch.autocast("cuda", dtype=torch.bfloat16):
             t_amp = timed(lambda: model(features), max(1, args.steps // 2), 1, flush)
-    emit({"workload": f"network forward {channels}ch x {blocks} blocks, batch {n}", "metric": "positions/s",
+    kind = "GroupNorm (the reference's PolicyValueNet)" if group else "batch norm folded"
+    emit({"workload": f"network forward {channels}ch x {blocks} blocks, {kind}, batch {n}", "metric": "positions/s",
           "value": n / (ms / 1e3), "unit": "positions/s", "ms_per_batch": ms, "dtype": "bf16",
           "roofline": {"bound": "tensor", "achieved": tflops, "peak": peaks[3], "unit": "TFLOP/s",
                        "frac": tflops / peaks[3], "peak_kind": f"{peaks[2]} bf16 burst (kernel timed alone)",

@@ -219,16 +219,25 @@ GK_API int gk_puct_search_hash_noalloc(int64_t batch, int simulations, const uin
 
 /* -------------------------------------------------------------- network */
 
-/* Device pointers of a packed policy/value network (BN folded). Layout of
- * conv_w, for each 3x3 layer (stem first, then two per residual block), the
- * stem's Cin padded from 10 to 16: with 128 channels, for each of the 9 taps
- * (row-major over (dr, dc)), bf16 [Cin/8][Cout][8]; with 64 channels, for each
- * row offset dr (-1, 0, 1), bf16 [Cin/8][3 (dc = -1, 0, 1)][Cout][8], the
- * three column taps side by side. conv_b: fp32 [layers][C]. head_w/head_b:
- * the 1x1 policy (2 rows) and value (1 row) convolutions. The rest are the
- * fully connected heads of python/kingdom_ai/model.py:51-69 (value hidden 64). */
+/* Device pointers of a packed policy/value network. Layout of conv_w, for each
+ * 3x3 layer (stem first, then two per residual block), the stem's Cin padded
+ * from 10 to 16: for each of the 9 taps (row-major over (dr, dc)), bf16
+ * [Cin/8][Cout][8]; except with 64 channels and batch norm, where it is for
+ * each row offset dr (-1, 0, 1) bf16 [Cin/8][3 (dc = -1, 0, 1)][Cout][8], the
+ * three column taps side by side. head_w/head_b: the 1x1 policy (2 rows) and
+ * value (1 row) convolutions. pol_*, val_*: the fully connected heads.
+ *
+ * norm = 0: batch norm folded into the convolutions (the self-play workload
+ * layout): conv_b fp32 [layers][C] is each layer's folded bias, the head
+ * convolutions carry their folded biases, and the value head's hidden width is
+ * 64. norm = 1: the reference's PolicyValueNet (python/kingdom_ai/model.py:
+ * 13-84): bias-free convolutions, each followed by GroupNorm(gcd(8, C), C)
+ * with norm_w/norm_b fp32 [layers][C] (eps 1e-5), the policy and value 1x1
+ * convolutions by GroupNorm(1, 2) and GroupNorm(1, 1) with head_norm fp32[6] =
+ * {policy weight[2], policy bias[2], value weight, value bias}, and a value
+ * hidden width of C; conv_b and head_b are unused. */
 typedef struct {
-    int channels; /* 64 or 128 */
+    int channels; /* 32, 64 or 128 */
     int blocks;   /* residual blocks */
     const void* conv_w;
     const float* conv_b;
@@ -236,10 +245,14 @@ typedef struct {
     const float* head_b; /* [3] */
     const float* pol_w;  /* [82][162] */
     const float* pol_b;  /* [82] */
-    const float* val_w1; /* [64][81] */
-    const float* val_b1; /* [64] */
-    const float* val_w2; /* [64] */
+    const float* val_w1; /* [H][81], H = 64 (norm 0) or C (norm 1) */
+    const float* val_b1; /* [H] */
+    const float* val_w2; /* [H] */
     const float* val_b2; /* [1] */
+    int norm;                /* 0 batch norm folded, 1 GroupNorm */
+    const float* norm_w;     /* [layers][C] (norm 1) */
+    const float* norm_b;     /* [layers][C] (norm 1) */
+    const float* head_norm;  /* [6] (norm 1) */
 } gk_net_t;
 
 /* Tensor-core self-test: D[128,64] (fp32) = A[128,16] x B[64,16]^T (bf16 bit

@@ -34,11 +34,17 @@ Fixtures
                         move played, the advance results and an occasional
                         illegal advance.
 
-Run with the argument ``tactics`` (or ``batched``) to write only that fixture.
+  groupnorm.npz         the reference's own PolicyValueNet (GroupNorm
+                        everywhere) at 32 x 2 and 64 x 1: seeded weights as
+                        its state_dict, generated positions' features and
+                        the module's fp32 logits and values.
+
+Run with the argument ``tactics``, ``batched`` or ``groupnorm`` to write only that fixture.
 """
 
 from __future__ import annotations
 
+import os
 import sys
 from pathlib import Path
 
@@ -254,6 +260,48 @@ def batched_fixture(ref):
     return out
 
 
+def reference_model_module():
+    """The reference's python/kingdom_ai/model.py, loaded on its own: its
+    package imports the compiled engine, so the one module it needs
+    (encoding's ACTION_SIZE, BOARD_SIZE, INPUT_CHANNELS) is stood in for."""
+    import importlib.util
+    import types
+    ref = Path(os.environ.get("GK_REFERENCE", "/root/reference"))
+    package = types.ModuleType("refkingdom")
+    package.__path__ = []
+    encoding = types.ModuleType("refkingdom.encoding")
+    encoding.ACTION_SIZE, encoding.BOARD_SIZE, encoding.INPUT_CHANNELS = 82, 9, 10
+    sys.modules["refkingdom"], sys.modules["refkingdom.encoding"] = package, encoding
+    spec = importlib.util.spec_from_file_location("refkingdom.model", ref / "python/kingdom_ai/model.py")
+    module = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(module)
+    return module
+
+
+def groupnorm_fixture(ref):
+    """The reference's PolicyValueNet (GroupNorm) at its default 32 x 2 and at
+    64 x 1: seeded weights as saved by state_dict, schema-1 features of
+    generated positions, and the reference module's fp32 outputs."""
+    import torch
+    model_module = reference_model_module()
+    features, _ = ref.encode_positions(57, 96)
+    out = {"features": features.astype(np.float32)}
+    for tag, (channels, blocks) in (("c32", (32, 2)), ("c64", (64, 1))):
+        torch.manual_seed(1000 + channels)
+        net = model_module.PolicyValueNet(channels, blocks)
+        with torch.no_grad():
+            for name, tensor in net.named_parameters():
+                if name.endswith("weight") and tensor.dim() == 1:  # GroupNorm affine
+                    tensor.copy_(1.0 + 0.1 * torch.randn_like(tensor))
+                elif name.endswith("bias"):
+                    tensor.copy_(0.1 * torch.randn_like(tensor))
+            logits, values = net.eval()(torch.from_numpy(out["features"]))
+        for name, tensor in net.state_dict().items():
+            out[f"{tag}/{name}"] = tensor.numpy()
+        out[f"{tag}/logits"], out[f"{tag}/values"] = logits.numpy(), values.numpy()
+    return out
+
+
 def save(name, data):
     np.savez_compressed(HERE / name, **data)
     print(name, {k: v.shape for k, v in data.items()})
@@ -263,6 +311,9 @@ def main():
     ref = Reference()
     if len(sys.argv) > 1 and sys.argv[1] == "tactics":
         save("tactics.npz", tactics_fixture(ref))
+        return
+    if len(sys.argv) > 1 and sys.argv[1] == "groupnorm":
+        save("groupnorm.npz", groupnorm_fixture(ref))
         return
     if len(sys.argv) > 1 and sys.argv[1] == "batched":
         save("batched.npz", batched_fixture(ref))

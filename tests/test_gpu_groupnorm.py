@@ -1,0 +1,75 @@
+"""The reference's own network (GroupNorm everywhere, python/kingdom_ai/model.py:
+13-84) on the native tcgen05 kernels.
+
+Tolerances against the fp32 PyTorch module (bf16 operands, fp32 accumulation
+and statistics): max |logit - fp32| <= 2e-2 * max |logit| + 5e-3 and
+max |value - fp32| <= 5e-2. The reference checkpoints come from
+tests/golden/groupnorm.npz (the reference module's own weights and outputs).
+"""
+
+import pytest
+import torch
+
+from test_gpu_net import native_or_skip, positions, selftest  # noqa: F401
+from test_model_host import load_reference
+
+pytestmark = pytest.mark.gpu
+
+RTOL, ATOL, VTOL = 2e-2, 5e-3, 5e-2
+
+
+def check(model, features, bits=None):
+    from kingdom_ai.model import NativePolicyValueNet
+    with torch.no_grad():
+        ref_logits, ref_values = model.cpu()(features.cpu())
+    net = NativePolicyValueNet(model, device="cuda")
+    logits, values = net.forward_features(features.cuda())
+    torch.cuda.synchronize()
+    net.check()
+    scale = ref_logits.abs().max().item()
+    assert (logits.cpu() - ref_logits).abs().max().item() <= RTOL * scale + ATOL
+    assert (values.cpu() - ref_values).abs().max().item() <= VTOL
+    if bits is not None:
+        l2, v2 = net.forward_states(bits)
+        assert torch.equal(l2, logits) and torch.equal(v2, values)
+    return net
+
+
+def test_reference_checkpoints(selftest, golden):  # noqa: F811
+    native_or_skip(selftest)
+    for tag in ("c32", "c64"):
+        g, net = load_reference(golden, tag)
+        features = torch.from_numpy(g["features"])
+        check(net, features)
+        # the stored reference outputs themselves
+        from kingdom_ai.model import NativePolicyValueNet
+        logits, values = NativePolicyValueNet(net, device="cuda").forward_features(features.cuda())
+        ref = torch.from_numpy(g[f"{tag}/logits"])
+        assert (logits.cpu() - ref).abs().max().item() <= RTOL * ref.abs().max().item() + ATOL
+        assert (values.cpu() - torch.from_numpy(g[f"{tag}/values"])).abs().max().item() <= VTOL
+
+
+@pytest.mark.parametrize("channels,blocks,n", [(32, 2, 1), (32, 2, 23), (32, 4, 1000), (64, 2, 333),
+                                               (128, 2, 517)])
+def test_random_groupnorm_networks(selftest, channels, blocks, n):  # noqa: F811
+    from kingdom_ai.gpu_puct import encode_packed
+    from kingdom_ai.model import random_groupnorm_network
+    native_or_skip(selftest)
+    bits = positions(n, channels + blocks)
+    features, _ = encode_packed(bits)
+    check(random_groupnorm_network(channels, blocks, 7), features, bits)
+
+
+def test_groupnorm_network_in_both_searches(selftest, oracle):  # noqa: F811
+    from kingdom_ai import GpuBatchedPUCT, GpuPUCT, GpuPUCTOptions, PUCTOptions
+    from kingdom_ai.model import random_groupnorm_network
+    native_or_skip(selftest)
+    model = random_groupnorm_network(32, 2, 3)
+    bits = positions(96, 11)
+    r = GpuPUCT(model, GpuPUCTOptions(simulations=16, seed=1)).search_packed(bits)
+    assert (r.visits.sum(1) == 16).all().item()
+    s = GpuBatchedPUCT(96, PUCTOptions(simulations=24), 8)
+    b = s.search(bits, model)
+    assert (b.visits.sum(1) == 24).all().item() and (b.simulations == 24).all().item()
+    legal = b.legal.gather(1, b.actions[:, None]).flatten()
+    assert legal.all().item()
