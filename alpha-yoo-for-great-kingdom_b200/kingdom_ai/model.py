@@ -215,6 +215,52 @@ def random_groupnorm_network(channels: int, blocks: int, seed: int) -> GroupNorm
     return net.eval()
 
 
+# Schema-1 checkpoint fields (python/kingdom_ai/checkpoint.py:14-37): the
+# observation planes in order, and the value perspective.
+FEATURE_NAMES = ("own_stones", "opponent_stones", "neutral_stones", "own_territory", "opponent_territory",
+                 "black_to_play", "own_remaining_fraction", "opponent_remaining_fraction",
+                 "consecutive_passes_fraction", "legal_placements")
+CHECKPOINT_FIELDS = {"format_version", "board_size", "action_size", "feature_names", "perspective",
+                     "model_config", "state_dict"}
+
+
+def load_reference_model(checkpoint, device="cpu") -> GroupNormPolicyValueNet:
+    """A reference checkpoint (a path, or the payload torch.load returns) as a
+    GroupNormPolicyValueNet in eval mode, with the checks of the reference's
+    load_model (python/kingdom_ai/checkpoint.py:40-90)."""
+    payload = checkpoint
+    if not isinstance(checkpoint, dict):
+        payload = torch.load(checkpoint, map_location="cpu", weights_only=True)
+    if not isinstance(payload, dict) or set(payload) != CHECKPOINT_FIELDS:
+        raise ValueError("checkpoint is missing or has unexpected schema fields")
+    for key, expected in (("format_version", 1), ("board_size", BOARD), ("action_size", ACTION_SIZE)):
+        if type(payload[key]) is not int or payload[key] != expected:
+            raise ValueError(f"checkpoint {key} does not match the supported schema")
+    names = payload["feature_names"]
+    if type(names) is not list or any(type(n) is not str for n in names) or names != list(FEATURE_NAMES):
+        raise ValueError("checkpoint feature_names do not match the input schema")
+    if type(payload["perspective"]) is not str or payload["perspective"] != "to_play":
+        raise ValueError("checkpoint value perspective must be to_play")
+    config = payload["model_config"]
+    if not isinstance(config, dict) or set(config) != {"channels", "residual_blocks"}:
+        raise ValueError("checkpoint model_config is invalid")
+    with torch.random.fork_rng(devices=[]):
+        model = GroupNormPolicyValueNet(**config)
+    state, expected = payload["state_dict"], model.state_dict()
+    if not isinstance(state, dict) or set(state) != set(expected):
+        raise ValueError("checkpoint parameters do not match the model configuration")
+    for name, reference in expected.items():
+        value = state[name]
+        if not isinstance(value, torch.Tensor):
+            raise ValueError(f"checkpoint parameter {name} is not a tensor")
+        if value.layout != torch.strided or value.shape != reference.shape or value.dtype != reference.dtype:
+            raise ValueError(f"checkpoint parameter {name} has the wrong shape or dtype")
+        if not bool(torch.isfinite(value).all()):
+            raise ValueError(f"checkpoint parameter {name} contains NaN or infinity")
+    model.load_state_dict(state, strict=True)
+    return model.to(device).eval()
+
+
 def native_supported(model) -> bool:
     """Whether the native kernels can evaluate this module as it is."""
     return ((type(model) is PolicyValueNet and model.channels in (32, 64, 128))
