@@ -280,24 +280,19 @@ __device__ __forceinline__ float gn_total(const float* parts, int img, int grp) 
 }
 
 // One pass of this warp over the accumulator of tile t: per group of the
-// warp's half (four groups), the sum over valid cells of x (centred == false)
-// or of (x - mean)^2 (centred == true, means from `sums`), reduced over the
-// warp separately for the two images a chunk can meet, into `parts`.
+// warp's half (four groups), the sums over valid cells of x and of x^2,
+// reduced over the warp separately for the two images a chunk can meet (one
+// reduction when the chunk lies inside one image), into `sums` and `squares`.
 template <int C>
-__device__ __forceinline__ void gn_partials(uint32_t tacc, int t, int q, int lane, int col0, int nimg, bool centred,
-                                            const float* sums, float* parts) {
+__device__ __forceinline__ void gn_partials(uint32_t tacc, int t, int q, int lane, int col0, int nimg, float* sums,
+                                            float* squares) {
     using K = NetCfg<C>;
     constexpr int W = K::W, CG = C / 8;
     const int m0 = t * 128 + q * 32, m = m0 + lane;
     const int img = m / 100, pos = m - img * 100, r = pos / 10, cc = pos - r * 10;
     const bool valid = img < nimg && r < 9 && cc < 9;
     const int g0 = col0 / CG;
-    float mu[4] = {0.0f, 0.0f, 0.0f, 0.0f};
-    if (centred && valid) {
-#pragma unroll
-        for (int gi = 0; gi < 4; ++gi) mu[gi] = gn_total(sums, img, g0 + gi) / (float)(81 * CG);
-    }
-    float acc[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+    float acc[4] = {0.0f, 0.0f, 0.0f, 0.0f}, sq[4] = {0.0f, 0.0f, 0.0f, 0.0f};
 #pragma unroll
     for (int cb = 0; cb < K::HALF / W; ++cb) {
         float v[W];
@@ -305,25 +300,39 @@ __device__ __forceinline__ void gn_partials(uint32_t tacc, int t, int q, int lan
 #pragma unroll
         for (int j = 0; j < W; ++j) {
             const int gi = (cb * W + j) / CG;
-            const float d = v[j] - mu[gi];
-            acc[gi] += valid ? (centred ? d * d : v[j]) : 0.0f;
+            const float x = valid ? v[j] : 0.0f;
+            acc[gi] += x;
+            sq[gi] = fmaf(x, x, sq[gi]);
         }
     }
     const int img0 = m0 / 100;
+    const bool straddles = (m0 + 31) / 100 != img0;  // warp-uniform
     const bool second = img != img0;
+    const int k = t * 4 + q;
 #pragma unroll
     for (int gi = 0; gi < 4; ++gi) {
-        float a = second ? 0.0f : acc[gi], b = second ? acc[gi] : 0.0f;
+        float a = second ? 0.0f : acc[gi], b = second ? 0.0f : sq[gi];
+        float c = second ? acc[gi] : 0.0f, d = second ? sq[gi] : 0.0f;
 #pragma unroll
         for (int off = 16; off; off >>= 1) {
             a += __shfl_xor_sync(0xffffffffu, a, off);
             b += __shfl_xor_sync(0xffffffffu, b, off);
+            if (straddles) {
+                c += __shfl_xor_sync(0xffffffffu, c, off);
+                d += __shfl_xor_sync(0xffffffffu, d, off);
+            }
         }
         if (lane == 0) {
-            const int k = t * 4 + q;
-            if (img0 < K::G) parts[(img0 * 8 + g0 + gi) * 5 + (k - gn_first(img0))] = a;
-            if (img0 + 1 < K::G && (m0 + 31) / 100 == img0 + 1)
-                parts[((img0 + 1) * 8 + g0 + gi) * 5 + (k - gn_first(img0 + 1))] = b;
+            if (img0 < K::G) {
+                const int slot = (img0 * 8 + g0 + gi) * 5 + (k - gn_first(img0));
+                sums[slot] = a;
+                squares[slot] = b;
+            }
+            if (straddles && img0 + 1 < K::G) {
+                const int slot = ((img0 + 1) * 8 + g0 + gi) * 5 + (k - gn_first(img0 + 1));
+                sums[slot] = c;
+                squares[slot] = d;
+            }
         }
     }
 }
@@ -343,7 +352,7 @@ __global__ void __launch_bounds__(NetCfg<C>::THREADS, 1)
     uint32_t* const tmem_holder = reinterpret_cast<uint32_t*>(bars + K::NBARS);
     float* const headw = reinterpret_cast<float*>(tmem_holder + 4);  // [3][C] then [3] biases
     float* const gn_sum = headw + K::HEADW;    // GroupNorm partial sums (norm 1)
-    float* const gn_sq = gn_sum + K::GN_PARTS;  // and centred squares
+    float* const gn_sq = gn_sum + K::GN_PARTS;  // and squares
     const uint32_t slot_full = tc::smem_u32(bars);
     const uint32_t slot_free = slot_full + 8 * K::NSLOT;
     const uint32_t acc_full = slot_free + 8 * K::NSLOT;
@@ -454,23 +463,18 @@ __global__ void __launch_bounds__(NetCfg<C>::THREADS, 1)
                     for (int j = 0; j < HALF; ++j) bias[j] = __ldg(p.conv_b + l * C + col0 + j);
                 }
                 if constexpr (GN) {
-                    // GroupNorm statistics: sums, then centred squares, each
-                    // followed by a bounded barrier of the eight warps.
+                    // GroupNorm statistics: sums of x and x^2 per (image,
+                    // group) slot, then a bounded barrier of the eight warps.
                     for (int t = 0; t < K::T; ++t) {
                         if (!warp_wait(acc_full + 8 * t, (uint32_t)a & 1u, status, lane == 0)) goto epi_done_label;
                         tc::tc_fence_after();
-                        gn_partials<C>(tq + t * C, t, q, lane, col0, nimg, false, gn_sum, gn_sum);
+                        gn_partials<C>(tq + t * C, t, q, lane, col0, nimg, gn_sum, gn_sq);
                     }
-                    for (int pass = 0; pass < 2; ++pass) {
-                        if (pass == 1) {
-                            for (int t = 0; t < K::T; ++t) gn_partials<C>(tq + t * C, t, q, lane, col0, nimg, true, gn_sum, gn_sq);
-                        }
-                        __syncwarp();
-                        if (lane == 0) tc::mbar_arrive(gn_ready);
-                        if (!warp_wait(gn_ready, gn_phase & 1u, status, lane == 0)) goto epi_done_label;
-                        ++gn_phase;
-                        __threadfence_block();
-                    }
+                    __syncwarp();
+                    if (lane == 0) tc::mbar_arrive(gn_ready);
+                    if (!warp_wait(gn_ready, gn_phase & 1u, status, lane == 0)) goto epi_done_label;
+                    ++gn_phase;
+                    __threadfence_block();
                 }
                 for (int t = 0; t < K::T; ++t) {
                     if (!gn && !warp_wait(acc_full + 8 * t, (uint32_t)a & 1u, status, lane == 0)) goto epi_done_label;
@@ -486,7 +490,8 @@ __global__ void __launch_bounds__(NetCfg<C>::THREADS, 1)
                         for (int gi = 0; gi < 4; ++gi) {
                             const int grp = col0 / CG + gi;
                             mean[gi] = gn_total(gn_sum, img, grp) / (float)(81 * CG);
-                            rstd[gi] = 1.0f / sqrtf(gn_total(gn_sq, img, grp) / (float)(81 * CG) + 1e-5f);
+                            const float var = gn_total(gn_sq, img, grp) / (float)(81 * CG) - mean[gi] * mean[gi];
+                            rstd[gi] = 1.0f / sqrtf(fmaxf(var, 0.0f) + 1e-5f);
                         }
                     }
 #pragma unroll
