@@ -73,3 +73,20 @@ def test_groupnorm_network_in_both_searches(selftest, oracle):  # noqa: F811
     assert (b.visits.sum(1) == 24).all().item() and (b.simulations == 24).all().item()
     legal = b.legal.gather(1, b.actions[:, None]).flatten()
     assert legal.all().item()
+
+
+def test_selfplay_with_the_reference_network(selftest):  # noqa: F811
+    """Self-play ply by ply with the reference's own 32 x 2 network: the rows
+    it writes pass the reference's replay checks."""
+    from kingdom_ai import GpuPUCTOptions, validate_rows
+    from kingdom_ai.model import random_groupnorm_network
+    from kingdom_ai.selfplay import SelfPlayEngine
+    native_or_skip(selftest)
+    engine = SelfPlayEngine(random_groupnorm_network(32, 2, 5), 64, GpuPUCTOptions(simulations=8, seed=2),
+                            replay_capacity=1 << 13)
+    engine.step(70)
+    torch.cuda.synchronize()
+    engine.check()
+    n = min(engine.stats()["rows"], engine.replay.capacity)
+    assert n > 0
+    validate_rows(*engine.replay.rows(0, n))
