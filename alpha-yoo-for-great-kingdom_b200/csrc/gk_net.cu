@@ -47,8 +47,12 @@ namespace gk {
 template <int C>
 struct NetCfg {
     static_assert(C == 32 || C == 64 || C == 128, "channels must be 32, 64 or 128");
-    static constexpr int G = C == 32 ? 10 : C == 64 ? 5 : 2;  // images per group
-    static constexpr int T = C == 32 ? 8 : C == 64 ? 4 : 2;   // 128-row tiles per group (>= 100*G rows)
+    static constexpr int G = C == 128 ? 2 : 5;  // images per group
+    static constexpr int T = C == 128 ? 2 : 4;  // 128-row tiles per group (>= 100*G rows)
+    // 32 channels: two CTAs per SM (256 TMEM columns and <= 102 registers
+    // each) so one CTA's epilogue latency overlaps the other's.
+    static constexpr int MIN_BLOCKS = C == 32 ? 2 : 1;
+    static constexpr int TMEM_COLS = 2 * T * C <= 256 ? 256 : 512;
     static constexpr int HALO = 11;              // max |tap row shift| = 10 + 1
     // Rows a kept output reads: the group's G*100 rows and a zero halo either
     // side. The tail of the last tile (rows G*100 .. T*128-1) is computed but
@@ -341,7 +345,7 @@ __device__ __forceinline__ void gn_partials(uint32_t tacc, int t, int q, int lan
 // folded into conv_b. Two instantiations keep the batch-norm epilogue free of
 // the GroupNorm passes.
 template <int C, bool GN>
-__global__ void __launch_bounds__(NetCfg<C>::THREADS, 1)
+__global__ void __launch_bounds__(NetCfg<C>::THREADS, NetCfg<C>::MIN_BLOCKS)
     net_tower_kernel(NetParams p, NetInput in, float* headfeat, uint32_t* status) {
     using K = NetCfg<C>;
     extern __shared__ __align__(1024) uint8_t smem[];
@@ -382,7 +386,7 @@ __global__ void __launch_bounds__(NetCfg<C>::THREADS, 1)
         tc::fence_mbar_init();
     }
     if (warp == 0) {
-        tc::tmem_alloc(tc::smem_u32(tmem_holder), 512);
+        tc::tmem_alloc(tc::smem_u32(tmem_holder), K::TMEM_COLS);
         tc::tmem_relinquish();
     }
     tc::tc_fence_before();
@@ -577,7 +581,7 @@ done:
     __syncthreads();
     if (warp == 0) {
         tc::tc_fence_after();
-        tc::tmem_dealloc(tmem, 512);
+        tc::tmem_dealloc(tmem, K::TMEM_COLS);
     }
 }
 
@@ -1248,7 +1252,8 @@ int launch_tower(const NetParams& p, const NetInput& in, float* headfeat, uint32
         }))
         return launch_status();
     const int64_t groups = (in.n + K::G - 1) / K::G;
-    const int grid = (int)(groups < kSmCount ? groups : kSmCount);
+    const int64_t slots = (int64_t)kSmCount * K::MIN_BLOCKS;
+    const int grid = (int)(groups < slots ? groups : slots);
     net_tower_kernel<C, GN><<<grid < 1 ? 1 : grid, K::THREADS, K::SMEM, stream>>>(p, in, headfeat, status);
     return launch_status();
 }
