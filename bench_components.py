@@ -6,6 +6,7 @@
     puct     1024 trees x 800 simulations with the injected evaluator
     replay   replay-row checks of DeviceReplayBuffer ingest on 2^20 rows (3.66 GB)
     batched  the evaluation searcher (BatchedPUCT) for 4096 games x 128 simulations, leaf batch 8
+    selfplay_reference  self-play with the reference's 32 x 2 GroupNorm network and its 128 simulations
 
 Every timed launch is bracketed by CUDA events on the launching stream; an L2
 flush (a 256 MB write) separates timed launches so each one reads its inputs
@@ -282,3 +283,39 @@ def bench_batched(args, peaks):
                       "evaluator": "native 64ch x 6-block bf16 network, one batch per wave",
                       "waves_per_search": batches},
           "cpu_baseline": cpu})
+
+
+def bench_selfplay_reference(args, peaks):
+    """Self-play as the reference's Trainer configures it (loop.py:36-57:
+    128 simulations per move, the 32 x 2 GroupNorm PolicyValueNet,
+    model.py:30-84), on `--lanes` games of one GPU at once: the device engine
+    runs one ply of every game per step. Reported with the same counters as
+    the headline line; no CPU baseline is run for this line."""
+    from kingdom_ai.gpu_puct import GpuPUCTOptions
+    from kingdom_ai.model import random_groupnorm_network
+    from kingdom_ai.selfplay import SelfPlayEngine
+
+    device = torch.device("cuda", 0)
+    opts = GpuPUCTOptions(simulations=128, c_puct=1.5, dirichlet_alpha=0.3, dirichlet_epsilon=0.25, seed=7)
+    engine = SelfPlayEngine(random_groupnorm_network(32, 2, 1234), args.lanes, opts, temperature=1.0,
+                            temperature_moves=10, final_temperature=0.0, replay_capacity=1 << 20, device=device)
+    for _ in range(args.warmup):
+        engine.step(1)
+    torch.cuda.synchronize(device)
+    engine.check()
+    before = engine.stats()
+    start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    start.record()
+    for _ in range(args.steps):
+        engine.step(1)
+    stop.record()
+    stop.synchronize()
+    engine.check()
+    after = engine.stats()
+    ms = start.elapsed_time(stop)
+    moves = after["moves"] - before["moves"]
+    emit({"workload": f"self-play, the reference's 32ch x 2-block GroupNorm network, {args.lanes} games, "
+                      "128 sims/move, c_puct 1.5, Dirichlet 0.3/0.25",
+          "metric": "simulations/s", "unit": "simulations/s", "value": moves * 128 / (ms / 1e3),
+          "moves_per_s": moves / (ms / 1e3), "ms_per_step": ms / args.steps, "steps": args.steps,
+          "warmup": args.warmup, "games_finished": after["games"] - before["games"]})
