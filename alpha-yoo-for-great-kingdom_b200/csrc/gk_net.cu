@@ -1000,7 +1000,7 @@ __global__ void __launch_bounds__(32 * kHeadWarps) net_heads_kernel(NetParams p,
     float* feat = feat_all + warp * (kHeadPos * 244);
     const int count = input_count(in);
     // Lane l owns actions l, l+32, l+64 (the last only for l < 18) and hidden
-    // units l, l+32 of the value head, for each of the warp's kHeadPos
+    // units l + 32k (k < H/32) of the value head, for each of the warp's kHeadPos
     // positions. Every accumulation runs over the features in order, so each
     // position's sums are those of a one-position loop.
     const float* wa = wp + lane * kPolStride;
