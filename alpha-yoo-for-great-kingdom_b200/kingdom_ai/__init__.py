@@ -14,3 +14,4 @@ from .gpu_puct import GpuPUCT, GpuPUCTOptions, GpuSearchResult, HashEvaluator  #
 from .training import Cell, EndReason, GameData, TrainingBatch, TrainingSample, collect_gpu_puct_games  # noqa: F401
 from .replay import DeviceReplayBuffer, validate_rows  # noqa: F401
 from .batched_puct import BatchedSearchResult, GpuBatchedPUCT, PUCTOptions  # noqa: F401
+from .evaluation import EvaluationResult, evaluate_models_gpu  # noqa: F401

@@ -289,3 +289,22 @@ def test_native_network_searches_many_games(oracle):
             assert ok[0]
             recs[t] = nxt[0]
         previous = np.where(recs[:, 166] == 0, previous, -1)
+
+
+def test_evaluation_games_between_models():
+    """evaluate_models_gpu (evaluation.py:235-360 played on the GPU): with
+    identical deterministic models every pair splits 1-1, because both games
+    of a pair use the same seed (evaluation.py:252-256); counts are consistent
+    from the candidate's side."""
+    from kingdom_ai import evaluate_models_gpu
+    from kingdom_ai.model import random_network
+    same = random_network(64, 2, 21)
+    r = evaluate_models_gpu(same, random_network(64, 2, 21), games=16, simulations=16, seed=9)
+    assert r.games == 16 and r.wins == 8 and r.losses == 8 and r.win_rate == 0.5
+    assert r.wins_as_black + r.wins_as_white == r.wins
+    assert sum(r.endings.values()) == 16 and r.total_plies > 16
+    other = evaluate_models_gpu(same, random_network(64, 2, 22), games=8, simulations=8, seed=3,
+                                opening_moves=0)
+    assert other.wins + other.losses == 8 and sum(other.endings.values()) == 8
+    with pytest.raises(ValueError):
+        evaluate_models_gpu(same, same, games=3)
