@@ -268,7 +268,7 @@ def main():
     parser.add_argument("--e2e-steps", type=int, default=3)
     parser.add_argument("--no-cpu-baseline", action="store_true")
     parser.add_argument("--workload", choices=["selfplay", "network", "rules", "encode", "puct", "replay", "batched",
-                                                   "selfplay_reference"],
+                                                   "selfplay_reference", "evaluation"],
                         default="selfplay",
                         help="selfplay is the headline; the others time one kernel family each")
     parser.add_argument("--net", default="128x10", help="network workload: CHANNELSxBLOCKS")
@@ -284,6 +284,7 @@ def main():
     parser.add_argument("--sims-batched", type=int, default=128, help="batched workload: simulations per search")
     parser.add_argument("--leaf", type=int, default=8, help="batched workload: leaf batch per tree")
     parser.add_argument("--lanes", type=int, default=4096, help="selfplay_reference workload: games at once")
+    parser.add_argument("--games", type=int, default=512, help="evaluation workload: games in the match")
     args = parser.parse_args()
     if args.impl == "reference":
         reference_arm(args)

@@ -7,6 +7,7 @@
     replay   replay-row checks of DeviceReplayBuffer ingest on 2^20 rows (3.66 GB)
     batched  the evaluation searcher (BatchedPUCT) for 4096 games x 128 simulations, leaf batch 8
     selfplay_reference  self-play with the reference's 32 x 2 GroupNorm network and its 128 simulations
+    evaluation  a 512-game evaluation match between two 6 x 64 networks (evaluate_models_gpu)
 
 Every timed launch is bracketed by CUDA events on the launching stream; an L2
 flush (a 256 MB write) separates timed launches so each one reads its inputs
@@ -319,3 +320,33 @@ def bench_selfplay_reference(args, peaks):
           "metric": "simulations/s", "unit": "simulations/s", "value": moves * 128 / (ms / 1e3),
           "moves_per_s": moves / (ms / 1e3), "ms_per_step": ms / args.steps, "steps": args.steps,
           "warmup": args.warmup, "games_finished": after["games"] - before["games"]})
+
+
+def bench_evaluation(args, peaks):
+    """A whole evaluation match on one GPU (python/kingdom_ai/evaluation.py:
+    235-360 with its defaults: 128 simulations, c_puct 1.5, leaf batch 8, six
+    sampled opening moves): `--games` games between two different 6 x 64
+    networks, every game stepped at once. Timed with CUDA events around the
+    match, after one warm-up match of 16 games; no CPU baseline is run."""
+    import time
+
+    from kingdom_ai import evaluate_models_gpu
+    from kingdom_ai.model import random_network
+
+    candidate, reference = random_network(64, 6, 31), random_network(64, 6, 32)
+    evaluate_models_gpu(candidate, reference, games=16, simulations=128)
+    torch.cuda.synchronize()
+    start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    wall = time.perf_counter()
+    start.record()
+    result = evaluate_models_gpu(candidate, reference, games=args.games, simulations=128, seed=5)
+    stop.record()
+    stop.synchronize()
+    wall = time.perf_counter() - wall
+    seconds = start.elapsed_time(stop) / 1e3
+    emit({"workload": f"evaluation match: {args.games} games between two 64ch x 6-block networks, 128 sims/move, "
+                      "leaf batch 8, 6 sampled opening moves, subtree reuse",
+          "metric": "games/s", "unit": "games/s", "value": args.games / seconds,
+          "moves_per_s": result.total_plies / seconds, "simulations_per_s": result.total_plies * 128 / seconds,
+          "seconds": seconds, "wall_seconds": wall, "total_plies": result.total_plies,
+          "candidate_win_rate": result.win_rate, "endings": result.endings})
