@@ -182,8 +182,6 @@ def bench_replay(args, peaks):
     restatement of the same checks on a bounded sample, one thread."""
     import time
 
-    import numpy as np
-
     device = torch.device("cuda", 0)
     flush = Flusher(device)
     stream = native.stream_of(device)
