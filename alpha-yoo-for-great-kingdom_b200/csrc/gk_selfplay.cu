@@ -13,7 +13,10 @@
 //     plies of each game and are the search's best action afterwards (:71-81);
 //   * a finished game's samples get value +1 for the winner's turns and -1
 //     otherwise (:114-117) and go into a FIFO replay ring laid out like the
-//     CPU ReplayBuffer (python/kingdom_ai/replay.py:106-125).
+//     CPU ReplayBuffer (python/kingdom_ai/replay.py:106-125);
+//   * the actions played are kept per lane and logged with the finished game,
+//     so the game replays from the start position (record_history, :50-51,
+//     :89-90, :113).
 // Random streams are keyed by (seed, game id, ply) - not by lane or GPU -
 // so a game's moves do not depend on how games are sharded across GPUs.
 #include <cuda_runtime.h>
@@ -43,6 +46,7 @@ struct SelfPlayView {
     uint64_t* game_id;             // [B]
     gk_bits* hist_bits;            // [kHist][B]
     float* hist_policy;            // [kHist][B][82]
+    uint8_t* hist_action;          // [kHist][B] action played at each ply
     int64_t* best;                 // [B] best action of the last search
     unsigned long long* counters;  // [kCounters]
 };
@@ -61,6 +65,7 @@ inline size_t selfplay_layout(void* base, int64_t B, SelfPlayView* v) {
     t.game_id = (uint64_t*)take(B * 8);
     t.hist_bits = (gk_bits*)take((size_t)kHist * B * sizeof(gk_bits));
     t.hist_policy = (float*)take((size_t)kHist * B * GK_ACTIONS * 4);
+    t.hist_action = (uint8_t*)take((size_t)kHist * B);
     t.best = (int64_t*)take(B * 8);
     t.counters = (unsigned long long*)take(kCounters * 8);
     if (v) *v = t;
@@ -73,6 +78,17 @@ struct ReplayView {
     float* policy;
     float* value;
     int8_t* to_play;
+    int64_t capacity;
+};
+
+struct GameLogView {
+    uint64_t* game_id;
+    uint64_t* first_row;
+    int32_t* plies;
+    int8_t* winner;
+    int8_t* reason;
+    gk_bits* final_state;
+    uint8_t* actions;
     int64_t capacity;
 };
 
@@ -97,7 +113,7 @@ __global__ void selfplay_noise_kernel(SelfPlayView v, PuctView p, int64_t B, int
 struct AdvanceParams {
     int temperature_moves;
     double temperature, final_temperature;
-    uint64_t seed, game_stride;
+    uint64_t sample_seed, game_stride, game_limit;
     int neutral;
 };
 
@@ -118,12 +134,18 @@ __device__ __forceinline__ float encoded_value(const EncodePlanes& e, int plane,
 }
 
 __global__ void __launch_bounds__(128) selfplay_advance_kernel(SelfPlayView v, PuctView p, int64_t B, int C,
-                                                               AdvanceParams ap, ReplayView rp) {
+                                                               AdvanceParams ap, ReplayView rp, GameLogView gl) {
     constexpr unsigned kAll = 0xffffffffu;
     const int lane = threadIdx.x & 31;
     const int64_t b = (blockIdx.x * (int64_t)blockDim.x + threadIdx.x) >> 5;
     if (b >= B) return;
     const int ply = v.lane_ply[b];
+    if (ply < 0) return;  // parked: the game limit was reached
+    if (ap.game_limit != 0 && v.game_id[b] >= ap.game_limit) {
+        // A lane that started past the limit (more lanes than games) plays nothing.
+        if (lane == 0) v.lane_ply[b] = -1;
+        return;
+    }
     gk_bits s = v.states[b];
     if (ply >= kHist) {  // unreachable: no game outlasts 2*81+4 plies
         if (lane == 0) {
@@ -155,7 +177,7 @@ __global__ void __launch_bounds__(128) selfplay_advance_kernel(SelfPlayView v, P
     const double temperature = ply < ap.temperature_moves ? ap.temperature : ap.final_temperature;
     int action = (int)v.best[b];
     if (temperature != 0.0 && sims > 0) {
-        gk_pcg32 r = gk_pcg32_seed(ap.seed ^ kSampleSalt, v.game_id[b] * 256u + (uint64_t)ply);
+        gk_pcg32 r = gk_pcg32_seed(ap.sample_seed ^ kSampleSalt, v.game_id[b] * 256u + (uint64_t)ply);
         double w[3];
         int nmax = max(n[0], max(n[1], n[2]));
 #pragma unroll
@@ -197,6 +219,7 @@ __global__ void __launch_bounds__(128) selfplay_advance_kernel(SelfPlayView v, P
     if (lane == 0) {
         const bool ok = play(s, action);
         if (!ok) atomicAdd(&v.counters[kErrors], 1ull);
+        v.hist_action[(int64_t)ply * B + b] = (uint8_t)(action >= 0 && action < GK_ACTIONS ? action : 255);
         atomicAdd(&v.counters[kMoves], 1ull);
         atomicAdd(&v.counters[kEvaluations], (unsigned long long)p.evals[b]);
         finished = gk_reason(&s) != GK_NONE;
@@ -212,14 +235,28 @@ __global__ void __launch_bounds__(128) selfplay_advance_kernel(SelfPlayView v, P
         return;
     }
     const int rows = ply + 1;
-    unsigned long long base = 0;
+    unsigned long long base = 0, order = 0;
     if (lane == 0) {
         base = atomicAdd(&v.counters[kRows], (unsigned long long)rows);
-        atomicAdd(&v.counters[kGames], 1ull);
+        order = atomicAdd(&v.counters[kGames], 1ull);
         atomicAdd(&v.counters[winner == 1 ? kBlackWins : kWhiteWins], 1ull);
         if (gk_reason(&s) == GK_CAPTURE) atomicAdd(&v.counters[kCaptureEnds], 1ull);
     }
     base = __shfl_sync(kAll, base, 0);
+    order = __shfl_sync(kAll, order, 0);
+    if (gl.capacity > 0) {
+        const int64_t slot = (int64_t)(order % (unsigned long long)gl.capacity);
+        for (int k = lane; k < rows; k += 32)
+            gl.actions[slot * GK_GAME_ACTIONS + k] = v.hist_action[(int64_t)k * B + b];
+        if (lane == 0) {  // only lane 0 played the move: its `s` is the final position
+            gl.final_state[slot] = s;
+            gl.game_id[slot] = v.game_id[b];
+            gl.first_row[slot] = base;
+            gl.plies[slot] = rows;
+            gl.winner[slot] = (int8_t)winner;
+            gl.reason[slot] = (int8_t)gk_reason(&s);
+        }
+    }
     if (rp.capacity > 0) {
         for (int k = 0; k < rows; ++k) {
             const int64_t row = (int64_t)((base + (unsigned long long)k) % (unsigned long long)rp.capacity);
@@ -241,9 +278,17 @@ __global__ void __launch_bounds__(128) selfplay_advance_kernel(SelfPlayView v, P
         }
     }
     if (lane == 0) {
-        v.states[b] = initial_bits(ap.neutral);
-        v.lane_ply[b] = 0;
-        v.game_id[b] += ap.game_stride;
+        const uint64_t next = v.game_id[b] + ap.game_stride;
+        if (ap.game_limit != 0 && next >= ap.game_limit) {
+            // Park on the finished position: later searches see a terminal
+            // root and do no work for this lane.
+            v.states[b] = s;
+            v.lane_ply[b] = -1;
+        } else {
+            v.states[b] = initial_bits(ap.neutral);
+            v.lane_ply[b] = 0;
+            v.game_id[b] = next;
+        }
     }
 }
 
@@ -329,9 +374,10 @@ int gk_timer_read(void* timer, double* total_ms, int* pairs) {
 }
 
 int gk_selfplay_ply(void* sp_ws, void* puct_ws, int64_t lanes, const gk_net_t* net, const gk_selfplay_params_t* prm,
-                    const gk_replay_t* replay, float* headfeat, uint32_t* status, void* timer, void* stream) {
-    if (sp_ws == nullptr || puct_ws == nullptr || lanes <= 0 || net == nullptr || prm == nullptr ||
-        headfeat == nullptr || status == nullptr || prm->simulations < 1)
+                    const gk_replay_t* replay, const gk_gamelog_t* games, float* headfeat, uint32_t* status,
+                    void* timer, void* stream) {
+    if (sp_ws == nullptr || puct_ws == nullptr || lanes <= 0 || prm == nullptr ||
+        (net != nullptr && headfeat == nullptr) || status == nullptr || prm->simulations < 1)
         return GK_EINVAL;
     const cudaStream_t st = as_stream(stream);
     const int C = prm->simulations + 1;
@@ -341,6 +387,7 @@ int gk_selfplay_ply(void* sp_ws, void* puct_ws, int64_t lanes, const gk_net_t* n
     puct_layout(puct_ws, lanes, C, &pv);
     Timer* tm = static_cast<Timer*>(timer);
     auto evaluate = [&]() -> int {
+        if (net == nullptr) return gk_puct_hash_eval(puct_ws, lanes, C, stream);
         cudaEvent_t e0 = nullptr, e1 = nullptr;
         if (tm && tm->used < tm->capacity) {
             e0 = tm->events[2 * tm->used];
@@ -369,13 +416,17 @@ int gk_selfplay_ply(void* sp_ws, void* puct_ws, int64_t lanes, const gk_net_t* n
     res.actions = v.best;
     res.status = status;
     if ((s = gk_puct_finish(puct_ws, lanes, C, &res, stream))) return s;
-    AdvanceParams ap{prm->temperature_moves, prm->temperature, prm->final_temperature, prm->seed,
-                     prm->game_stride, prm->neutral_cell >= 0 && prm->neutral_cell < GK_CELLS ? prm->neutral_cell : -1};
+    AdvanceParams ap{prm->temperature_moves, prm->temperature, prm->final_temperature, prm->sample_seed,
+                     prm->game_stride, prm->game_limit,
+                     prm->neutral_cell >= 0 && prm->neutral_cell < GK_CELLS ? prm->neutral_cell : -1};
     ReplayView rp{};
     if (replay) rp = ReplayView{replay->features, replay->masks, replay->policy, replay->value, replay->to_play,
                                 replay->capacity};
+    GameLogView gl{};
+    if (games) gl = GameLogView{games->game_id, games->first_row, games->plies, games->winner, games->reason,
+                                reinterpret_cast<gk_bits*>(games->final_state), games->actions, games->capacity};
     const int64_t blocks = (lanes + 3) / 4;
-    selfplay_advance_kernel<<<(int)blocks, 128, 0, st>>>(v, pv, lanes, C, ap, rp);
+    selfplay_advance_kernel<<<(int)blocks, 128, 0, st>>>(v, pv, lanes, C, ap, rp, gl);
     return launch_status();
 }
 

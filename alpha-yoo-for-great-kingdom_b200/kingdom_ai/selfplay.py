@@ -10,6 +10,12 @@ and their lanes start the next game.
 Randomness is keyed by (seed, game id, ply), so the games played are the same
 however lanes are split across GPUs: rank r of W plays game ids
 r*lanes + i, then + W*lanes per finished game.
+
+Each finished game is also written to an optional device ``GameLog``: its id,
+the actions played (which replay it from the start position), winner, end
+reason, final position and the index of its first replay row. With
+``game_limit`` set, a lane whose next game id would reach the limit parks on
+its finished position, so a run plays exactly the games below the limit.
 """
 
 from __future__ import annotations
@@ -33,12 +39,22 @@ class SelfPlayParams(ctypes.Structure):
                 ("fpu_reduction", ctypes.c_double), ("temperature_moves", ctypes.c_int),
                 ("temperature", ctypes.c_double), ("final_temperature", ctypes.c_double),
                 ("seed", ctypes.c_uint64), ("game_stride", ctypes.c_uint64), ("neutral_cell", ctypes.c_int),
-                ("tactical_checks", ctypes.c_int)]
+                ("tactical_checks", ctypes.c_int), ("sample_seed", ctypes.c_uint64),
+                ("game_limit", ctypes.c_uint64)]
 
 
 class ReplayStruct(ctypes.Structure):
     _fields_ = [("features", ctypes.c_void_p), ("masks", ctypes.c_void_p), ("policy", ctypes.c_void_p),
                 ("value", ctypes.c_void_p), ("to_play", ctypes.c_void_p), ("capacity", ctypes.c_int64)]
+
+
+class GameLogStruct(ctypes.Structure):
+    _fields_ = [("game_id", ctypes.c_void_p), ("first_row", ctypes.c_void_p), ("plies", ctypes.c_void_p),
+                ("winner", ctypes.c_void_p), ("reason", ctypes.c_void_p), ("final_state", ctypes.c_void_p),
+                ("actions", ctypes.c_void_p), ("capacity", ctypes.c_int64)]
+
+
+GAME_ACTIONS = 2 * 81 + 4  # GK_GAME_ACTIONS: longest game plus slack
 
 
 class SelfPlayBuffers(ctypes.Structure):
@@ -56,8 +72,8 @@ def _bind():
     native.register("gk_selfplay_buffers", [ctypes.c_void_p, ctypes.c_int64, ctypes.POINTER(SelfPlayBuffers)])
     native.register("gk_selfplay_ply", [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int64,
                                         ctypes.POINTER(native.NetStruct), ctypes.POINTER(SelfPlayParams),
-                                        ctypes.POINTER(ReplayStruct), ctypes.c_void_p, ctypes.c_void_p,
-                                        ctypes.c_void_p, ctypes.c_void_p])
+                                        ctypes.POINTER(ReplayStruct), ctypes.POINTER(GameLogStruct),
+                                        ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p])
     native.register("gk_timer_create", [ctypes.c_int], ctypes.c_void_p)
     native.register("gk_timer_destroy", [ctypes.c_void_p], None)
     native.register("gk_timer_reset", [ctypes.c_void_p], None)
@@ -90,6 +106,32 @@ class ReplayRing:
         return (self.features[idx], self.masks[idx], self.policy[idx], self.value[idx], self.to_play[idx])
 
 
+class GameLog:
+    """Device log of finished games; the k-th game to finish goes to slot k % capacity."""
+
+    def __init__(self, capacity: int, device):
+        self.capacity = int(capacity)
+        self.device = torch.device(device)
+        c = max(self.capacity, 1)
+        z = lambda shape, dtype: torch.zeros(shape, dtype=dtype, device=self.device)  # noqa: E731
+        self.game_id = z((c,), torch.int64)
+        self.first_row = z((c,), torch.int64)
+        self.plies = z((c,), torch.int32)
+        self.winner = z((c,), torch.int8)
+        self.reason = z((c,), torch.int8)
+        self.final_state = z((c, 16), torch.int32)
+        self.actions = z((c, GAME_ACTIONS), torch.uint8)
+        self.struct = GameLogStruct(*(t.data_ptr() for t in (self.game_id, self.first_row, self.plies, self.winner,
+                                                             self.reason, self.final_state, self.actions)),
+                                    self.capacity)
+
+    def read(self, count: int) -> dict:
+        """The first `count` slots (count <= capacity) as host numpy arrays."""
+        count = min(int(count), self.capacity)
+        names = ("game_id", "first_row", "plies", "winner", "reason", "final_state", "actions")
+        return {n: getattr(self, n)[:count].cpu().numpy() for n in names}
+
+
 class Timer:
     """CUDA-event pairs recorded around the network tower inside a ply."""
 
@@ -115,18 +157,32 @@ class Timer:
 
 
 class SelfPlayEngine:
-    """`lanes` concurrent games on one GPU, advanced one ply per ``step()``."""
+    """`lanes` concurrent games on one GPU, advanced one ply per ``step()``.
 
-    def __init__(self, model: PolicyValueNet, lanes: int, options: GpuPUCTOptions | None = None, *,
+    `model` is a network the native kernels run (``PolicyValueNet``,
+    ``GroupNormPolicyValueNet`` or a ``NativePolicyValueNet``), or
+    ``HashEvaluator()`` / None for the injected evaluator. `seed` drives root
+    noise and `sample_seed` (default: `seed`) move sampling. `game_log`
+    slots record finished games; `game_limit` > 0 stops lanes at that game id.
+    """
+
+    def __init__(self, model, lanes: int, options: GpuPUCTOptions | None = None, *,
                  temperature: float = 1.0, temperature_moves: int | None = 10, final_temperature: float = 0.0,
-                 replay_capacity: int = 1 << 20, seed: int | None = None, rank: int = 0, world_size: int = 1,
-                 device="cuda", neutral=(4, 4)):
+                 replay_capacity: int = 1 << 20, seed: int | None = None, sample_seed: int | None = None,
+                 rank: int = 0, world_size: int = 1, device="cuda", neutral=(4, 4), game_log: int = 0,
+                 game_limit: int = 0, first_game: int | None = None):
+        from .gpu_puct import HashEvaluator
+
         lib = _bind()
         self.device = native.require_cuda(device)
         self.options = options or GpuPUCTOptions()
         self.lanes = int(lanes)
-        self.net = model if isinstance(model, NativePolicyValueNet) else NativePolicyValueNet(model, self.device)
+        if model is None or isinstance(model, HashEvaluator):
+            self.net = None
+        else:
+            self.net = model if isinstance(model, NativePolicyValueNet) else NativePolicyValueNet(model, self.device)
         seed = self.options.seed if seed is None else seed
+        sample_seed = seed if sample_seed is None else sample_seed
         neutral_cell = -1 if neutral is None else neutral[0] * 9 + neutral[1]
         self.params = SelfPlayParams(
             self.options.simulations, float(self.options.c_puct), float(self.options.dirichlet_alpha),
@@ -134,8 +190,8 @@ class SelfPlayEngine:
             float(self.options.fpu_reduction or 0.0),
             self.options.simulations + 10**9 if temperature_moves is None else int(temperature_moves),
             float(temperature), float(final_temperature), seed & (2**64 - 1), world_size * self.lanes, neutral_cell,
-            1 if self.options.tactical_checks else 0)
-        self.first_game = rank * self.lanes
+            1 if self.options.tactical_checks else 0, sample_seed & (2**64 - 1), int(game_limit))
+        self.first_game = rank * self.lanes if first_game is None else int(first_game)
         self.neutral_cell = neutral_cell
         nbytes = lib.gk_selfplay_workspace_bytes(self.lanes)
         self.storage = torch.empty(nbytes, dtype=torch.uint8, device=self.device)
@@ -143,12 +199,14 @@ class SelfPlayEngine:
         self.headfeat = torch.empty((self.lanes, 243), dtype=torch.float32, device=self.device)
         self.status = torch.zeros(2, dtype=torch.int32, device=self.device)
         self.replay = ReplayRing(replay_capacity, self.device) if replay_capacity > 0 else None
+        self.games = GameLog(game_log, self.device) if game_log > 0 else None
         bufs = SelfPlayBuffers()
         native.call("gk_selfplay_buffers", native.ptr(self.storage), self.lanes, bufs)
         base = self.storage.data_ptr()
         self.counters = self.storage[bufs.counters - base:bufs.counters - base + 64].view(torch.int64)
         self.states = self.storage[bufs.states - base:bufs.states - base + self.lanes * 64].view(torch.int32).view(
             self.lanes, 16)
+        self.lane_ply = self.storage[bufs.lane_ply - base:bufs.lane_ply - base + self.lanes * 4].view(torch.int32)
         self.timer = None
         self.reset()
 
@@ -163,13 +221,21 @@ class SelfPlayEngine:
         self.timer = Timer(plies * (self.options.simulations + 1))
         return self.timer
 
+    def set_simulations(self, simulations: int):
+        """Search `simulations` per move from the next ply on (at most the options' count)."""
+        if type(simulations) is not int or not 1 <= simulations <= self.options.simulations:
+            raise ValueError("simulations must be an integer in [1, options.simulations]")
+        self.params.simulations = simulations
+
     def step(self, plies: int = 1):
         with torch.cuda.device(self.device):
             stream = _launch_scope(self.device, self.storage, self.search.storage, self.headfeat)
             replay = self.replay.struct if self.replay is not None else None
+            games = self.games.struct if self.games is not None else None
+            net = self.net.struct if self.net is not None else None
             for _ in range(plies):
                 native.call("gk_selfplay_ply", native.ptr(self.storage), self.search.pointer, self.lanes,
-                            self.net.struct, self.params, replay, native.ptr(self.headfeat),
+                            net, self.params, replay, games, native.ptr(self.headfeat),
                             native.ptr(self.status), self.timer.handle if self.timer else None, stream)
 
     def stats(self) -> dict:

@@ -2,26 +2,30 @@
 
 ``collect_gpu_puct_games`` is the drop-in for the reference's
 ``collect_gpu_puct_games`` (python/kingdom_ai/gpu_training.py:124-175), the
-call behind the Trainer's CUDA self-play hook. Games run in chunks of
-``batch_size`` lanes on this package's kernels (rules, encoder, PUCT with the
-native tcgen05 network). The per-ply histories stay on the device until a
-chunk ends and then cross to the host in one copy per tensor. The returned
-``GameData`` / ``TrainingSample`` carry the fields of the reference types
+call behind the Trainer's CUDA self-play hook (python/kingdom_ai/loop.py:
+524-541). For the networks the native kernels run (``PolicyValueNet``,
+``GroupNormPolicyValueNet``) and for ``HashEvaluator`` it drives the
+device-resident engine (``SelfPlayEngine``, ``gk_selfplay_ply``): a whole ply
+per call with no host synchronisation inside it, ``batch_size`` lanes that
+start the next game as soon as one ends, and per-game action histories and
+replay rows kept on the device until the call's games are done, then copied to
+the host in one copy per tensor. Any other ``nn.Module`` runs through
+``GpuPUCT`` ply by ply with torch evaluating the leaves, in chunks of
+``batch_size`` games as the reference does. The returned ``GameData`` /
+``TrainingSample`` carry the fields of the reference types
 (python/kingdom_ai/training.py:17-30).
-
-For sustained throughput on one or more GPUs use ``SelfPlayEngine``
-(kingdom_ai/selfplay.py), which runs a whole ply natively without host
-synchronisation and refills finished lanes.
 """
 
 from __future__ import annotations
 
+import copy
 import enum
 import math
 from dataclasses import dataclass
 
 import torch
 
+from . import _native as native
 from .gpu_puct import GpuPUCT, GpuPUCTOptions
 from .gpu_rules import (GPU_ACTION_SIZE, GPU_ACTOR, GPU_CAPTURE, GPU_REASON, GPU_SUICIDE, GPU_TWO_PASSES,
                         GPU_WINNER, GpuStateBatch)
@@ -153,18 +157,84 @@ def _play_chunk(searcher, state, temperature, generator, temperature_moves, fina
     return games
 
 
+# Games per engine run: their replay rows (at most 166 per game, 3,655 B each)
+# stay on the device until the run ends, so a larger request runs in id ranges
+# of this size (about 3.7 GB of rows). Game randomness is keyed by game id, so
+# the split does not change any game.
+_GAMES_PER_RUN = 6144
+
+
+def _run_engine(engine, count):
+    """Step `engine` until `count` games have finished.
+
+    The host reads the finished-game counter one ply behind the GPU: after
+    enqueueing ply p it waits for ply p-1's counter copy, so the device always
+    has the next ply queued and never idles on the host.
+    """
+    from .selfplay import GAME_ACTIONS
+
+    stream = torch.cuda.current_stream(engine.device)
+    host = torch.zeros((2, engine.counters.numel()), dtype=torch.int64).pin_memory()
+    done = [torch.cuda.Event(), torch.cuda.Event()]
+    bound = (-(-count // engine.lanes)) * GAME_ACTIONS + 2
+    for ply in range(bound + 1):
+        engine.step()
+        host[ply % 2].copy_(engine.counters, non_blocking=True)
+        done[ply % 2].record(stream)
+        if ply >= 1:
+            done[(ply - 1) % 2].synchronize()
+            if int(host[(ply - 1) % 2, 1]) >= count:
+                break
+    stream.synchronize()
+    engine.check()
+    if engine.stats()["games"] != count:
+        raise RuntimeError("a game exceeded its finite move bound")
+
+
+def _engine_games(net, games, options, temperature, batch_size, seed, device, temperature_moves, final_temperature,
+                  record_history):
+    from .selfplay import GAME_ACTIONS, SelfPlayEngine
+
+    out = []
+    for start in range(0, games, _GAMES_PER_RUN):
+        count = min(_GAMES_PER_RUN, games - start)
+        lanes = min(batch_size, count)
+        engine = SelfPlayEngine(net, lanes, options, temperature=temperature, temperature_moves=temperature_moves,
+                                final_temperature=final_temperature, replay_capacity=count * GAME_ACTIONS,
+                                seed=options.seed, sample_seed=seed, device=device, game_log=count,
+                                game_limit=start + count, first_game=start)
+        _run_engine(engine, count)
+        rows = engine.stats()["rows"]
+        ring = engine.replay
+        feats, masks, policy, value, to_play = (t[:rows].cpu() for t in (ring.features, ring.masks, ring.policy,
+                                                                           ring.value, ring.to_play))
+        log = engine.games.read(count)
+        order = log["game_id"].argsort(kind="stable")
+        values, actors = value.tolist(), to_play.tolist()
+        for slot in order:
+            first, plies = int(log["first_row"][slot]), int(log["plies"][slot])
+            winner = Cell(int(log["winner"][slot]))
+            samples = [TrainingSample(feats[r], masks[r], policy[r], values[r], Cell(actors[r]))
+                       for r in range(first, first + plies)]
+            history = tuple(log["actions"][slot, :plies].tolist()) if record_history else None
+            out.append(GameData(samples, winner, _REASONS[int(log["reason"][slot])], history))
+        del engine
+    return out
+
+
 def collect_gpu_puct_games(model, games, *, options=None, temperature=1.0, batch_size=128, seed=42, device="cuda",
                            temperature_moves=None, final_temperature=0.0, record_history=False) -> list:
     """Play `games` complete games with GPU PUCT; return them in order as GameData.
 
     Same contract as the reference (gpu_training.py:124-175): ``options.seed``
     drives root noise and ``seed`` drives move sampling (default options use
-    ``seed`` for both, with root noise epsilon 0.25); games run in chunks of
-    ``batch_size`` lanes and finished lanes are not refilled;
-    ``temperature_moves`` switches each game to ``final_temperature`` after
-    that many plies; ``record_history`` keeps the played actions, which replay
-    the game from the default start. The caller's model and the global RNG
-    state are left untouched. Sample values are +1 for the winner's moves.
+    ``seed`` for both, with root noise epsilon 0.25); at most ``batch_size``
+    games are in flight; ``temperature_moves`` switches each game to
+    ``final_temperature`` after that many plies; ``record_history`` keeps the
+    played actions, which replay the game from the default start. The caller's
+    model and the global RNG state are left untouched. Sample values are +1
+    for the winner's moves. With the device engine, game k's randomness is
+    keyed by (seed, k, ply), so a game does not depend on ``batch_size``.
     """
     if type(games) is not int or games < 0:
         raise ValueError("games must be a non-negative integer")
@@ -181,6 +251,17 @@ def collect_gpu_puct_games(model, games, *, options=None, temperature=1.0, batch
         raise TypeError("options must be GpuPUCTOptions")
     if games == 0:
         return []
+    from .gpu_puct import HashEvaluator
+    from .model import NativePolicyValueNet, native_supported
+
+    if isinstance(model, HashEvaluator) or native_supported(model):
+        dev = native.require_cuda(device)
+        net = None
+        if not isinstance(model, HashEvaluator):
+            net = NativePolicyValueNet(copy.deepcopy(model).cpu().float(), dev)
+        with torch.cuda.device(dev), torch.no_grad():
+            return _engine_games(net, games, options, temperature, batch_size, seed, dev, temperature_moves,
+                                 final_temperature, record_history)
     searcher = GpuPUCT(model, options=options, device=device)
     generator = torch.Generator(device=searcher.device).manual_seed(seed ^ _SAMPLING_SALT)
     out = []

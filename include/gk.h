@@ -311,11 +311,32 @@ typedef struct {
     int temperature_moves;    /* plies per game that use `temperature` */
     double temperature;       /* before temperature_moves (0 = best action) */
     double final_temperature; /* afterwards */
-    uint64_t seed;            /* root noise and move sampling */
+    uint64_t seed;            /* root noise (GpuPUCTOptions.seed) */
     uint64_t game_stride;     /* game-id step when a lane starts its next game */
     int neutral_cell;         /* start position's neutral stone, -1 for none */
     int tactical_checks;      /* nonzero: gk_puct_root_tactics at every root (GpuPUCTOptions.tactical_checks) */
+    uint64_t sample_seed;     /* move sampling (the `seed` argument of collect_gpu_puct_games) */
+    uint64_t game_limit;      /* 0: lanes play forever; else a lane whose next game id would reach
+                                 game_limit parks on its finished position and plays no more */
 } gk_selfplay_params_t;
+
+/* Finished-game log of gk_selfplay_ply: the k-th game to finish (in device
+ * order) goes to slot k % capacity. Its action history replays the game from
+ * the start position through the rules (the record_history output of
+ * collect_gpu_puct_games, gpu_training.py:50-51, 89-90, 113), and its replay
+ * rows are rows first_row .. first_row + plies - 1 of the replay ring (ring
+ * index = row % replay capacity). */
+#define GK_GAME_ACTIONS (GK_MAX_PLIES + 2)
+typedef struct {
+    uint64_t* game_id;      /* [capacity] */
+    uint64_t* first_row;    /* [capacity] replay rows written before this game's */
+    int32_t* plies;         /* [capacity] moves played, = replay rows of the game */
+    int8_t* winner;         /* [capacity] 1 black, 2 white */
+    int8_t* reason;         /* [capacity] GPU reason code (GK_CAPTURE, GK_SUICIDE, GK_TWO_PASSES) */
+    uint32_t* final_state;  /* [capacity][16] packed final position */
+    uint8_t* actions;       /* [capacity][GK_GAME_ACTIONS] action of each ply (81 = pass) */
+    int64_t capacity;
+} gk_gamelog_t;
 
 /* FIFO replay ring in the CPU ReplayBuffer's row schema
  * (python/kingdom_ai/replay.py:106-125): features f32[cap,10,9,9],
@@ -355,14 +376,18 @@ GK_API int gk_selfplay_buffers(void* ws, int64_t lanes, gk_selfplay_buffers_t* o
 
 /* One ply of batched self-play: a full search per lane with the native
  * network (no host synchronisation), then one move per lane; finished games
- * are written to `replay` (may be NULL) and their lanes restart. `puct_ws`
- * is a search workspace for (lanes, simulations + 1); `headfeat` holds
+ * are written to `replay` and `games` (each may be NULL) and their lanes
+ * restart, or park once params->game_limit is reached. `puct_ws` is a search
+ * workspace for (lanes, simulations + 1); `headfeat` holds
  * gk_net_headfeat_bytes(lanes); `timer` (may be NULL, see gk_timer_create)
- * records the network tower's launches. Replaces one iteration of the
- * reference's per-ply loop (gpu_training.py:59-87). */
+ * records the network tower's launches. `net` may be NULL: leaves are then
+ * scored by the injected evaluator (gk_puct_hash_eval) and headfeat may be
+ * NULL. Replaces one iteration of the reference's per-ply loop
+ * (gpu_training.py:59-87). */
 GK_API int gk_selfplay_ply(void* sp_ws, void* puct_ws, int64_t lanes, const gk_net_t* net,
-                           const gk_selfplay_params_t* params, const gk_replay_t* replay, float* headfeat,
-                           uint32_t* status, void* timer, void* stream);
+                           const gk_selfplay_params_t* params, const gk_replay_t* replay,
+                           const gk_gamelog_t* games, float* headfeat, uint32_t* status, void* timer,
+                           void* stream);
 
 /* ------------------------------------------------------ batched search */
 

@@ -657,6 +657,119 @@ int gko_puct_search_batch(const int32_t* recs, int64_t n, int simulations, doubl
     return status;
 }
 
+/* ------------------------------------------------------------ self-play */
+/* One self-play game as the device engine plays it with the injected
+ * evaluator and no root noise. Per ply (python/kingdom_ai/gpu_training.py:
+ * 59-87): search, record the visit shares n / simulations as floats (:69-70),
+ * then move. At temperature 0 the move is the search's best action (:76-77);
+ * otherwise it is drawn with weights exp((log n - log n_max) / T) (:28-37),
+ * which are the visit counts themselves at T = 1. The draw uses the PCG32
+ * stream (sample_seed ^ GKO_SAMPLE_SALT, game * 256 + ply): at T = 1 an
+ * integer u = bounded(simulations) picks the first action whose running visit
+ * total exceeds u (exact integer arithmetic); at other temperatures
+ * u = uniform01 * total picks the first positive-weight action whose running
+ * weight total exceeds u. */
+#define GKO_SAMPLE_SALT 0x9E3779B97F4A7C15ULL
+
+static double o_uniform01(gk_pcg32* r) {
+    uint64_t hi = gk_pcg32_next(r) >> 5, lo = gk_pcg32_next(r) >> 6; /* 27 + 26 bits */
+    return ((double)(hi * 67108864ull + lo) + 0.5) * (1.0 / 9007199254740992.0);
+}
+
+int gko_selfplay_hash_game(uint64_t sample_seed, uint64_t game, int neutral_cell, int simulations, double c_puct,
+                           int temperature_moves, double temperature, double final_temperature, uint8_t* actions,
+                           float* policy, int32_t* rec) {
+    gko_initial(rec, neutral_cell);
+    for (int ply = 0; ply < GK_MAX_PLIES + 2; ++ply) {
+        if (rec[GK_REASON] != GK_NONE) return ply;
+        int32_t visits[GK_ACTIONS], stats[4];
+        double priors[GK_ACTIONS], values[2];
+        int status = gko_puct_search(rec, simulations, c_puct, visits, priors, stats, values);
+        if (status != 0) return status < 0 ? status : -1;
+        const int sims = stats[1];
+        for (int a = 0; a < GK_ACTIONS; ++a)
+            policy[(size_t)ply * GK_ACTIONS + a] = sims > 0 ? (float)visits[a] / (float)sims : 0.0f;
+        const double t = ply < temperature_moves ? temperature : final_temperature;
+        int action = stats[0];
+        if (t != 0.0 && sims > 0) {
+            gk_pcg32 r = gk_pcg32_seed(sample_seed ^ GKO_SAMPLE_SALT, game * 256u + (uint64_t)ply);
+            if (t == 1.0) {
+                int64_t u = (int64_t)gk_pcg32_bounded(&r, (uint32_t)sims), run = 0;
+                for (int a = 0; a < GK_ACTIONS; ++a) {
+                    run += visits[a];
+                    if (visits[a] > 0 && u < run) {
+                        action = a;
+                        break;
+                    }
+                }
+            } else {
+                int nmax = 0;
+                for (int a = 0; a < GK_ACTIONS; ++a) nmax = visits[a] > nmax ? visits[a] : nmax;
+                double w[GK_ACTIONS], total = 0.0;
+                for (int a = 0; a < GK_ACTIONS; ++a) {
+                    w[a] = visits[a] > 0 ? exp((log((double)visits[a]) - log((double)nmax)) / t) : 0.0;
+                    total += w[a];
+                }
+                double u = o_uniform01(&r) * total, run = 0.0;
+                for (int a = 0; a < GK_ACTIONS; ++a) {
+                    const double before = run;
+                    run += w[a];
+                    if (w[a] > 0.0 && u >= before && u < run) {
+                        action = a;
+                        break;
+                    }
+                }
+            }
+        }
+        if (action < 0 || !gko_play(rec, action)) return -1;
+        actions[ply] = (uint8_t)action;
+    }
+    return rec[GK_REASON] != GK_NONE ? GK_MAX_PLIES + 2 : -1;
+}
+
+typedef struct {
+    uint64_t sample_seed, first_game;
+    int64_t begin, end;
+    int neutral_cell, simulations, temperature_moves;
+    double c_puct, temperature, final_temperature;
+    uint8_t* actions;
+    float* policy;
+    int32_t* recs;
+    int32_t* plies;
+} selfplay_job;
+
+static void* selfplay_worker(void* arg) {
+    selfplay_job* j = (selfplay_job*)arg;
+    for (int64_t i = j->begin; i < j->end; ++i)
+        j->plies[i] = gko_selfplay_hash_game(j->sample_seed, j->first_game + (uint64_t)i, j->neutral_cell,
+                                             j->simulations, j->c_puct, j->temperature_moves, j->temperature,
+                                             j->final_temperature, j->actions + i * (GK_MAX_PLIES + 2),
+                                             j->policy + i * (int64_t)(GK_MAX_PLIES + 2) * GK_ACTIONS,
+                                             j->recs + i * GK_STATE_WIDTH);
+    return NULL;
+}
+
+void gko_selfplay_hash_games(uint64_t sample_seed, uint64_t first_game, int64_t n, int neutral_cell,
+                             int simulations, double c_puct, int temperature_moves, double temperature,
+                             double final_temperature, uint8_t* actions, float* policy, int32_t* recs,
+                             int32_t* plies, int threads) {
+    if (threads < 1) threads = 1;
+    if (threads > 256) threads = 256;
+    pthread_t tid[256];
+    selfplay_job jobs[256];
+    int64_t per = (n + threads - 1) / threads;
+    int started = 0;
+    for (int t = 0; t < threads; ++t) {
+        int64_t b = (int64_t)t * per, e = b + per < n ? b + per : n;
+        if (b >= e) break;
+        jobs[t] = (selfplay_job){sample_seed, first_game, b, e, neutral_cell, simulations, temperature_moves,
+                                 c_puct, temperature, final_temperature, actions, policy, recs, plies};
+        pthread_create(&tid[t], NULL, selfplay_worker, &jobs[t]);
+        ++started;
+    }
+    for (int t = 0; t < started; ++t) pthread_join(tid[t], NULL);
+}
+
 /* ----------------------------------------------------------- BatchedPUCT */
 /* The evaluation searcher of mcts/src/BatchedPUCT.cpp restated: leaf batches
  * gathered under a virtual loss of one per pending simulation (143-227), the

@@ -83,3 +83,51 @@ def test_zero_temperature_plays_the_search_best_move():
             visits = sample.policy
             assert visits[action] == visits.max()
 
+
+def test_games_do_not_depend_on_batch_size_or_run_split(monkeypatch):
+    """The device engine keys each game's randomness by its index, so neither
+    the number of lanes nor splitting the call into runs changes a game."""
+    from kingdom_ai import training
+    from kingdom_ai.gpu_puct import HashEvaluator
+
+    whole = _collect(HashEvaluator(), 10, batch_size=10, seed=4)
+    narrow = _collect(HashEvaluator(), 10, batch_size=3, seed=4)
+    monkeypatch.setattr(training, "_GAMES_PER_RUN", 4)
+    split = _collect(HashEvaluator(), 10, batch_size=3, seed=4)
+    for a, b, c in zip(whole, narrow, split):
+        assert a.action_history == b.action_history == c.action_history
+        assert a.winner == b.winner == c.winner and a.reason == b.reason == c.reason
+        for x, y in zip(a.samples, c.samples):
+            assert np.array_equal(x.policy.numpy(), y.policy.numpy()) and x.value == y.value
+
+
+def test_other_modules_run_through_gpupuct(oracle):
+    """A module the native kernels do not run is evaluated by torch inside
+    GpuPUCT, ply by ply; its games replay exactly too."""
+    import torch
+    from torch import nn
+
+    class Flat(nn.Module):
+        def __init__(self):
+            super().__init__()
+            self.fc = nn.Linear(810, 83)
+
+        def forward(self, x):
+            out = self.fc(x.flatten(1))
+            return out[:, :82], torch.tanh(out[:, 82])
+
+    torch.manual_seed(0)
+    games = _collect(Flat(), 4, batch_size=4, seed=8)
+    for game in games:
+        _replay_and_check(oracle, game)
+
+
+def test_the_callers_model_is_left_untouched():
+    import torch
+    from kingdom_ai.model import random_network
+
+    model = random_network(64, 1, 3).train()
+    before = {k: v.clone() for k, v in model.state_dict().items()}
+    _collect(model, 2, batch_size=2, seed=1)
+    assert model.training
+    assert all(torch.equal(before[k], v) for k, v in model.state_dict().items())
