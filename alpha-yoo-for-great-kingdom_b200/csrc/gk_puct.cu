@@ -634,7 +634,8 @@ using namespace gk;
 extern "C" {
 
 size_t gk_puct_workspace_bytes(int64_t batch, int capacity) {
-    if (batch <= 0 || capacity < 1) return 0;
+    // Beyond 2^40 nodes (a workspace of petabytes) the byte counts could wrap.
+    if (batch <= 0 || capacity < 1 || capacity >= (1 << 24) || batch > ((int64_t)1 << 40) / capacity) return 0;
     return puct_layout(nullptr, batch, capacity, nullptr);
 }
 
@@ -652,6 +653,7 @@ int gk_puct_buffers(void* ws, int64_t batch, int capacity, gk_puct_buffers_t* ou
     out->errors = v.errors;
     out->leaf = v.leaf;
     out->root_allow = v.root_allow;
+    out->node_visits = v.node_visits;
     return 0;
 }
 

@@ -47,6 +47,8 @@ struct SelfPlayView {
     gk_bits* hist_bits;            // [kHist][B]
     float* hist_policy;            // [kHist][B][82]
     uint8_t* hist_action;          // [kHist][B] action played at each ply
+    int32_t* last_action;          // [B] action played in the last ply (-1: none)
+    float* last_policy;            // [B][82] visit shares of the last ply's search
     int64_t* best;                 // [B] best action of the last search
     unsigned long long* counters;  // [kCounters]
 };
@@ -66,6 +68,8 @@ inline size_t selfplay_layout(void* base, int64_t B, SelfPlayView* v) {
     t.hist_bits = (gk_bits*)take((size_t)kHist * B * sizeof(gk_bits));
     t.hist_policy = (float*)take((size_t)kHist * B * GK_ACTIONS * 4);
     t.hist_action = (uint8_t*)take((size_t)kHist * B);
+    t.last_action = (int32_t*)take(B * 4);
+    t.last_policy = (float*)take((size_t)B * GK_ACTIONS * 4);
     t.best = (int64_t*)take(B * 8);
     t.counters = (unsigned long long*)take(kCounters * 8);
     if (v) *v = t;
@@ -98,6 +102,7 @@ __global__ void selfplay_reset_kernel(SelfPlayView v, int64_t B, int neutral, ui
         v.lane_ply[b] = 0;
         v.game_id[b] = first_game + (uint64_t)b;
         v.best[b] = -1;
+        v.last_action[b] = -1;
     }
     if (blockIdx.x == 0 && threadIdx.x < kCounters) v.counters[threadIdx.x] = 0ull;
 }
@@ -140,10 +145,13 @@ __global__ void __launch_bounds__(128) selfplay_advance_kernel(SelfPlayView v, P
     const int64_t b = (blockIdx.x * (int64_t)blockDim.x + threadIdx.x) >> 5;
     if (b >= B) return;
     const int ply = v.lane_ply[b];
-    if (ply < 0) return;  // parked: the game limit was reached
-    if (ap.game_limit != 0 && v.game_id[b] >= ap.game_limit) {
-        // A lane that started past the limit (more lanes than games) plays nothing.
-        if (lane == 0) v.lane_ply[b] = -1;
+    if (ply < 0 || (ap.game_limit != 0 && v.game_id[b] >= ap.game_limit)) {
+        // Parked (the game limit was reached), or a lane that started past
+        // the limit (more lanes than games): it plays nothing.
+        if (lane == 0) {
+            v.lane_ply[b] = -1;
+            v.last_action[b] = -1;
+        }
         return;
     }
     gk_bits s = v.states[b];
@@ -167,10 +175,11 @@ __global__ void __launch_bounds__(128) selfplay_advance_kernel(SelfPlayView v, P
     }
     // Policy target: raw visit proportions, before temperature.
     float* hp = v.hist_policy + ((int64_t)ply * B + b) * GK_ACTIONS;
+    float* lp = v.last_policy + b * GK_ACTIONS;
 #pragma unroll
     for (int k = 0; k < 3; ++k) {
         const int a = lane + 32 * k;
-        if (a < GK_ACTIONS) hp[a] = sims > 0 ? __fdiv_rn((float)n[k], (float)sims) : 0.0f;
+        if (a < GK_ACTIONS) hp[a] = lp[a] = sims > 0 ? __fdiv_rn((float)n[k], (float)sims) : 0.0f;
     }
     if (lane == 0) v.hist_bits[(int64_t)ply * B + b] = s;
 
@@ -220,6 +229,7 @@ __global__ void __launch_bounds__(128) selfplay_advance_kernel(SelfPlayView v, P
         const bool ok = play(s, action);
         if (!ok) atomicAdd(&v.counters[kErrors], 1ull);
         v.hist_action[(int64_t)ply * B + b] = (uint8_t)(action >= 0 && action < GK_ACTIONS ? action : 255);
+        v.last_action[b] = action;
         atomicAdd(&v.counters[kMoves], 1ull);
         atomicAdd(&v.counters[kEvaluations], (unsigned long long)p.evals[b]);
         finished = gk_reason(&s) != GK_NONE;
@@ -322,6 +332,8 @@ int gk_selfplay_buffers(void* ws, int64_t lanes, gk_selfplay_buffers_t* out) {
     out->lane_ply = v.lane_ply;
     out->game_id = v.game_id;
     out->counters = reinterpret_cast<uint64_t*>(v.counters);
+    out->last_action = v.last_action;
+    out->last_policy = v.last_policy;
     return 0;
 }
 

@@ -15,3 +15,4 @@ from .training import Cell, EndReason, GameData, TrainingBatch, TrainingSample, 
 from .replay import DeviceReplayBuffer, validate_rows  # noqa: F401
 from .batched_puct import BatchedSearchResult, GpuBatchedPUCT, PUCTOptions  # noqa: F401
 from .evaluation import EvaluationResult, evaluate_models_gpu  # noqa: F401
+from .engine_api import BatchedPUCT, PUCTMoveStatistics, PUCTSearchResult, encode_puct_batch  # noqa: F401

@@ -33,7 +33,7 @@ class PuctOptions(ctypes.Structure):
 class PuctBuffers(ctypes.Structure):
     _fields_ = [("needs_eval", c_void_p), ("leaf_bits", c_void_p), ("leaf_value", c_void_p),
                 ("policy", c_void_p), ("noise", c_void_p), ("active", c_void_p), ("active_count", c_void_p),
-                ("errors", c_void_p), ("leaf", c_void_p), ("root_allow", c_void_p)]
+                ("errors", c_void_p), ("leaf", c_void_p), ("root_allow", c_void_p), ("node_visits", c_void_p)]
 
 
 class PuctResults(ctypes.Structure):

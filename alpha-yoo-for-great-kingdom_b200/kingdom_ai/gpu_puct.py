@@ -122,6 +122,7 @@ class SearchWorkspace:
         self.errors = view(buffers.errors, batch, torch.int32, (batch,))
         self.leaf = view(buffers.leaf, batch, torch.int32, (batch,))
         self.root_allow = view(buffers.root_allow, batch * 3, torch.int32, (batch, 3))
+        self.node_visits = view(buffers.node_visits, batch * capacity, torch.int32, (batch, capacity))
 
     def root_masks(self, rows: torch.Tensor) -> torch.Tensor:
         """bool [len(rows), 82]: the root candidates of the given trees."""
@@ -312,11 +313,17 @@ def _allocate_results(batch, device):
     return _Results(batch, device)
 
 
-def search_hash(roots: torch.Tensor, simulations: int, c_puct: float = 1.5) -> GpuSearchResult:
-    """Full injected-evaluator search in one native call (no host synchronisation)."""
+def search_hash(roots: torch.Tensor, simulations: int, c_puct: float = 1.5,
+                workspace: SearchWorkspace | None = None) -> GpuSearchResult:
+    """Full injected-evaluator search in one native call (no host synchronisation).
+
+    `workspace` (batch, simulations + 1) may be passed to reuse it and read
+    the trees afterwards."""
     batch = roots.shape[0]
     device = roots.device
-    ws = SearchWorkspace(batch, simulations + 1, device)
+    ws = workspace if workspace is not None else SearchWorkspace(batch, simulations + 1, device)
+    if (ws.batch, ws.capacity) != (batch, simulations + 1):
+        raise ValueError("workspace size does not match the search")
     out = _allocate_results(batch, device)
     opts = native.PuctOptions(float(c_puct), 0.0, 0, 0.0)
     with torch.cuda.device(device):

@@ -59,7 +59,7 @@ GAME_ACTIONS = 2 * 81 + 4  # GK_GAME_ACTIONS: longest game plus slack
 
 class SelfPlayBuffers(ctypes.Structure):
     _fields_ = [("states", ctypes.c_void_p), ("lane_ply", ctypes.c_void_p), ("game_id", ctypes.c_void_p),
-                ("counters", ctypes.c_void_p)]
+                ("counters", ctypes.c_void_p), ("last_action", ctypes.c_void_p), ("last_policy", ctypes.c_void_p)]
 
 
 def _bind():
@@ -198,6 +198,7 @@ class SelfPlayEngine:
         self.search = SearchWorkspace(self.lanes, self.options.simulations + 1, self.device)
         self.headfeat = torch.empty((self.lanes, 243), dtype=torch.float32, device=self.device)
         self.status = torch.zeros(2, dtype=torch.int32, device=self.device)
+        self._load_status = torch.zeros(1, dtype=torch.int32, device=self.device)
         self.replay = ReplayRing(replay_capacity, self.device) if replay_capacity > 0 else None
         self.games = GameLog(game_log, self.device) if game_log > 0 else None
         bufs = SelfPlayBuffers()
@@ -207,6 +208,10 @@ class SelfPlayEngine:
         self.states = self.storage[bufs.states - base:bufs.states - base + self.lanes * 64].view(torch.int32).view(
             self.lanes, 16)
         self.lane_ply = self.storage[bufs.lane_ply - base:bufs.lane_ply - base + self.lanes * 4].view(torch.int32)
+        self.last_action = self.storage[bufs.last_action - base:bufs.last_action - base + self.lanes * 4].view(
+            torch.int32)
+        self.last_policy = self.storage[bufs.last_policy - base:bufs.last_policy - base + self.lanes * 82 * 4].view(
+            torch.float32).view(self.lanes, 82)
         self.timer = None
         self.reset()
 
@@ -238,11 +243,34 @@ class SelfPlayEngine:
                             net, self.params, replay, games, native.ptr(self.headfeat),
                             native.ptr(self.status), self.timer.handle if self.timer else None, stream)
 
+    def load_records(self, records: torch.Tensor):
+        """Set every lane's position from wire records (int32 [lanes,170], host
+        or device; a pinned host tensor is copied asynchronously). Lanes keep
+        their game ids and ply counts; the next ply searches these positions."""
+        if tuple(records.shape) != (self.lanes, 170) or records.dtype != torch.int32:
+            raise ValueError("records must be int32 [lanes, 170]")
+        with torch.cuda.device(self.device):
+            dev = records.to(self.device, non_blocking=True) if records.device != self.device else records
+            stream = _launch_scope(self.device, dev, self.storage)
+            native.call("gk_records_to_bits", native.ptr(dev), native.ptr(self.states), native.ptr(self._load_status),
+                        self.lanes, stream)
+
+    def records(self, out: torch.Tensor | None = None) -> torch.Tensor:
+        """Every lane's position as wire records (int32 [lanes,170] on the device)."""
+        with torch.cuda.device(self.device):
+            if out is None:
+                out = torch.empty((self.lanes, 170), dtype=torch.int32, device=self.device)
+            stream = _launch_scope(self.device, out, self.storage)
+            native.call("gk_bits_to_records", native.ptr(self.states), native.ptr(out), self.lanes, stream)
+        return out
+
     def stats(self) -> dict:
         values = self.counters.cpu().tolist()
         return dict(zip(COUNTER_NAMES, values))
 
     def check(self):
+        if int(self._load_status.item()):
+            raise ValueError("a loaded record is outside the wire format's value ranges")
         code = int(self.status[0].item())
         stats = self.stats()
         if code or stats["errors"]:

@@ -122,141 +122,255 @@ def peaks():
     return 1400.0, 6650.0, "fallback", 1590.0
 
 
-def cpu_baseline_sample(seconds: float = 15.0):
-    """Reference C++ PUCT (compiled from its sources) + fp32 CPU network, batch 1.
+REF_INSTALL = ROOT / "baseline" / "_ref"  # the reference package, installed offline with pip
 
-    Mirrors the reference's CPU self-play (collect_puct_game: kingdom::PUCT with
-    a NeuralAgent-style single-position evaluator) on the same network and
-    search settings; runs searches from the opening until `seconds` elapse.
+
+def _reference_imports():
+    """Put the installed reference first on sys.path (its package is also
+    named kingdom_ai, so this runs only in processes that never import ours)."""
+    if not (REF_INSTALL / "kingdom_ai").exists():
+        raise FileNotFoundError("the reference is not installed under baseline/_ref")
+    sys.path.insert(0, str(REF_INSTALL))
+
+
+def reference_cpu_selfplay(steps: int, warmup: int):
+    """The reference's own CPU self-play path on every host core.
+
+    It is the pattern of examples/gpu_puct_benchmark.py:57-77 and of the
+    "CPU PUCT + CPU batch inference" row of docs/performance.md:292, run through
+    the reference's public API: one kingdom::PUCT (my_board_engine.PUCT,
+    400 simulations, c_puct 1.5, Dirichlet 0.3 / 0.25) and one game per worker
+    thread, `cores` workers; leaves from all workers are batched into one
+    fp32 CPU forward of the reference's PolicyValueNet(64, 6) by its
+    BatchedEvaluator (1 ms batch deadline); moves are sampled from the visits
+    at T = 1 for 10 plies, then the best move (sample_visits). torch runs
+    cores / 2 intra-op threads, set explicitly so torchrun's
+    OMP_NUM_THREADS=1 cannot change it (the fastest split measured on the
+    B200 host). One step = one move in every worker's game.
     """
-    import ctypes
+    from concurrent.futures import ThreadPoolExecutor
 
-    import numpy as np
+    _reference_imports()
     import torch
+    import my_board_engine as engine
+    from kingdom_ai import BatchedEvaluator, PolicyValueNet
+    from kingdom_ai.puct import sample_visits
 
-    from oracle.oracle import Reference, RefState
+    cores = len(os.sched_getaffinity(0))
+    workers, threads = cores, max(1, cores // 2)
+    torch.set_num_threads(threads)
+    torch.manual_seed(1234)
+    model = PolicyValueNet(CHANNELS, BLOCKS).eval()
+    states = [engine.State() for _ in range(workers)]
+    plies = [0] * workers
+    generators = [torch.Generator().manual_seed(100 + i) for i in range(workers)]
+    searchers = [engine.PUCT(engine.PUCTOptions(simulations=SIMULATIONS, c_puct=1.5, seed=1000 + i,
+                                                dirichlet_alpha=0.3, dirichlet_epsilon=0.25))
+                 for i in range(workers)]
+    with BatchedEvaluator(model, device="cpu", max_batch_size=workers, max_wait_ms=1.0) as evaluator, \
+            ThreadPoolExecutor(workers) as pool:
+        def move(i):
+            result = searchers[i].search(states[i], evaluator)
+            choice = sample_visits(result, 1.0 if plies[i] < 10 else 0.0, generators[i])
+            if not states[i].play(choice).accepted():
+                raise RuntimeError("the reference played an illegal move")
+            plies[i] += 1
+            if states[i].result.finished():
+                states[i], plies[i] = engine.State(), 0
+            return result.simulations
 
-    from kingdom_ai.model import calibrate_batchnorm, random_network
-    from oracle.oracle import Oracle
+        for _ in range(warmup):
+            sum(pool.map(move, range(workers)))
+        sims, seconds = 0, []
+        for _ in range(steps):
+            start = time.perf_counter()
+            sims += sum(pool.map(move, range(workers)))
+            seconds.append(time.perf_counter() - start)
+    total = sum(seconds)
+    return {"value": sims / total, "unit": "simulations/s", "moves_per_s": steps * workers / total,
+            "ms_per_step": 1000.0 * total / steps, "cores": cores, "kind": "reference",
+            "sample": f"{steps} steps x {workers} concurrent games x {SIMULATIONS} simulations after {warmup} "
+                      f"warm-up steps: the reference's my_board_engine.PUCT per worker thread + "
+                      f"kingdom_ai.BatchedEvaluator (PolicyValueNet({CHANNELS}, {BLOCKS}) fp32, batch <= "
+                      f"{workers}, {threads} torch threads), {total:.1f} s"}
 
-    ref = Reference()
-    # Same network as the GPU arm: same seed, batch norms calibrated on the
-    # same generated positions (here produced by the CPU oracle).
-    oracle = Oracle()
-    features, _ = oracle.encode(oracle.gen_positions(1234, 4096))
-    model = calibrate_batchnorm(random_network(CHANNELS, BLOCKS, 1234), torch.from_numpy(features)).float().eval()
-    ref.lib.gkr_puct_search_cb.argtypes = [ctypes.c_void_p, ctypes.c_int, ctypes.c_double, ctypes.c_double,
-                                           ctypes.c_double, ctypes.c_uint64, ctypes.c_void_p, ctypes.c_void_p,
-                                           np.ctypeslib.ndpointer(np.int32), np.ctypeslib.ndpointer(np.int32)]
-    ref.lib.gkr_puct_search_cb.restype = ctypes.c_int
-    threads = torch.get_num_threads()
-    EVAL = ctypes.CFUNCTYPE(None, ctypes.POINTER(ctypes.c_float), ctypes.POINTER(ctypes.c_uint8),
-                            ctypes.POINTER(ctypes.c_double), ctypes.POINTER(ctypes.c_double), ctypes.c_void_p)
 
-    def evaluate(features, mask, policy, value, ctx):
-        f = torch.from_numpy(np.ctypeslib.as_array(features, shape=(810,)).copy()).view(1, 10, 9, 9)
-        m = torch.from_numpy(np.ctypeslib.as_array(mask, shape=(82,)).astype(bool))
-        with torch.inference_mode():
-            logits, v = model(f)
-            p = torch.softmax(logits[0].masked_fill(~m, -torch.inf), 0).masked_fill(~m, 0.0)
-        out = np.ctypeslib.as_array(policy, shape=(82,))
-        out[:] = p.double().numpy()
-        value[0] = float(v[0])
+def reference_nvrtc_selfplay(plies: int, warmup: int, lanes: int = LANES):
+    """The reference's own GPU path (NVRTC kernels) on this B200.
 
-    callback = EVAL(evaluate)
-    state = RefState.initial(ref, 40)
-    visits = np.zeros(82, np.int32)
-    stats = np.zeros(4, np.int32)
-    sims = moves = 0
+    The per-ply loop of _collect_chunk (python/kingdom_ai/gpu_training.py:
+    59-87) through its public classes: GpuStateBatch.encode, GpuPUCT.search
+    (400 simulations, c_puct 1.5, Dirichlet 0.3 / 0.25) with the reference's
+    PolicyValueNet(64, 6) in fp32 as leaf evaluator, visit sampling at T = 1
+    for 10 plies then the best move, GpuStateBatch.play; `lanes` games from
+    the opening. The stock collect_gpu_puct_games plays every chunk to the
+    end of its longest game (about 100 plies of 3.4 s at 4096 lanes), so the
+    loop is timed over a bounded number of plies after `warmup` plies, with
+    CUDA synchronisation before each clock read (gpu_puct_benchmark.py:87-90).
+    Compilation and model transfer happen in the warm-up.
+    """
+    _reference_imports()
+    import torch
+    from kingdom_ai import PolicyValueNet
+    from kingdom_ai.gpu_puct import GpuPUCT, GpuPUCTOptions
+    from kingdom_ai.gpu_rules import GPU_REASON, GpuStateBatch
+    from kingdom_ai.gpu_runtime import nvrtc_version
+    from kingdom_ai.gpu_training import _visit_sampling_weights
+
+    torch.manual_seed(1234)
+    searcher = GpuPUCT(PolicyValueNet(CHANNELS, BLOCKS), GpuPUCTOptions(
+        simulations=SIMULATIONS, c_puct=1.5, dirichlet_alpha=0.3, dirichlet_epsilon=0.25, seed=7))
+    state = GpuStateBatch.initial(lanes)
+    generator = torch.Generator(device="cuda").manual_seed(11)
+    sims = torch.zeros((), dtype=torch.int64, device="cuda")
+
+    def ply(index):
+        alive = state.states[:, GPU_REASON] == 0
+        state.encode()
+        result = searcher.search(state)
+        if index < 10:
+            weights = _visit_sampling_weights(result.visits, 1.0)
+            weights[:, -1] += (~alive).to(weights.dtype)
+            actions = torch.where(alive, torch.multinomial(weights, 1, generator=generator).flatten(),
+                                  result.actions)
+        else:
+            actions = result.actions
+        state.play(actions)
+        sims.add_(result.simulations.sum())
+
+    for i in range(warmup):
+        ply(i)
+    torch.cuda.synchronize()
+    sims.zero_()
     start = time.perf_counter()
-    while time.perf_counter() - start < seconds:
-        status = ref.lib.gkr_puct_search_cb(state.h, SIMULATIONS, 1.5, 0.3, 0.25, 42 + moves,
-                                            ctypes.cast(callback, ctypes.c_void_p), None, visits, stats)
-        if status != 0:
-            raise RuntimeError("reference PUCT failed")
-        sims += int(stats[1])
-        moves += 1
-        if not state.play(int(stats[0])) or state.record()[166] != 0:
-            state = RefState.initial(ref, 40)
-    elapsed = time.perf_counter() - start
-    return {"value": sims / elapsed, "unit": "simulations/s", "cores": threads, "kind": "reference",
-            "moves_per_s": moves / elapsed,
-            "sample": f"{moves} moves x {SIMULATIONS} simulations from the opening (reference kingdom::PUCT "
-                      f"compiled from source, fp32 PyTorch CPU network at batch 1, {threads} threads), "
-                      f"{elapsed:.1f} s"}
+    for i in range(warmup, warmup + plies):
+        ply(i)
+    torch.cuda.synchronize()
+    seconds = time.perf_counter() - start
+    return {"value": int(sims.item()) / seconds, "unit": "simulations/s", "moves_per_s": lanes * plies / seconds,
+            "ms_per_ply": 1000.0 * seconds / plies, "lanes": lanes, "plies": plies, "warmup_plies": warmup,
+            "nvrtc": "%d.%d" % nvrtc_version(),
+            "path": "reference GpuStateBatch / GpuPUCT (NVRTC kernels) + PolicyValueNet(64, 6) fp32, "
+                    "the per-ply loop of collect_gpu_puct_games"}
+
+
+def _subprocess_json(argv, timeout):
+    """Run bench.py in a fresh interpreter and return its last JSON line."""
+    env = dict(os.environ)
+    for key in ("RANK", "LOCAL_RANK", "WORLD_SIZE", "LOCAL_WORLD_SIZE", "MASTER_ADDR", "MASTER_PORT",
+                "TORCHELASTIC_RUN_ID", "GROUP_RANK", "ROLE_RANK"):
+        env.pop(key, None)
+    try:
+        out = subprocess.run([sys.executable, str(ROOT / "bench.py"), *argv], capture_output=True, text=True,
+                             timeout=timeout, env=env)
+    except subprocess.TimeoutExpired:
+        return {"value": None, "unavailable": f"timed out after {timeout} s"}
+    lines = [line for line in out.stdout.splitlines() if line.startswith("{")]
+    if out.returncode != 0 or not lines:
+        return {"value": None, "unavailable": (out.stderr.strip().splitlines() or ["no output"])[-1][:300]}
+    return json.loads(lines[-1])
 
 
 def reference_arm(args):
-    rank = int(os.environ.get("RANK", "0"))
-    if rank != 0:
+    """`--impl reference`: the reference's CPU self-play on the host cores,
+    K timed steps after W warm-up steps, rank 0 only."""
+    if int(os.environ.get("RANK", "0")) != 0:
         return
     try:
-        base = cpu_baseline_sample(max(5.0, min(60.0, 4.0 * args.steps)))
-    except FileNotFoundError as exc:
-        print(json.dumps({"impl": "reference", "unavailable": f"reference engine not built: {exc}"}))
+        base = reference_cpu_selfplay(args.steps, args.warmup)
+    except Exception as exc:  # noqa: BLE001 - the line says why
+        print(json.dumps({"impl": "reference", "unavailable": f"{type(exc).__name__}: {exc}"[:300]}))
         return
     line = {
         "impl": "reference", "metric": METRIC, "value": base["value"], "unit": "simulations/s",
-        "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
-        "ms_per_step": 1000.0 * LANES * SIMULATIONS / base["value"], "higher_is_better": True,
-        "scaling": "weak", "vs_baseline": None, "dtype": "fp32", "data": "synthetic",
+        "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup, "ms_per_step": base["ms_per_step"],
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "fp32", "data": "synthetic",
         "moves_per_s": base["moves_per_s"],
-        "config": {"workload": f"self-play, {CHANNELS}ch x {BLOCKS} blocks net, {SIMULATIONS} sims/move, "
-                               "c_puct 1.5, Dirichlet 0.3/0.25", "lanes": 1},
+        "config": {"workload": f"self-play, {CHANNELS}ch x {BLOCKS}-block net (the reference's PolicyValueNet), "
+                               f"{SIMULATIONS} sims/move, c_puct 1.5, Dirichlet 0.3/0.25, T=1 for 10 plies "
+                               "then best", "concurrent_games": base["cores"],
+                   "path": "CPU: my_board_engine.PUCT per worker thread + kingdom_ai.BatchedEvaluator"},
         "cpu_baseline": base,
         "e2e": {"value": base["value"], "unit": "simulations/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
 
 
-def e2e_arm(model, steps: int, warmup: int, device):
-    """The same self-play ply through the public API with host buffers.
+def nvrtc_arm(args):
+    """`--impl nvrtc`: the reference's NVRTC GPU path on cuda:0 (one JSON line)."""
+    try:
+        line = reference_nvrtc_selfplay(args.steps, args.warmup)
+    except Exception as exc:  # noqa: BLE001 - the line says why
+        line = {"value": None, "unavailable": f"{type(exc).__name__}: {exc}"[:300]}
+    line["impl"] = "nvrtc"
+    print(json.dumps(line), flush=True)
 
-    Every step copies the 4096 current wire records from pinned host memory,
-    runs GpuPUCT.search (native network, 400 simulations), plays the chosen
-    actions with GpuStateBatch.play and reads the actions, visit policies and
-    new records back to the host; finished games restart on the host.
-    """
-    import torch
 
-    import kingdom_ai
-    from kingdom_ai.gpu_rules import GPU_REASON
+class HostPly:
+    """One self-play ply driven from host memory through the engine's public
+    API: the lanes' positions are copied in from pinned host records, the
+    ply runs (search, temperature sampling, history, replay flush), and the
+    new positions, the moves played, the visit-share targets and the replay
+    rows of games that finished cross back to pinned host buffers."""
 
-    opts = kingdom_ai.GpuPUCTOptions(simulations=SIMULATIONS, c_puct=1.5, dirichlet_alpha=0.3,
-                                     dirichlet_epsilon=0.25, seed=7)
-    searcher = kingdom_ai.GpuPUCT(model, opts, device=device)
-    initial = kingdom_ai.GpuStateBatch.initial(1, device=device).states.cpu()
-    host = initial.repeat(LANES, 1).pin_memory()
-    actions_h = torch.empty(LANES, dtype=torch.int64).pin_memory()
-    policy_h = torch.empty((LANES, 82), dtype=torch.float32).pin_memory()
-    h2d = host.numel() * 4
-    d2h = actions_h.numel() * 8 + policy_h.numel() * 4 + host.numel() * 4
+    def __init__(self, engine):
+        import torch
 
-    def step():
-        states = host.to(device, non_blocking=True)
-        batch = kingdom_ai.GpuStateBatch(states)
-        result = searcher.search(batch)
-        batch.play(result.actions)
-        actions_h.copy_(result.actions, non_blocking=True)
-        policy_h.copy_(result.policy, non_blocking=True)
-        host.copy_(batch.states, non_blocking=True)
-        torch.cuda.current_stream(device).synchronize()
-        done = host[:, GPU_REASON] != 0
-        if bool(done.any()):
-            host[done] = initial
+        self.engine = engine
+        n = engine.lanes
+        self.records = engine.records().cpu().pin_memory()
+        self.records_dev = torch.empty_like(self.records, device=engine.device)
+        self.actions = torch.empty(n, dtype=torch.int32).pin_memory()
+        self.policy = torch.empty((n, 82), dtype=torch.float32).pin_memory()
+        self.counters = torch.empty(engine.counters.numel(), dtype=torch.int64).pin_memory()
+        cap = 4 * n
+        ring = engine.replay
+        self.rows = [torch.empty((cap,) + tuple(t.shape[1:]), dtype=t.dtype).pin_memory()
+                     for t in (ring.features, ring.masks, ring.policy, ring.value, ring.to_play)]
+        self.row_bytes = sum(t[0].numel() * t.element_size() for t in self.rows)
+        self.rows_seen = int(engine.stats()["rows"])
+        self.rows_out = 0
+        self.h2d = self.records.numel() * 4
+        self.d2h_fixed = (self.records.numel() * 4 + self.actions.numel() * 4 + self.policy.numel() * 4
+                          + self.counters.numel() * 8)
 
-    for _ in range(warmup):
-        step()
-    torch.cuda.synchronize(device)
-    start = time.perf_counter()
-    for _ in range(steps):
-        step()
-    torch.cuda.synchronize(device)
-    elapsed = time.perf_counter() - start
-    return {"value": steps * LANES * SIMULATIONS / elapsed, "unit": "simulations/s",
-            "moves_per_s": steps * LANES / elapsed, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
-            "api": "GpuStateBatch + GpuPUCT.search + GpuStateBatch.play with pinned host records",
-            "_moves": steps * LANES, "_elapsed": elapsed}
+    def __call__(self):
+        import torch
+
+        e = self.engine
+        e.load_records(self.records)
+        e.step()
+        e.records(self.records_dev)
+        self.records.copy_(self.records_dev, non_blocking=True)
+        self.actions.copy_(e.last_action, non_blocking=True)
+        self.policy.copy_(e.last_policy, non_blocking=True)
+        self.counters.copy_(e.counters, non_blocking=True)
+        torch.cuda.current_stream(e.device).synchronize()
+        written = int(self.counters[2])
+        ring = e.replay
+        while self.rows_seen < written:
+            count = min(written - self.rows_seen, self.rows[0].shape[0], ring.capacity - self.rows_seen % ring.capacity)
+            lo = self.rows_seen % ring.capacity
+            for host, dev in zip(self.rows, (ring.features, ring.masks, ring.policy, ring.value, ring.to_play)):
+                host[:count].copy_(dev[lo:lo + count], non_blocking=True)
+            torch.cuda.current_stream(e.device).synchronize()
+            self.rows_seen += count
+            self.rows_out += count
+
+
+def component_lines(args):
+    """Compact C1-C4 measurements for the headline line (rank 0, one GPU)."""
+    import bench_components
+
+    small = argparse.Namespace(**vars(args))
+    small.steps, small.warmup = 5, 2
+    lines = {}
+    for name in ("rules", "encode", "puct", "network"):
+        try:
+            lines[name] = getattr(bench_components, f"bench_{name}")(small, peaks())
+        except Exception as exc:  # noqa: BLE001 - reported, not fatal
+            lines[name] = {"value": None, "unavailable": f"{type(exc).__name__}: {exc}"[:300]}
+    return lines
 
 
 def main():
@@ -264,9 +378,13 @@ def main():
     parser.add_argument("--gpus", type=int, default=1)
     parser.add_argument("--steps", type=int, default=10)
     parser.add_argument("--warmup", type=int, default=3)
-    parser.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    parser.add_argument("--e2e-steps", type=int, default=3)
-    parser.add_argument("--no-cpu-baseline", action="store_true")
+    parser.add_argument("--impl", choices=["ours", "reference", "nvrtc"], default="ours",
+                        help="reference: the reference's CPU self-play; nvrtc: the reference's NVRTC GPU path")
+    parser.add_argument("--preroll-plies", type=int, default=150,
+                        help="plies played at --preroll-sims before warm-up, so games are spread over all phases")
+    parser.add_argument("--preroll-sims", type=int, default=16)
+    parser.add_argument("--no-extras", action="store_true",
+                        help="skip the component lines, the CPU baseline and the NVRTC figure")
     parser.add_argument("--workload", choices=["selfplay", "network", "rules", "encode", "puct", "replay", "batched",
                                                    "selfplay_reference", "evaluation"],
                         default="selfplay",
@@ -289,9 +407,12 @@ def main():
     if args.impl == "reference":
         reference_arm(args)
         return
+    if args.impl == "nvrtc":
+        nvrtc_arm(args)
+        return
     if args.workload != "selfplay":
         import bench_components
-        getattr(bench_components, f"bench_{args.workload}")(args, peaks())
+        bench_components.emit(getattr(bench_components, f"bench_{args.workload}")(args, peaks()))
         return
 
     import torch
@@ -322,8 +443,15 @@ def main():
     def step():
         engine.step(1)
         if gather is not None:
-            gather.run(int(engine.counters[2].item()))
+            gather.run(engine.counters)
 
+    # Steady state: a short pre-roll at a few simulations per move lets games
+    # end and restart at different plies, so the timed plies see every phase
+    # of a game (openings, middle games, endings, restarts) as a long run does.
+    engine.set_simulations(max(1, min(args.preroll_sims, SIMULATIONS)))
+    for _ in range(args.preroll_plies):
+        step()
+    engine.set_simulations(SIMULATIONS)
     for _ in range(args.warmup):
         step()
     torch.cuda.synchronize(device)
@@ -347,6 +475,7 @@ def main():
     after = engine.stats()
     tower_ms, tower_launches = timer.read()
     engine.timer = None
+    clock = clocks.summary()
     local_counts = torch.tensor([after[k] - before[k] for k in ("moves", "evaluations", "games", "rows")],
                                 dtype=torch.float64, device=device)
     ms = torch.tensor([elapsed_ms, tower_ms], dtype=torch.float64, device=device)
@@ -361,39 +490,74 @@ def main():
     tflops = my_evals * TOWER_FLOPS_PER_EVAL / tower_s / 1e12 if tower_s > 0 else None
     peak_tf, hbm, peak_kind, _ = peaks()
 
-    e2e = None
-    if args.e2e_steps > 0:
-        e2e = e2e_arm(model, args.e2e_steps, 1, device)
-        e2e_moves, e2e_elapsed = float(e2e.pop("_moves")), e2e.pop("_elapsed")
-        if world > 1:
-            # Whole job: every rank's moves over the slowest rank's time.
-            t = torch.tensor([e2e_moves], dtype=torch.float64, device=device)
-            dist.all_reduce(t, op=dist.ReduceOp.SUM)
-            e2e_moves = t.item()
-            t = torch.tensor([e2e_elapsed], dtype=torch.float64, device=device)
-            dist.all_reduce(t, op=dist.ReduceOp.MAX)
-            e2e_elapsed = t.item()
-        e2e["value"] = e2e_moves * SIMULATIONS / e2e_elapsed
-        e2e["moves_per_s"] = e2e_moves / e2e_elapsed
-    cpu = None
-    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+    # e2e: the same number of plies, continuing the same games, driven from
+    # host memory through the engine's public API (HostPly).
+    host_ply = HostPly(engine)
+    for _ in range(min(args.warmup, 2)):
+        host_ply()
+        if gather is not None:
+            gather.run(engine.counters)
+    e2e_before = engine.stats()
+    rows_out_before = host_ply.rows_out
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize(device)
+    wall = time.perf_counter()
+    for _ in range(args.steps):
+        host_ply()
+        if gather is not None:
+            gather.run(engine.counters)
+    torch.cuda.synchronize(device)
+    wall = time.perf_counter() - wall
+    engine.check()
+    e2e_moves = engine.stats()["moves"] - e2e_before["moves"]
+    e2e_rows = host_ply.rows_out - rows_out_before
+    t = torch.tensor([float(e2e_moves), float(e2e_rows)], dtype=torch.float64, device=device)
+    w = torch.tensor([wall], dtype=torch.float64, device=device)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.SUM)
+        dist.all_reduce(w, op=dist.ReduceOp.MAX)
+    e2e_moves, e2e_rows = t.tolist()
+    wall = w.item()
+    e2e = {"value": e2e_moves * SIMULATIONS / wall, "unit": "simulations/s", "moves_per_s": e2e_moves / wall,
+           "h2d_bytes_per_step": host_ply.h2d,
+           "d2h_bytes_per_step": host_ply.d2h_fixed + int(round(host_ply.row_bytes * e2e_rows / world / args.steps)),
+           "steps": args.steps,
+           "api": "SelfPlayEngine driven from pinned host records: load_records (H2D) -> step (search, T=1 "
+                  "sampling for 10 plies then best, history, replay flush) -> records, last_action, last_policy, "
+                  "counters and the new replay rows (D2H), two host synchronisations per ply",
+           "replay_rows_per_step": e2e_rows / world / args.steps}
+
+    extras = {}
+    if rank == 0 and world == 1 and not args.no_extras:
+        net_error = None
         try:
-            cpu = cpu_baseline_sample(15.0)
+            import bench_components
+            from kingdom_ai.model import NativePolicyValueNet
+
+            net_error = bench_components.network_error(
+                model, NativePolicyValueNet(model, device), bench_components.positions(LANES, 4321, device))
         except Exception as exc:  # noqa: BLE001 - reported, not fatal
-            cpu = {"value": None, "unavailable": str(exc)}
-    clock = clocks.summary()
+            net_error = {"unavailable": str(exc)}
+        extras["network_error"] = net_error
+        extras["components"] = component_lines(args)
+        extras["nvrtc"] = _subprocess_json(["--impl", "nvrtc", "--steps", "2", "--warmup", "1"], timeout=600)
+        cpu = _subprocess_json(["--impl", "reference", "--steps", "3", "--warmup", "1"], timeout=600)
+        extras["cpu_baseline"] = cpu.get("cpu_baseline", cpu)
     if rank == 0:
         line = {
             "metric": METRIC, "value": sims / elapsed_s, "unit": "simulations/s", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms[0].item() / args.steps,
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
-            "data": "synthetic (self-play from the opening; random-init network)",
+            "data": "synthetic (continuous self-play at steady state; random-init network)",
             "moves_per_s": moves / elapsed_s, "games_finished": games, "replay_rows": rows,
             "network_evaluations_per_s": evals / elapsed_s,
             "config": {"workload": f"batched self-play, {LANES} games/GPU, {CHANNELS}ch x {BLOCKS}-block bf16 net, "
                                    f"{SIMULATIONS} PUCT sims/move, c_puct 1.5, Dirichlet 0.3/0.25, T=1 for 10 "
                                    "plies then best, 1M-row replay FIFO",
                        "lanes_per_gpu": LANES, "simulations": SIMULATIONS, "parallelism": f"games sharded x{world}",
+                       "steady_state": f"{args.preroll_plies} pre-roll plies at {args.preroll_sims} sims/move, "
+                                       f"then {args.warmup} warm-up plies at {SIMULATIONS}",
                        "l2": "working set (search trees 3.2 GB/GPU) far larger than L2"},
             "roofline": {"bound": "tensor", "kernel": "net_tower_cols_kernel",
                          "achieved": tflops, "peak": peak_tf, "unit": "TFLOP/s",
@@ -401,8 +565,11 @@ def main():
                          "peak_kind": f"{peak_kind} bf16 sustained",
                          "flops_per_eval": TOWER_FLOPS_PER_EVAL, "launches": tower_launches,
                          "avg_launch_ms": tower_ms / max(tower_launches, 1)},
-            "cpu_baseline": cpu,
+            "cpu_baseline": extras.get("cpu_baseline"),
+            "nvrtc": extras.get("nvrtc"),
             "e2e": e2e,
+            "network_error": extras.get("network_error"),
+            "components": extras.get("components"),
             "gpu_launches": int(args.steps * LAUNCHES_PER_PLY),
             "clocks": clock,
         }

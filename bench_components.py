@@ -59,6 +59,41 @@ def emit(line):
     print(json.dumps(line), flush=True)
 
 
+def host_cores():
+    import os
+    return len(os.sched_getaffinity(0))
+
+
+def _reference():
+    """The reference engine compiled from its sources (oracle/_ref), or None."""
+    try:
+        from oracle.oracle import Reference
+        return Reference()
+    except Exception:  # noqa: BLE001 - the caller reports the baseline as unavailable
+        return None
+
+
+def network_error(model, net, bits):
+    """Max |native bf16 - PyTorch fp32| on logits and values over `bits`
+    positions (TF32 off, so the reference forward is true fp32)."""
+    from kingdom_ai.gpu_puct import encode_packed
+
+    features, _ = encode_packed(bits)
+    tf32 = (torch.backends.cudnn.allow_tf32, torch.backends.cuda.matmul.allow_tf32)
+    torch.backends.cudnn.allow_tf32 = torch.backends.cuda.matmul.allow_tf32 = False
+    try:
+        with torch.no_grad():
+            ref_logits, ref_values = model.to(bits.device).float().eval()(features)
+    finally:
+        torch.backends.cudnn.allow_tf32, torch.backends.cuda.matmul.allow_tf32 = tf32
+    logits, values = net.forward_states(bits)
+    net.check()
+    return {"positions": int(bits.shape[0]),
+            "fp32_max_abs_logit": float((logits - ref_logits).abs().max()),
+            "fp32_max_abs_value": float((values - ref_values).abs().max()),
+            "fp32_max_logit_magnitude": float(ref_logits.abs().max())}
+
+
 def bench_network(args, peaks):
     from kingdom_ai.gpu_puct import encode_packed
     from kingdom_ai.model import (NativePolicyValueNet, calibrate_batchnorm, random_groupnorm_network,
@@ -81,20 +116,45 @@ def bench_network(args, peaks):
     flops = 2 * 81 * 9 * 10 * channels + 2 * blocks * 2 * 81 * 9 * channels * channels + 2 * 81 * (
         channels * 3 + 162 * 82 + 81 * hidden + hidden)
     tflops = n * flops / (ms / 1e3) / 1e12
+    error = network_error(model, net, bits)
+    model = model.to(device)
     with torch.no_grad():
-        t_ref = timed(lambda: model.to(device)(features), max(1, args.steps // 2), 1, flush)
+        t_ref = timed(lambda: model(features), max(1, args.steps // 2), 1, flush)
         with torch.autocast("cuda", dtype=torch.bfloat16):
             t_amp = timed(lambda: model(features), max(1, args.steps // 2), 1, flush)
+    cpu = None
+    try:
+        import time
+        cores = host_cores()
+        threads = torch.get_num_threads()
+        torch.set_num_threads(cores)
+        cpu_model, sample = model.cpu().float().eval(), features[:128].cpu()
+        with torch.no_grad():
+            cpu_model(sample[:8])
+            start, reps = time.perf_counter(), 0
+            while reps < 1 or time.perf_counter() - start < 3.0:
+                cpu_model(sample)
+                reps += 1
+        elapsed = time.perf_counter() - start
+        torch.set_num_threads(threads)
+        cpu = {"value": reps * len(sample) / elapsed, "unit": "positions/s", "cores": cores, "kind": "port",
+               "sample": f"{reps} fp32 PyTorch CPU forwards of {len(sample)} positions ({cores} threads), "
+                         f"{elapsed:.1f} s"}
+    except Exception as exc:  # noqa: BLE001 - reported, not fatal
+        cpu = {"value": None, "unavailable": str(exc)}
     kind = "GroupNorm (the reference's PolicyValueNet)" if group else "batch norm folded"
-    emit({"workload": f"network forward {channels}ch x {blocks} blocks, {kind}, batch {n}", "metric": "positions/s",
-          "value": n / (ms / 1e3), "unit": "positions/s", "ms_per_batch": ms, "dtype": "bf16",
-          "roofline": {"bound": "tensor", "achieved": tflops, "peak": peaks[3], "unit": "TFLOP/s",
-                       "frac": tflops / peaks[3], "peak_kind": f"{peaks[2]} bf16 burst (kernel timed alone)",
-                       "flops_per_position": flops},
-          "pytorch_fp32_ms": t_ref, "pytorch_bf16_autocast_ms": t_amp})
+    return {"workload": f"network forward {channels}ch x {blocks} blocks, {kind}, batch {n}", "metric": "positions/s",
+            "value": n / (ms / 1e3), "unit": "positions/s", "ms_per_batch": ms, "dtype": "bf16",
+            "roofline": {"bound": "tensor", "achieved": tflops, "peak": peaks[3], "unit": "TFLOP/s",
+                         "frac": tflops / peaks[3], "peak_kind": f"{peaks[2]} bf16 burst (kernel timed alone)",
+                         "flops_per_position": flops},
+            "error_vs_fp32": error, "pytorch_fp32_ms": t_ref, "pytorch_bf16_autocast_ms": t_amp,
+            "cpu_baseline": cpu}
 
 
 def bench_rules(args, peaks):
+    import time
+
     device = torch.device("cuda", 0)
     flush = Flusher(device)
     n = 4096
@@ -124,12 +184,25 @@ def bench_rules(args, peaks):
     play_ms = total / args.steps
     bytes_per_state = 64 + 4 + 64 + 1
     gbs = big * bytes_per_state / (play_ms / 1e3) / 1e9
-    emit({"workload": f"rules: 4096 uniform-random complete playouts; one transition of {big} packed states",
-          "metric": "playout moves/s", "value": plies / (ms / 1e3), "unit": "moves/s",
-          "games_per_s": n / (ms / 1e3), "playout_ms": ms, "mean_plies": plies / n,
-          "play_kernel": {"states": big, "ms": play_ms, "states_per_s": big / (play_ms / 1e3)},
-          "roofline": {"bound": "hbm", "kernel": "play_bits_kernel", "achieved": gbs, "peak": peaks[1],
-                       "unit": "GB/s", "frac": gbs / peaks[1], "bytes_per_state": bytes_per_state}})
+    ref, cpu = _reference(), None
+    if ref is not None:
+        cores = host_cores()
+        rates = {}
+        for fast, name in ((0, "legal_moves"), (1, "candidates")):
+            start = time.perf_counter()
+            _, ref_infos = ref.random_playouts(2024, n, fast=bool(fast), threads=cores)
+            rates[name] = int(ref_infos[:, 4].sum()) / (time.perf_counter() - start)
+        cpu = {"value": rates["legal_moves"], "unit": "moves/s", "cores": cores, "kind": "reference",
+               "candidates_moves_per_s": rates["candidates"],
+               "sample": f"the same {n} playouts through kingdom::State::play on {cores} threads, legal moves "
+                         "from State::legal_moves() (value) and from the MCTS::candidates rule"}
+    return {"workload": f"rules: 4096 uniform-random complete playouts; one transition of {big} packed states",
+            "metric": "playout moves/s", "value": plies / (ms / 1e3), "unit": "moves/s",
+            "games_per_s": n / (ms / 1e3), "playout_ms": ms, "mean_plies": plies / n,
+            "play_kernel": {"states": big, "ms": play_ms, "states_per_s": big / (play_ms / 1e3)},
+            "roofline": {"bound": "hbm", "kernel": "play_bits_kernel", "achieved": gbs, "peak": peaks[1],
+                         "unit": "GB/s", "frac": gbs / peaks[1], "bytes_per_state": bytes_per_state},
+            "cpu_baseline": cpu}
 
 
 def bench_encode(args, peaks):
@@ -149,31 +222,73 @@ def bench_encode(args, peaks):
     n = small
     gbs = n * bytes_per_pos / (out[n] / 1e3) / 1e9
     gbs_big = big * bytes_per_pos / (out[big] / 1e3) / 1e9
-    emit({"workload": f"encode {n} generated positions (and 2^20)", "metric": "positions/s",
-          "value": n / (out[n] / 1e3), "unit": "positions/s", "ms": out[n], "ms_2pow20": out[big],
-          "roofline": {"bound": "hbm", "kernel": "encode_bits_kernel", "achieved": gbs, "peak": peaks[1],
-                       "unit": "GB/s", "frac": gbs / peaks[1], "bytes_per_position": bytes_per_pos,
-                       "achieved_2pow20": gbs_big, "frac_2pow20": gbs_big / peaks[1]}})
+    ref, cpu = _reference(), None
+    if ref is not None:
+        cores = host_cores()
+        seconds, _, _ = ref.encode_timed(11, n, threads=cores)
+        cpu = {"value": n / seconds, "unit": "positions/s", "cores": cores, "kind": "reference",
+               "sample": f"kingdom::encode_puct_position over the same {n} generated positions on {cores} threads "
+                         "(generation excluded)"}
+    return {"workload": f"encode {n} generated positions (and 2^20)", "metric": "positions/s",
+            "value": n / (out[n] / 1e3), "unit": "positions/s", "ms": out[n], "ms_2pow20": out[big],
+            "roofline": {"bound": "hbm", "kernel": "encode_bits_kernel", "achieved": gbs, "peak": peaks[1],
+                         "unit": "GB/s", "frac": gbs / peaks[1], "bytes_per_position": bytes_per_pos,
+                         "achieved_2pow20": gbs_big, "frac_2pow20": gbs_big / peaks[1]},
+            "cpu_baseline": cpu}
+
+
+def puct_bytes_per_simulation(mean_depth: float) -> float:
+    """Algorithmic HBM bytes of one simulation: every level of the descent
+    reads the node's 82 edges (N i32, W f64, P f64 = 20 B each) and writes a
+    12-byte backup; the leaf's expansion writes one 20-byte row of 82 edges;
+    the new child state and its scalars take 96 B."""
+    return mean_depth * (82 * 20 + 12) + 82 * 20 + 96
 
 
 def bench_puct(args, peaks):
-    from kingdom_ai.gpu_puct import search_hash
+    import time
+
+    from kingdom_ai.gpu_puct import SearchWorkspace, search_hash
 
     device = torch.device("cuda", 0)
     flush = Flusher(device)
     n, sims = args.trees, args.sims
     bits = positions(n, 4242, device)
+    ws = SearchWorkspace(n, sims + 1, device)
     holder = {}
 
     def run():
-        holder["r"] = search_hash(bits, sims)
+        holder["r"] = search_hash(bits, sims, workspace=ws)
 
     ms = timed(run, max(1, args.steps // 3), 1, flush)
     r = holder["r"]
     assert int(r.simulations.sum().item()) == n * sims
-    emit({"workload": f"PUCT {n} trees x {sims} simulations, injected evaluator, c_puct 1.5", "metric": "simulations/s",
-          "value": n * sims / (ms / 1e3), "unit": "simulations/s", "ms_per_search": ms,
-          "nodes_mean": float(r.nodes.float().mean().item())})
+    # Mean selection depth: each simulation adds one visit to every non-root
+    # node on its path, so the visits of all non-root nodes sum to the total depth.
+    live = torch.arange(sims + 1, device=device)[None, :] < r.nodes[:, None]
+    depth_total = (ws.node_visits * live)[:, 1:].sum().item()
+    mean_depth = depth_total / (n * sims)
+    bps = puct_bytes_per_simulation(mean_depth)
+    gbs = n * sims * bps / (ms / 1e3) / 1e9
+    ref, cpu = _reference(), None
+    if ref is not None:
+        cores = host_cores()
+        m = min(n, 8 * cores)
+        start = time.perf_counter()
+        visits, best = ref.puct_positions(4242, m, sims, threads=cores)
+        elapsed = time.perf_counter() - start
+        assert (visits == r.visits[:m].cpu().numpy()).all(), "reference visits differ from the device search"
+        cpu = {"value": m * sims / elapsed, "unit": "simulations/s", "cores": cores, "kind": "reference",
+               "sample": f"kingdom::PUCT::search over the first {m} of the same roots ({sims} simulations, injected "
+                         f"evaluator) on {cores} threads, {elapsed:.2f} s; visit counts equal the device's"}
+    return {"workload": f"PUCT {n} trees x {sims} simulations, injected evaluator, c_puct 1.5",
+            "metric": "simulations/s", "value": n * sims / (ms / 1e3), "unit": "simulations/s",
+            "ms_per_search": ms, "nodes_mean": float(r.nodes.float().mean().item()),
+            "roofline": {"bound": "hbm", "kernel": "puct_search_hash_kernel", "achieved": gbs, "peak": peaks[1],
+                         "unit": "GB/s", "frac": gbs / peaks[1], "mean_depth": mean_depth,
+                         "bytes_per_simulation": bps,
+                         "bytes_rule": "d*(82*20+12) + 82*20 + 96 with d the measured mean selection depth"},
+            "cpu_baseline": cpu}
 
 
 def bench_replay(args, peaks):
@@ -218,11 +333,11 @@ def bench_replay(args, peaks):
                "sample": f"{reps} passes over {m} rows (numpy restatement of replay.py:35-74), {elapsed:.1f} s"}
     except Exception as exc:  # noqa: BLE001 - reported, not fatal
         cpu = {"value": None, "unavailable": str(exc)}
-    emit({"workload": f"replay row checks, {n} generated positions with masked-uniform policies",
+    return {"workload": f"replay row checks, {n} generated positions with masked-uniform policies",
           "metric": "rows/s", "value": n / (ms / 1e3), "unit": "rows/s", "ms": ms, "dtype": "f32",
           "roofline": {"bound": "hbm", "kernel": "replay_validate_kernel", "achieved": gbs, "peak": peaks[1],
                        "unit": "GB/s", "frac": gbs / peaks[1], "bytes_per_row": row_bytes},
-          "cpu_baseline": cpu})
+          "cpu_baseline": cpu}
 
 
 def bench_batched(args, peaks):
@@ -273,7 +388,7 @@ def bench_batched(args, peaks):
                          f"reference kingdom::BatchedPUCT, {elapsed:.1f} s"}
     except Exception as exc:  # noqa: BLE001 - reported, not fatal
         cpu = {"value": None, "unavailable": str(exc)}
-    emit({"workload": f"batched evaluation search: {T} games x {S} simulations, leaf batch {L}, c_puct 1.5, "
+    return {"workload": f"batched evaluation search: {T} games x {S} simulations, leaf batch {L}, c_puct 1.5, "
                       "generated positions, new trees every search",
           "metric": "simulations/s", "unit": "simulations/s",
           "value": T * S / (ms_hash / 1e3), "ms_per_search": ms_hash, "evaluator": "injected (one launch)",
@@ -281,7 +396,7 @@ def bench_batched(args, peaks):
           "network": {"value": T * S / (ms_net / 1e3), "ms_per_search": ms_net,
                       "evaluator": "native 64ch x 6-block bf16 network, one batch per wave",
                       "waves_per_search": batches},
-          "cpu_baseline": cpu})
+          "cpu_baseline": cpu}
 
 
 def bench_selfplay_reference(args, peaks):
@@ -313,11 +428,11 @@ def bench_selfplay_reference(args, peaks):
     after = engine.stats()
     ms = start.elapsed_time(stop)
     moves = after["moves"] - before["moves"]
-    emit({"workload": f"self-play, the reference's 32ch x 2-block GroupNorm network, {args.lanes} games, "
+    return {"workload": f"self-play, the reference's 32ch x 2-block GroupNorm network, {args.lanes} games, "
                       "128 sims/move, c_puct 1.5, Dirichlet 0.3/0.25",
           "metric": "simulations/s", "unit": "simulations/s", "value": moves * 128 / (ms / 1e3),
           "moves_per_s": moves / (ms / 1e3), "ms_per_step": ms / args.steps, "steps": args.steps,
-          "warmup": args.warmup, "games_finished": after["games"] - before["games"]})
+          "warmup": args.warmup, "games_finished": after["games"] - before["games"]}
 
 
 def bench_evaluation(args, peaks):
@@ -342,9 +457,9 @@ def bench_evaluation(args, peaks):
     stop.synchronize()
     wall = time.perf_counter() - wall
     seconds = start.elapsed_time(stop) / 1e3
-    emit({"workload": f"evaluation match: {args.games} games between two 64ch x 6-block networks, 128 sims/move, "
+    return {"workload": f"evaluation match: {args.games} games between two 64ch x 6-block networks, 128 sims/move, "
                       "leaf batch 8, 6 sampled opening moves, subtree reuse",
           "metric": "games/s", "unit": "games/s", "value": args.games / seconds,
           "moves_per_s": result.total_plies / seconds, "simulations_per_s": result.total_plies * 128 / seconds,
           "seconds": seconds, "wall_seconds": wall, "total_plies": result.total_plies,
-          "candidate_win_rate": result.win_rate, "endings": result.endings})
+          "candidate_win_rate": result.win_rate, "endings": result.endings}

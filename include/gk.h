@@ -118,6 +118,8 @@ typedef struct {
     uint32_t* errors;      /* [B] GK_ERR_* per tree */
     int32_t* leaf;         /* [B] node of the leaf to evaluate (0: the root) */
     uint32_t* root_allow;  /* [B,3] root candidates: bit a%32 of word a/32 (all after gk_puct_begin) */
+    int32_t* node_visits;  /* [B,capacity] visits of each node (node 0 the root; nodes >= the tree's node
+                              count hold stale values) */
 } gk_puct_buffers_t;
 
 /* Search outputs (GpuSearchResult, gpu_puct.py:66-76); any pointer may be
@@ -189,7 +191,9 @@ GK_API int gk_puct_finish(void* ws, int64_t batch, int capacity, const gk_puct_r
  * begin, then one kernel in which each tree's warp runs the root evaluation
  * and `simulations` x (select, evaluate, expand/backup), then finish. Results
  * equal those of the separate gk_puct_* steps. The workspace must be sized
- * for capacity = simulations + 1. Equivalent of PUCT::search
+ * for capacity = simulations + 1. With options->dirichlet_epsilon != 0 the
+ * root mixes in the workspace's noise rows, which gk_puct_noise must have
+ * drawn (or the caller zeroed) first. Equivalent of PUCT::search
  * (mcts/src/PUCT.cpp:177-268) per tree. */
 GK_API int gk_puct_search_hash(void* ws, int64_t batch, int simulations, const uint32_t* root_bits,
                         const gk_puct_options* options, const gk_puct_results_t* results, void* stream);
@@ -207,12 +211,14 @@ GK_API int gk_puct_search_hash(void* ws, int64_t batch, int simulations, const u
  * was given), or a service whose device memory is fixed at start-up. The
  * trees live in a file-scope device array of GK_NOALLOC_SCRATCH_BYTES; a
  * request whose gk_puct_workspace_bytes(batch, simulations + 1) exceeds it
- * returns GK_ENOSPC and launches nothing. The first call on a device
- * resolves the array's address with that device current (set-up): make it
- * before any stream capture. Each call clears the root-noise rows to zero
- * (this search draws no noise). All calls on a device share the array, so
- * calls that overlap in time (other streams, other host threads) race: the
- * caller serialises them. Calls no allocator. */
+ * returns GK_ENOSPC and launches nothing. The first call in each CUDA context
+ * on a device resolves the array's address with that device current
+ * (set-up): make it before any stream capture. The search draws no root
+ * noise: options->dirichlet_epsilon must be 0 (else GK_EINVAL). Each call
+ * writes every per-tree field it reads, so the previous call's contents do
+ * not matter. All calls on a device share the array, so calls that overlap in
+ * time (other streams, other host threads) race: the caller serialises them.
+ * Calls no allocator. */
 GK_API int gk_puct_search_hash_noalloc(int64_t batch, int simulations, const uint32_t* root_bits,
                                        const gk_puct_options* options, const gk_puct_results_t* results,
                                        void* stream);
@@ -354,10 +360,12 @@ typedef struct {
  * finished games, replay rows written (monotone; ring index = rows % cap),
  * errors, black wins, white wins, capture endings, network evaluations. */
 typedef struct {
-    uint32_t* states;   /* [lanes,16] packed current positions */
-    int32_t* lane_ply;  /* [lanes] */
-    uint64_t* game_id;  /* [lanes] */
-    uint64_t* counters; /* [8] */
+    uint32_t* states;      /* [lanes,16] packed current positions (writable between plies) */
+    int32_t* lane_ply;     /* [lanes] plies of the current game; -1 once parked */
+    uint64_t* game_id;     /* [lanes] */
+    uint64_t* counters;    /* [8] */
+    int32_t* last_action;  /* [lanes] action played in the last ply, -1 if none */
+    float* last_policy;    /* [lanes,82] visit shares of the last ply's search (the policy target) */
 } gk_selfplay_buffers_t;
 
 /* Bytes of self-play workspace for `lanes` concurrent games (positions,

@@ -276,6 +276,9 @@ class Reference:
         _bind(L, "gkr_encode_positions", [_u64, _u64, _i64, _int, _f32p, _u8p])
         _bind(L, "gkr_puct_search", [vp, _int, ctypes.c_double, _i32p, _f64p, _i32p, _f64p], _int)
         _bind(L, "gkr_puct_positions", [_u64, _u64, _i64, _int, ctypes.c_double, _int, _i32p, _i32p], _int)
+        _bind(L, "gkr_states_generate", [_u64, _u64, _i64, _int], vp)
+        _bind(L, "gkr_states_free", [vp])
+        _bind(L, "gkr_states_encode", [vp, _int, _f32p, _u8p])
         _bind_batched(L, "gkr")
 
     def batched(self, simulations, c_puct=1.5, leaf_batch=8, reuse=True, evaluator="hash"):
@@ -298,6 +301,23 @@ class Reference:
         masks = np.zeros((n, ACTIONS), dtype=np.uint8)
         self.lib.gkr_encode_positions(seed, first, n, threads, features, masks)
         return features.reshape(n, 10, 9, 9), masks.astype(bool)
+
+    def encode_timed(self, seed, n, threads=1, repeats=1):
+        """Seconds per kingdom::encode_puct_position pass over n generated
+        positions on `threads` workers (generation excluded), and the outputs."""
+        import time
+        h = self.lib.gkr_states_generate(seed, 0, n, threads)
+        features = np.zeros((n, FEATURES), dtype=np.float32)
+        masks = np.zeros((n, ACTIONS), dtype=np.uint8)
+        try:
+            self.lib.gkr_states_encode(h, threads, features, masks)  # warm
+            start = time.perf_counter()
+            for _ in range(repeats):
+                self.lib.gkr_states_encode(h, threads, features, masks)
+            seconds = (time.perf_counter() - start) / repeats
+        finally:
+            self.lib.gkr_states_free(h)
+        return seconds, features.reshape(n, 10, 9, 9), masks.astype(bool)
 
     def puct_positions(self, seed, n, simulations, c_puct=1.5, first=0, threads=1):
         visits = np.zeros((n, ACTIONS), dtype=np.int32)

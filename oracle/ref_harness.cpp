@@ -272,6 +272,27 @@ void gkr_encode_positions(uint64_t seed, uint64_t first, int64_t n, int threads,
     });
 }
 
+// Generated positions held as kingdom::State, so the encoder can be timed
+// without the generator.
+void* gkr_states_generate(uint64_t seed, uint64_t first, int64_t n, int threads) {
+    auto* v = new std::vector<State>(static_cast<std::size_t>(n));
+    parallel_for(n, threads, [&](int64_t i) { (*v)[static_cast<std::size_t>(i)] = gen_position(seed, first + i); });
+    return v;
+}
+
+void gkr_states_free(void* h) { delete static_cast<std::vector<State>*>(h); }
+
+// kingdom::encode_puct_position over every held state on `threads` workers.
+void gkr_states_encode(const void* h, int threads, float* features, uint8_t* masks) {
+    const auto& v = *static_cast<const std::vector<State>*>(h);
+    parallel_for(static_cast<int64_t>(v.size()), threads, [&](int64_t i) {
+        const auto e = kingdom::encode_puct_position(v[static_cast<std::size_t>(i)]);
+        std::memcpy(features + i * GK_FEATURES, e.features.data(), sizeof(float) * GK_FEATURES);
+        for (int a = 0; a < GK_ACTIONS; ++a)
+            masks[i * GK_ACTIONS + a] = e.legal_mask[static_cast<std::size_t>(a)] ? 1 : 0;
+    });
+}
+
 // PUCT with the injected hash evaluator and no root noise.
 // stats = {best_action, simulations, nodes, network_evaluations}; values = {root, best}.
 int gkr_puct_search(const void* h, int simulations, double c_puct, int32_t* visits, double* priors,

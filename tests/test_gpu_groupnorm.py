@@ -7,10 +7,13 @@ max |value - fp32| <= 5e-2. The reference checkpoints come from
 tests/golden/groupnorm.npz (the reference module's own weights and outputs).
 """
 
+import json
+import os
+
 import pytest
 import torch
 
-from test_gpu_net import native_or_skip, positions, selftest  # noqa: F401
+from test_gpu_net import native_or_fail, positions, selftest  # noqa: F401
 from test_model_host import load_reference
 
 pytestmark = pytest.mark.gpu
@@ -27,8 +30,16 @@ def check(model, features, bits=None):
     torch.cuda.synchronize()
     net.check()
     scale = ref_logits.abs().max().item()
-    assert (logits.cpu() - ref_logits).abs().max().item() <= RTOL * scale + ATOL
-    assert (values.cpu() - ref_values).abs().max().item() <= VTOL
+    err_logit = (logits.cpu() - ref_logits).abs().max().item()
+    err_value = (values.cpu() - ref_values).abs().max().item()
+    stats = dict(norm="group", channels=model.channels, blocks=model.residual_blocks, n=features.shape[0],
+                 logit_scale=scale, fp32_max_abs_logit=err_logit, fp32_max_abs_value=err_value)
+    print(json.dumps(stats))
+    if os.environ.get("GK_NET_STATS"):
+        with open(os.environ["GK_NET_STATS"], "a") as f:
+            f.write(json.dumps(stats) + "\n")
+    assert err_logit <= RTOL * scale + ATOL
+    assert err_value <= VTOL
     if bits is not None:
         l2, v2 = net.forward_states(bits)
         assert torch.equal(l2, logits) and torch.equal(v2, values)
@@ -36,7 +47,7 @@ def check(model, features, bits=None):
 
 
 def test_reference_checkpoints(selftest, golden):  # noqa: F811
-    native_or_skip(selftest)
+    native_or_fail(selftest)
     for tag in ("c32", "c64"):
         g, net = load_reference(golden, tag)
         features = torch.from_numpy(g["features"])
@@ -54,7 +65,7 @@ def test_reference_checkpoints(selftest, golden):  # noqa: F811
 def test_random_groupnorm_networks(selftest, channels, blocks, n):  # noqa: F811
     from kingdom_ai.gpu_puct import encode_packed
     from kingdom_ai.model import random_groupnorm_network
-    native_or_skip(selftest)
+    native_or_fail(selftest)
     bits = positions(n, channels + blocks)
     features, _ = encode_packed(bits)
     check(random_groupnorm_network(channels, blocks, 7), features, bits)
@@ -63,7 +74,7 @@ def test_random_groupnorm_networks(selftest, channels, blocks, n):  # noqa: F811
 def test_groupnorm_network_in_both_searches(selftest, oracle):  # noqa: F811
     from kingdom_ai import GpuBatchedPUCT, GpuPUCT, GpuPUCTOptions, PUCTOptions
     from kingdom_ai.model import random_groupnorm_network
-    native_or_skip(selftest)
+    native_or_fail(selftest)
     model = random_groupnorm_network(32, 2, 3)
     bits = positions(96, 11)
     r = GpuPUCT(model, GpuPUCTOptions(simulations=16, seed=1)).search_packed(bits)
@@ -81,7 +92,7 @@ def test_selfplay_with_the_reference_network(selftest):  # noqa: F811
     from kingdom_ai import GpuPUCTOptions, validate_rows
     from kingdom_ai.model import random_groupnorm_network
     from kingdom_ai.selfplay import SelfPlayEngine
-    native_or_skip(selftest)
+    native_or_fail(selftest)
     engine = SelfPlayEngine(random_groupnorm_network(32, 2, 5), 64, GpuPUCTOptions(simulations=8, seed=2),
                             replay_capacity=1 << 13)
     engine.step(70)

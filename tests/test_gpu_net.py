@@ -81,10 +81,21 @@ def test_tensor_core_selftest(selftest):
     torch.testing.assert_close(d, expected, rtol=1e-5, atol=1e-4)
 
 
-def native_or_skip(selftest):
+def native_or_fail(selftest):
+    """The network kernels run on the tensor cores: a broken tcgen05 path
+    fails every network test rather than skipping it."""
     d, expected, status = selftest
-    if status != 0 or not torch.allclose(d, expected, rtol=1e-5, atol=1e-4):
-        pytest.skip("tensor-core self-test failed; the network kernels are not run")
+    assert status == 0, f"tensor-core self-test reported status {status:#x}"
+    torch.testing.assert_close(d, expected, rtol=1e-5, atol=1e-4)
+
+
+@pytest.fixture(autouse=True)
+def true_fp32():
+    """The fp32 reference forward runs in fp32: cuDNN's TF32 convolutions off."""
+    saved = (torch.backends.cudnn.allow_tf32, torch.backends.cuda.matmul.allow_tf32)
+    torch.backends.cudnn.allow_tf32 = torch.backends.cuda.matmul.allow_tf32 = False
+    yield
+    torch.backends.cudnn.allow_tf32, torch.backends.cuda.matmul.allow_tf32 = saved
 
 
 def positions(n, seed):
@@ -99,7 +110,7 @@ def compare(channels, blocks, n, seed, selftest, calibrate=False, emu_rtol=EMU_R
     from kingdom_ai.gpu_puct import encode_packed
     from kingdom_ai.model import NativePolicyValueNet, calibrate_batchnorm, random_network
 
-    native_or_skip(selftest)
+    native_or_fail(selftest)
     model = random_network(channels, blocks, seed)
     bits = positions(n, seed)
     features, _ = encode_packed(bits)
@@ -199,7 +210,7 @@ def test_integer_network_is_exact(selftest, channels, blocks, n):
     from kingdom_ai.gpu_puct import encode_packed
     from kingdom_ai.model import NativePolicyValueNet
 
-    native_or_skip(selftest)
+    native_or_fail(selftest)
     model = integer_network(channels, blocks, 13).cuda()
     bits = positions(n, 77)
     features, _ = encode_packed(bits)
@@ -223,7 +234,7 @@ def test_native_network_in_search(selftest, oracle):
     import kingdom_ai
     from kingdom_ai.model import random_network
 
-    native_or_skip(selftest)
+    native_or_fail(selftest)
     from test_gpu_puct import assert_result
 
     model = random_network(64, 2, 3)

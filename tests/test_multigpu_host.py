@@ -4,7 +4,9 @@ Games shard with no data-path exchange; the collectives are the replay-row
 gather into rank 0's FIFO and the counter sum (kingdom_ai/distributed.py).
 Two gloo ranks drive them here with rings of known rows: uneven per-rank
 counts (padding), ring wrap-around, a rank that outran its ring (only the
-newest rows survive), a rank with nothing new, and a FIFO that wraps.
+newest rows survive), a rank with nothing new, and a FIFO that wraps; and
+again with a slab narrower than a round's new rows, whose excess waits for
+the next gather.
 """
 
 import datetime
@@ -38,7 +40,7 @@ def _write(ring, rank, first, last):
         ring.to_play[j] = (i + rank) % 2
 
 
-def _worker(rank, world, port, out):
+def _worker(rank, world, port, out, width):
     sys.path[:0] = [str(ROOT), str(ROOT / "alpha-yoo-for-great-kingdom_b200")]
     import torch.distributed as dist
 
@@ -50,12 +52,14 @@ def _worker(rank, world, port, out):
     try:
         ring = ReplayRing(RING, "cpu")
         fifo = ReplayRing(FIFO, "cpu") if rank == 0 else None
-        gather = ReplayGather(ring, fifo)
+        gather = ReplayGather(ring, fifo, width=width)
         written, appended = 0, []
         for counts in ROUNDS:
             _write(ring, rank, written, counts[rank])
             written = counts[rank]
-            appended.append(gather.run(written))
+            # The count goes in as a tensor, as the engine's device counters do.
+            got = gather.run(torch.tensor(written))
+            appended.append(None if got is None else int(got))
         totals = total_counters(torch.arange(8, dtype=torch.int64) + 10 * rank)
         if rank == 0:
             torch.save({"appended": appended, "totals": totals, "fifo_rows": gather.fifo_rows,
@@ -66,37 +70,46 @@ def _worker(rank, world, port, out):
         dist.destroy_process_group()
 
 
-def _expected_rows():
-    """(rank, row index) in FIFO order: per round, rank 0's new rows then rank 1's."""
-    rows, sent = [], [0, 0]
+def _expected_rounds(width):
+    """Per round, the (rank, row index) pairs appended: rank 0's rows, then
+    rank 1's, each rank sending its oldest rows not yet sent, at most `width`,
+    after skipping rows its ring overwrote."""
+    rounds, sent = [], [0, 0]
     for counts in ROUNDS:
+        rows = []
         for rank in (0, 1):
-            first = max(sent[rank], counts[rank] - RING)  # overwritten rows are skipped
-            rows += [(rank, i) for i in range(first, counts[rank])]
-            sent[rank] = counts[rank]
-    return rows
+            first = max(sent[rank], counts[rank] - RING)
+            last = min(counts[rank], first + width)
+            rows += [(rank, i) for i in range(first, last)]
+            sent[rank] = last
+        rounds.append(rows)
+    return rounds
 
 
-@pytest.fixture(scope="module")
-def gathered(tmp_path_factory):
+def _run(tmp_path_factory, width):
     with socket.socket() as s:
         s.bind(("127.0.0.1", 0))
         port = s.getsockname()[1]
     out = tmp_path_factory.mktemp("gather") / "rank0.pt"
-    mp.spawn(_worker, args=(2, port, str(out)), nprocs=2, join=True)
+    mp.spawn(_worker, args=(2, port, str(out), width), nprocs=2, join=True)
     return torch.load(out)
 
 
-def test_rows_arrive_in_rank_order_with_overwritten_rows_skipped(gathered):
-    rows = _expected_rows()
-    per_round = []
-    sent = [0, 0]
-    for counts in ROUNDS:
-        n = sum(counts[r] - max(sent[r], counts[r] - RING) for r in (0, 1))
-        per_round.append(n)
-        sent = list(counts)
-    assert gathered["appended"] == per_round
-    assert gathered["fifo_rows"] == len(rows) == sum(per_round)
+@pytest.fixture(scope="module")
+def gathered(tmp_path_factory):
+    return _run(tmp_path_factory, RING)
+
+
+@pytest.fixture(scope="module")
+def gathered_narrow(tmp_path_factory):
+    return _run(tmp_path_factory, 3)
+
+
+def _check(gathered, width):
+    rounds = _expected_rounds(width)
+    rows = [r for rnd in rounds for r in rnd]
+    assert gathered["appended"] == [len(rnd) for rnd in rounds]
+    assert gathered["fifo_rows"] == len(rows)
     # The FIFO wrapped: slot k holds the newest row whose position is k mod FIFO.
     for pos, (rank, i) in enumerate(rows):
         if pos + FIFO < len(rows):
@@ -108,6 +121,14 @@ def test_rows_arrive_in_rank_order_with_overwritten_rows_skipped(gathered):
         assert torch.allclose(gathered["policy"][k], torch.full((82,), v / 7.0))
         assert gathered["value"][k].item() == (1.0 if (i + rank) % 2 == 0 else -1.0)
         assert gathered["to_play"][k].item() == (i + rank) % 2
+
+
+def test_rows_arrive_in_rank_order_with_overwritten_rows_skipped(gathered):
+    _check(gathered, RING)
+
+
+def test_a_narrow_slab_defers_rows_to_the_next_gather(gathered_narrow):
+    _check(gathered_narrow, 3)
 
 
 def test_counters_sum_over_ranks(gathered):

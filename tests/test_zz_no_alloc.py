@@ -45,15 +45,13 @@ def _options(c_puct=1.5, epsilon=0.0, fpu=None):
     return native.PuctOptions(float(c_puct), float(epsilon), 0 if fpu is None else 1, float(fpu or 0.0))
 
 
-def _with_workspace(roots, sims, opts, zero_noise=False):
+def _with_workspace(roots, sims, opts):
     """The existing entry point on a fresh caller workspace."""
     from kingdom_ai import _native as native
     from kingdom_ai.gpu_puct import SearchWorkspace, _allocate_results
 
     n = roots.shape[0]
     ws = SearchWorkspace(n, sims + 1, roots.device)
-    if zero_noise:
-        ws.noise.zero_()
     out = _allocate_results(n, roots.device)
     native.call("gk_puct_search_hash", ws.pointer, n, sims, native.ptr(roots), opts, out.struct,
                 native.stream_of(roots.device))
@@ -90,17 +88,16 @@ def test_two_calls_in_a_row_match_the_workspace_entry_point():
     assert int(first.status.item()) == 0 and int(second.status.item()) == 0
 
 
-def test_noise_rows_start_at_zero_on_a_dirty_scratch():
-    """20 trees of 400 simulations fill the array; 256 trees of 28 then find
-    their noise rows (bytes 15.3-15.4 MB) where the first search kept child
-    indices. With root noise weighted in, the result must equal the workspace
-    entry point on zeroed noise rows."""
+def test_a_dirty_scratch_gives_the_same_results():
+    """20 trees of 400 simulations fill the array; 256 trees of 28 then run
+    over bytes the first search left behind and must still equal the
+    workspace entry point."""
     assert _noalloc(_roots(20, 303), 400, _options())[0] == 0
     roots = _roots(256, 304)
-    opts = _options(epsilon=0.25)
+    opts = _options(c_puct=1.25)
     rc, got = _noalloc(roots, 28, opts)
     assert rc == 0
-    _assert_same(got, _with_workspace(roots, 28, opts, zero_noise=True))
+    _assert_same(got, _with_workspace(roots, 28, opts))
 
 
 def test_largest_request_runs_and_a_larger_one_is_refused():
@@ -129,3 +126,8 @@ def test_invalid_arguments_are_rejected():
     assert fn(4, 0, native.ptr(roots), _options(), out.struct, stream) == GK_EINVAL
     assert fn(4, 8, None, _options(), out.struct, stream) == GK_EINVAL
     assert fn(4, 8, native.ptr(roots), None, out.struct, stream) == GK_EINVAL
+    # This search draws no root noise, so a noise weight is refused.
+    assert fn(4, 8, native.ptr(roots), _options(epsilon=0.25), out.struct, stream) == GK_EINVAL
+    # Sizes whose byte counts would overflow are refused before any arithmetic.
+    assert fn(1 << 62, 8, native.ptr(roots), _options(), out.struct, stream) == GK_ENOSPC
+    assert fn(4, 2**31 - 1, native.ptr(roots), _options(), out.struct, stream) == GK_ENOSPC
