@@ -3,8 +3,10 @@
 
 Tolerances against the fp32 PyTorch module (bf16 operands, fp32 accumulation
 and statistics): max |logit - fp32| <= 2e-2 * max |logit| + 5e-3 and
-max |value - fp32| <= 5e-2. The reference checkpoints come from
-tests/golden/groupnorm.npz (the reference module's own weights and outputs).
+max |value - fp32| <= 4e-2, about twice the largest errors measured on a
+B200 (logits 0.044 at max |logit| 3.63, values 0.021, 128 x 2 on 517
+positions). The reference checkpoints come from tests/golden/groupnorm.npz
+(the reference module's own weights and outputs).
 """
 
 import json
@@ -18,7 +20,7 @@ from test_model_host import load_reference
 
 pytestmark = pytest.mark.gpu
 
-RTOL, ATOL, VTOL = 2e-2, 5e-3, 5e-2
+RTOL, ATOL, VTOL = 2e-2, 5e-3, 4e-2
 
 
 def check(model, features, bits=None):

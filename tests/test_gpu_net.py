@@ -1,16 +1,25 @@
 """Native tcgen05 network against PyTorch models of the same layout.
 
 Two references:
-  * the fp32 PyTorch model - the accuracy statement for bf16 arithmetic:
-    max |logit - logit_fp32| <= rtol * max |logit_fp32| + 5e-3 and
-    max |value - value_fp32| <= vtol, with (rtol, vtol) = (1e-2, 5e-2) for one
-    block, (2e-2, 0.1) for 6 x 64 and (4e-2, 0.15) for 10 x 128 (Kaiming
-    initialisation, batch norms calibrated on generated positions; rounding
-    differences compound with depth);
+  * the fp32 PyTorch model (TF32 off) - the accuracy statement for bf16
+    arithmetic: max |logit - logit_fp32| <= rtol * max |logit_fp32| + 5e-3 and
+    max |value - value_fp32| <= vtol (Kaiming initialisation, batch norms
+    calibrated on generated positions; rounding differences compound with
+    depth);
   * a PyTorch model that rounds to bf16 exactly where the kernels do (inputs,
     folded weights, every stored activation). It differs from the kernels
     only by fp32 summation order; with integer-valued networks, whose
     arithmetic is exact, the two must agree to fp32 round-off in the heads.
+
+Each tolerance is about twice the error measured on a B200 (max over the
+batch, TF32 off in the reference):
+
+  network, positions                 |logit - fp32| (max |logit|)  |value - fp32|
+  1 block x 64, 4096                 0.0196 (3.16)                 0.0023
+  1 block x 64, 5                    0.0018 (0.17)                 0.0153
+  6 x 64 calibrated, 4096            0.0891 (7.16)                 0.0432
+  6 x 64 uncalibrated, 2048          0.297 (17.3)                  0 (tanh saturated)
+  10 x 128 calibrated, 8192          0.129 (5.03)                  0.0713
 """
 
 import json
@@ -24,9 +33,9 @@ pytestmark = pytest.mark.gpu
 
 LOGIT_RTOL = 1e-2   # vs fp32, relative to the largest |logit|
 LOGIT_ATOL = 5e-3   # vs fp32, absolute floor for networks with tiny logits
-VALUE_ATOL = 5e-2   # vs fp32
+VALUE_ATOL = 3e-2   # vs fp32 (1 block: measured <= 0.0153)
 EMU_RTOL = 2e-3     # vs the bf16-rounding emulation, relative to the largest |logit|
-EMU_VALUE_ATOL = 5e-3
+EMU_VALUE_ATOL = 1e-3  # (1 block: measured <= 3.7e-4)
 
 
 def bf16_emulation(model, features):
@@ -156,7 +165,7 @@ def test_many_groups_per_cta(selftest):
 
 def test_selfplay_network_full_batch(selftest):
     """6 blocks x 64 channels, 4096 leaves (the self-play evaluation batch)."""
-    compare(64, 6, 4096, 5, selftest, calibrate=True, emu_rtol=1e-2, rtol=2e-2, emu_vtol=0.05, vtol=0.1)
+    compare(64, 6, 4096, 5, selftest, calibrate=True, emu_rtol=1e-2, rtol=2e-2, emu_vtol=0.05, vtol=0.09)
 
 
 def test_large_network(selftest):
@@ -166,7 +175,7 @@ def test_large_network(selftest):
 
 def test_uncalibrated_deep_network_stays_within_bf16_drift(selftest):
     """Arbitrary BN statistics blow logits up to ~30; the error stays a fraction of that."""
-    compare(64, 6, 2048, 6, selftest, emu_rtol=2e-2, rtol=3e-2, emu_vtol=0.05, vtol=0.1)
+    compare(64, 6, 2048, 6, selftest, emu_rtol=2e-2, rtol=3e-2, emu_vtol=1e-3, vtol=1e-3)
 
 
 def integer_network(channels, blocks, seed):
@@ -216,8 +225,10 @@ def test_integer_network_is_exact(selftest, channels, blocks, n):
     features, _ = encode_packed(bits)
     with torch.no_grad():
         emu_logits, emu_values = bf16_emulation(model, features)
-        ref_logits, ref_values = model(features)
-    net = NativePolicyValueNet(model.cpu(), device="cuda")
+        # float64 on the CPU: every convolution sum of this network is exact
+        # (cuDNN's fp32 algorithms, Winograd among them, need not be).
+        ref_logits, ref_values = (t.float().cuda() for t in model.cpu().double()(features.cpu().double()))
+    net = NativePolicyValueNet(model.cpu().float(), device="cuda")
     logits, values = net.forward_states(bits)
     torch.cuda.synchronize()
     net.check()
