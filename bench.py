@@ -44,6 +44,8 @@ TOWER_FLOPS_PER_EVAL = (2 * 81 * 9 * 10 * CHANNELS + 2 * BLOCKS * 2 * 81 * 9 * C
 # weights streamed once per image group plus the packed input states;
 # activations never leave shared memory and the head features stay in L2.
 TOWER_DRAM_BYTES_PER_LAUNCH = 1_257_216
+# The tower's per-launch CUDA events are recorded on every TIMER_EVERY-th timed ply.
+TIMER_EVERY = 4
 # Kernel launches per ply: begin, noise, finish, advance; (compact, tower,
 # heads, expand/backup) per evaluation; select per simulation.
 LAUNCHES_PER_PLY = 4 + 4 * (SIMULATIONS + 1) + SIMULATIONS
@@ -458,14 +460,24 @@ def main():
     engine.check()
     before = engine.stats()
     timer = engine.enable_timer(args.steps)
+    sampled_evals = torch.zeros((), dtype=torch.int64, device=device)
     start_ev, stop_ev = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     if world > 1:
         dist.barrier()
     torch.cuda.synchronize(device)
     with ClockSampler(local) as clocks:
         start_ev.record()
-        for _ in range(args.steps):
+        for i in range(args.steps):
+            # CUDA events bracket every tower launch of every TIMER_EVERY-th
+            # timed ply: a live sample that costs the step little. The
+            # evaluations of those plies are summed on the device.
+            sampled_ply = i % TIMER_EVERY == 0
+            engine.timer = timer if sampled_ply else None
+            if sampled_ply:
+                evals_before = engine.counters[7].clone()
             step()
+            if sampled_ply:
+                sampled_evals += engine.counters[7] - evals_before
         stop_ev.record()
         torch.cuda.synchronize(device)
     if world > 1:
@@ -485,9 +497,8 @@ def main():
     moves, evals, games, rows = local_counts.tolist()
     elapsed_s = ms[0].item() / 1000.0
     sims = moves * SIMULATIONS
-    my_evals = after["evaluations"] - before["evaluations"]
     tower_s = tower_ms / 1000.0
-    tflops = my_evals * TOWER_FLOPS_PER_EVAL / tower_s / 1e12 if tower_s > 0 else None
+    tflops = int(sampled_evals.item()) * TOWER_FLOPS_PER_EVAL / tower_s / 1e12 if tower_s > 0 else None
     peak_tf, hbm, peak_kind, _ = peaks()
 
     # e2e: the same number of plies, continuing the same games, driven from
@@ -564,6 +575,7 @@ def main():
                          "frac": (tflops / peak_tf) if tflops else None, "traffic": TOWER_DRAM_BYTES_PER_LAUNCH,
                          "peak_kind": f"{peak_kind} bf16 sustained",
                          "flops_per_eval": TOWER_FLOPS_PER_EVAL, "launches": tower_launches,
+                         "sampled": f"every tower launch of every {TIMER_EVERY}th timed ply",
                          "avg_launch_ms": tower_ms / max(tower_launches, 1)},
             "cpu_baseline": extras.get("cpu_baseline"),
             "nvrtc": extras.get("nvrtc"),

@@ -21,7 +21,9 @@ import numpy as np
 HERE = Path(__file__).resolve().parent
 ORACLE_SO = HERE / "_build" / "libgkoracle.so"
 REF_SO = HERE / "_ref" / "libgkref.so"
-REFERENCE_ROOT = Path(os.environ.get("GK_REFERENCE_ROOT", "/root/reference"))
+# Root of the reference sources, for building oracle/_ref: GK_REFERENCE_ROOT or
+# the `root` argument of build_reference (no default).
+REFERENCE_ROOT = os.environ.get("GK_REFERENCE_ROOT")
 
 STATE_WIDTH = 170
 ACTIONS = 82
@@ -44,13 +46,15 @@ def build_oracle(force: bool = False) -> Path:
     return ORACLE_SO
 
 
-def build_reference(force: bool = False) -> Path | None:
-    """Compile the reference engine from its sources when they are present."""
+def build_reference(force: bool = False, root: str | os.PathLike | None = None) -> Path | None:
+    """Compile the reference engine from its sources under `root` (or
+    GK_REFERENCE_ROOT) when they are present; else keep the built library."""
     if REF_SO.exists() and not force:
         return REF_SO
-    if not (REFERENCE_ROOT / "engine" / "src" / "State.cpp").exists():
-        return None
-    subprocess.run(["make", "-s", "-C", str(HERE), "ref", f"REF={REFERENCE_ROOT}"], check=True)
+    root = root or REFERENCE_ROOT
+    if root is None or not (Path(root) / "engine" / "src" / "State.cpp").exists():
+        return REF_SO if REF_SO.exists() else None
+    subprocess.run(["make", "-s", "-C", str(HERE), "ref", f"REF={Path(root)}"], check=True)
     return REF_SO
 
 

@@ -3,9 +3,10 @@
 The reference engine (engine/ and mcts/ of the reference repository) is
 compiled from its own sources by ``oracle/Makefile`` into
 ``oracle/_ref/libgkref.so`` and driven through ``oracle/ref_harness.cpp``.
-Run from the repository root, where the reference sources are mounted:
+Run from the repository root with the reference source root in GK_REFERENCE
+(both the engine build and the GroupNorm fixture read it):
 
-    python tests/golden/make_golden.py
+    GK_REFERENCE=<reference root> GK_REFERENCE_ROOT=<reference root> python tests/golden/make_golden.py
 
 Fixtures
   rules_<scenario>.npz  board set-ups and action sequences of the reference's
@@ -266,7 +267,7 @@ def reference_model_module():
     (encoding's ACTION_SIZE, BOARD_SIZE, INPUT_CHANNELS) is stood in for."""
     import importlib.util
     import types
-    ref = Path(os.environ.get("GK_REFERENCE", "/root/reference"))
+    ref = Path(os.environ["GK_REFERENCE"])  # the reference source root (required)
     package = types.ModuleType("refkingdom")
     package.__path__ = []
     encoding = types.ModuleType("refkingdom.encoding")
