@@ -90,9 +90,9 @@ struct NetParams {
     const float* conv_b;    // [layers][C]
     const float* head_w;    // [3][C]: policy 1x1 (2 rows) then value 1x1 (BN folded)
     const float* head_b;    // [3]
-    const float* pol_w;     // [82][162]
+    const float* pol_w;     // [162][82] feature-major
     const float* pol_b;     // [82]
-    const float* val_w1;    // [H][81], H = 64 (norm 0) or C (norm 1)
+    const float* val_w1;    // [81][H] feature-major, H = 64 (norm 0) or C (norm 1)
     const float* val_b1;    // [H]
     const float* val_w2;    // [H]
     const float* val_b2;    // [1]
@@ -961,25 +961,23 @@ struct HeadOut {
     const uint32_t* root_allow;  // search mode: [B][3] root candidates, or null (no root narrowing)
 };
 
-constexpr int kPolStride = 163;  // odd row stride: conflict-free lane-per-row reads
-constexpr int kValStride = 81;
 constexpr int kHeadWarps = 8;   // per block
 constexpr int kHeadPos = 4;     // positions per warp: each weight read from shared memory feeds four
-// Shared memory of the heads kernel for a value head of H hidden units.
+// Shared memory of the heads kernel for a value head of H hidden units:
+// the feature-major FC weights as they lie in global memory, then per warp
+// the features of its positions.
 constexpr size_t head_smem(int H) {
-    return (size_t)(82 * kPolStride + H * kValStride + kHeadWarps * kHeadPos * 244) * sizeof(float);
+    return (size_t)(162 * GK_ACTIONS + 81 * H + kHeadWarps * kHeadPos * 244) * sizeof(float);
 }
 
-// Copies an N-float row-major matrix of COLS columns into shared memory with
-// row stride STRIDE, as 4-byte asynchronous copies: every copy of the block
-// is in flight at once instead of one global round trip per batch of loads.
-// The caller commits and waits (cp.async.wait_all) before reading.
-template <int N, int COLS, int STRIDE>
-__device__ __forceinline__ void stage_matrix(float* dst, const float* src) {
-    for (int i = threadIdx.x; i < N; i += blockDim.x) {
-        const uint32_t d = tc::smem_u32(dst + (i / COLS) * STRIDE + i % COLS);
-        asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(d), "l"(src + i) : "memory");
-    }
+// Copies N floats (N a multiple of 4, both addresses 16-byte aligned) into
+// shared memory as 16-byte asynchronous copies: every copy of the block is
+// in flight at once. The caller commits and waits (cp.async.wait_all).
+template <int N>
+__device__ __forceinline__ void stage_floats(float* dst, const float* src) {
+    static_assert(N % 4 == 0, "16-byte copies");
+    for (int i = 4 * threadIdx.x; i < N; i += 4 * blockDim.x)
+        asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(tc::smem_u32(dst + i)), "l"(src + i) : "memory");
 }
 
 // H = value-head hidden units: 64 for the batch-norm layout, C for the
@@ -988,12 +986,12 @@ template <int H>
 __global__ void __launch_bounds__(32 * kHeadWarps) net_heads_kernel(NetParams p, const float* headfeat, NetInput in,
                                                                HeadOut out) {
     constexpr int HU = H / 32;  // hidden units per lane
-    extern __shared__ float hs[];
-    float* wp = hs;
-    float* w1 = wp + 82 * kPolStride;
-    float* feat_all = w1 + H * kValStride;
-    stage_matrix<82 * 162, 162, kPolStride>(wp, p.pol_w);
-    stage_matrix<H * 81, 81, kValStride>(w1, p.val_w1);
+    extern __shared__ __align__(16) float hs[];
+    float* wp = hs;                      // [162][82]
+    float* w1 = wp + 162 * GK_ACTIONS;   // [81][H]
+    float* feat_all = w1 + 81 * H;
+    stage_floats<162 * GK_ACTIONS>(wp, p.pol_w);
+    stage_floats<81 * H>(w1, p.val_w1);
     asm volatile("cp.async.wait_all;" ::: "memory");
     __syncthreads();
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -1003,9 +1001,9 @@ __global__ void __launch_bounds__(32 * kHeadWarps) net_heads_kernel(NetParams p,
     // units l + 32k (k < H/32) of the value head, for each of the warp's kHeadPos
     // positions. Every accumulation runs over the features in order, so each
     // position's sums are those of a one-position loop.
-    const float* wa = wp + lane * kPolStride;
-    const float* wb = wp + (lane + 32) * kPolStride;
-    const float* wc = wp + (lane + 64 < GK_ACTIONS ? lane + 64 : GK_ACTIONS - 1) * kPolStride;
+    const float* wa = wp + lane;       // weights of actions lane, lane+32, lane+64 at feature j: [j * 82 + a]
+    const float* wb = wp + lane + 32;
+    const float* wc = wp + (lane + 64 < GK_ACTIONS ? lane + 64 : GK_ACTIONS - 1);
     const bool gn = p.norm != 0;
     for (int img0 = (blockIdx.x * kHeadWarps + warp) * kHeadPos; img0 < count;
          img0 += gridDim.x * kHeadWarps * kHeadPos) {
@@ -1067,7 +1065,7 @@ __global__ void __launch_bounds__(32 * kHeadWarps) net_heads_kernel(NetParams p,
         for (int u = 0; u < kHeadPos; ++u) la[u] = lb[u] = lc[u] = 0.f;
 #pragma unroll 3
         for (int j = 0; j < 162; ++j) {
-            const float xa = wa[j], xb = wb[j], xc = wc[j];
+            const float xa = wa[j * GK_ACTIONS], xb = wb[j * GK_ACTIONS], xc = wc[j * GK_ACTIONS];
 #pragma unroll
             for (int u = 0; u < kHeadPos; ++u) {
                 const float f = feat[u * 244 + j];
@@ -1087,7 +1085,7 @@ __global__ void __launch_bounds__(32 * kHeadWarps) net_heads_kernel(NetParams p,
         for (int j = 0; j < 81; ++j) {
             float x[HU];
 #pragma unroll
-            for (int k = 0; k < HU; ++k) x[k] = w1[(lane + 32 * k) * kValStride + j];
+            for (int k = 0; k < HU; ++k) x[k] = w1[j * H + lane + 32 * k];
 #pragma unroll
             for (int u = 0; u < kHeadPos; ++u) {
                 const float f = feat[u * 244 + 162 + j];

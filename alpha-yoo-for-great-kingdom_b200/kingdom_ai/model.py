@@ -343,8 +343,12 @@ class NativePolicyValueNet:
             "conv_b": torch.stack([b for _, b in convs]).float(),
             "head_w": torch.cat([pw.reshape(2, -1), vw.reshape(1, -1)]).float(),
             "head_b": torch.cat([pb, vb]).float(),
-            "pol_w": model.policy_fc.weight.detach().float(), "pol_b": model.policy_fc.bias.detach().float(),
-            "val_w1": model.value_fc1.weight.detach().float(), "val_b1": model.value_fc1.bias.detach().float(),
+            # Fully connected heads feature-major ([162][82], [81][H]): the heads
+            # kernel stages them with contiguous 16-byte copies.
+            "pol_w": model.policy_fc.weight.detach().float().t().contiguous(),
+            "pol_b": model.policy_fc.bias.detach().float(),
+            "val_w1": model.value_fc1.weight.detach().float().t().contiguous(),
+            "val_b1": model.value_fc1.bias.detach().float(),
             "val_w2": model.value_fc2.weight.detach().float().reshape(-1),
             "val_b2": model.value_fc2.bias.detach().float().reshape(-1),
         }
@@ -372,8 +376,8 @@ class NativePolicyValueNet:
                                  vh[0].weight.detach().float().reshape(1, -1)]),
             "head_norm": torch.cat([ph[1].weight.detach().float(), ph[1].bias.detach().float(),
                                     vh[1].weight.detach().float(), vh[1].bias.detach().float()]),
-            "pol_w": ph[4].weight.detach().float(), "pol_b": ph[4].bias.detach().float(),
-            "val_w1": vh[4].weight.detach().float(), "val_b1": vh[4].bias.detach().float(),
+            "pol_w": ph[4].weight.detach().float().t().contiguous(), "pol_b": ph[4].bias.detach().float(),
+            "val_w1": vh[4].weight.detach().float().t().contiguous(), "val_b1": vh[4].bias.detach().float(),
             "val_w2": vh[6].weight.detach().float().reshape(-1), "val_b2": vh[6].bias.detach().float().reshape(-1),
         }
 

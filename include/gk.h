@@ -249,9 +249,9 @@ typedef struct {
     const float* conv_b;
     const float* head_w; /* [3][C] */
     const float* head_b; /* [3] */
-    const float* pol_w;  /* [82][162] */
+    const float* pol_w;  /* [162][82]: policy FC, feature-major (the transpose of torch's [82][162]) */
     const float* pol_b;  /* [82] */
-    const float* val_w1; /* [H][81], H = 64 (norm 0) or C (norm 1) */
+    const float* val_w1; /* [81][H], H = 64 (norm 0) or C (norm 1): value FC, feature-major */
     const float* val_b1; /* [H] */
     const float* val_w2; /* [H] */
     const float* val_b2; /* [1] */
