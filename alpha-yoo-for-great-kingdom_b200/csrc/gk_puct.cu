@@ -49,6 +49,9 @@ __device__ __forceinline__ float terminal_value(const gk_bits& s) {
 // increasing action order; every lane returns the same total.
 __device__ __forceinline__ double ordered_sum(const double (&v)[3], const bool (&use)[3]) {
     double total = 0.0;
+    // Unrolled so the shuffles of later actions issue while the adds, which
+    // stay in action order, wait on one another.
+#pragma unroll 8
     for (int a = 0; a < GK_ACTIONS; ++a) {
         const int k = a >> 5, src = a & 31;
         const double x = __shfl_sync(kFull, k == 0 ? v[0] : k == 1 ? v[1] : v[2], src);
