@@ -170,7 +170,7 @@ class SelfPlayEngine:
                  temperature: float = 1.0, temperature_moves: int | None = 10, final_temperature: float = 0.0,
                  replay_capacity: int = 1 << 20, seed: int | None = None, sample_seed: int | None = None,
                  rank: int = 0, world_size: int = 1, device="cuda", neutral=(4, 4), game_log: int = 0,
-                 game_limit: int = 0, first_game: int | None = None):
+                 game_limit: int = 0, first_game: int | None = None, game_stride: int | None = None):
         from .gpu_puct import HashEvaluator
 
         lib = _bind()
@@ -189,7 +189,8 @@ class SelfPlayEngine:
             float(self.options.dirichlet_epsilon), 1 if self.options.fpu_reduction is not None else 0,
             float(self.options.fpu_reduction or 0.0),
             self.options.simulations + 10**9 if temperature_moves is None else int(temperature_moves),
-            float(temperature), float(final_temperature), seed & (2**64 - 1), world_size * self.lanes, neutral_cell,
+            float(temperature), float(final_temperature), seed & (2**64 - 1),
+            world_size * self.lanes if game_stride is None else int(game_stride), neutral_cell,
             1 if self.options.tactical_checks else 0, sample_seed & (2**64 - 1), int(game_limit))
         self.first_game = rank * self.lanes if first_game is None else int(first_game)
         self.neutral_cell = neutral_cell

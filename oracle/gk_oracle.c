@@ -668,7 +668,9 @@ int gko_puct_search_batch(const int32_t* recs, int64_t n, int simulations, doubl
  * integer u = bounded(simulations) picks the first action whose running visit
  * total exceeds u (exact integer arithmetic); at other temperatures
  * u = uniform01 * total picks the first positive-weight action whose running
- * weight total exceeds u. */
+ * weight total exceeds u. With `tactics` each search narrows its root by the
+ * root tactical checks (gko_root_tactics), as the engine does with
+ * tactical_checks set. */
 #define GKO_SAMPLE_SALT 0x9E3779B97F4A7C15ULL
 
 static double o_uniform01(gk_pcg32* r) {
@@ -677,14 +679,15 @@ static double o_uniform01(gk_pcg32* r) {
 }
 
 int gko_selfplay_hash_game(uint64_t sample_seed, uint64_t game, int neutral_cell, int simulations, double c_puct,
-                           int temperature_moves, double temperature, double final_temperature, uint8_t* actions,
-                           float* policy, int32_t* rec) {
+                           int temperature_moves, double temperature, double final_temperature, int tactics,
+                           uint8_t* actions, float* policy, int32_t* rec) {
     gko_initial(rec, neutral_cell);
     for (int ply = 0; ply < GK_MAX_PLIES + 2; ++ply) {
         if (rec[GK_REASON] != GK_NONE) return ply;
         int32_t visits[GK_ACTIONS], stats[4];
         double priors[GK_ACTIONS], values[2];
-        int status = gko_puct_search(rec, simulations, c_puct, visits, priors, stats, values);
+        int status = tactics ? gko_puct_search_tactics(rec, simulations, c_puct, 0, visits, priors, stats, values)
+                             : gko_puct_search(rec, simulations, c_puct, visits, priors, stats, values);
         if (status != 0) return status < 0 ? status : -1;
         const int sims = stats[1];
         for (int a = 0; a < GK_ACTIONS; ++a)
@@ -730,7 +733,7 @@ int gko_selfplay_hash_game(uint64_t sample_seed, uint64_t game, int neutral_cell
 typedef struct {
     uint64_t sample_seed, first_game;
     int64_t begin, end;
-    int neutral_cell, simulations, temperature_moves;
+    int neutral_cell, simulations, temperature_moves, tactics;
     double c_puct, temperature, final_temperature;
     uint8_t* actions;
     float* policy;
@@ -743,7 +746,7 @@ static void* selfplay_worker(void* arg) {
     for (int64_t i = j->begin; i < j->end; ++i)
         j->plies[i] = gko_selfplay_hash_game(j->sample_seed, j->first_game + (uint64_t)i, j->neutral_cell,
                                              j->simulations, j->c_puct, j->temperature_moves, j->temperature,
-                                             j->final_temperature, j->actions + i * (GK_MAX_PLIES + 2),
+                                             j->final_temperature, j->tactics, j->actions + i * (GK_MAX_PLIES + 2),
                                              j->policy + i * (int64_t)(GK_MAX_PLIES + 2) * GK_ACTIONS,
                                              j->recs + i * GK_STATE_WIDTH);
     return NULL;
@@ -751,7 +754,7 @@ static void* selfplay_worker(void* arg) {
 
 void gko_selfplay_hash_games(uint64_t sample_seed, uint64_t first_game, int64_t n, int neutral_cell,
                              int simulations, double c_puct, int temperature_moves, double temperature,
-                             double final_temperature, uint8_t* actions, float* policy, int32_t* recs,
+                             double final_temperature, int tactics, uint8_t* actions, float* policy, int32_t* recs,
                              int32_t* plies, int threads) {
     if (threads < 1) threads = 1;
     if (threads > 256) threads = 256;
@@ -763,7 +766,7 @@ void gko_selfplay_hash_games(uint64_t sample_seed, uint64_t first_game, int64_t 
         int64_t b = (int64_t)t * per, e = b + per < n ? b + per : n;
         if (b >= e) break;
         jobs[t] = (selfplay_job){sample_seed, first_game, b, e, neutral_cell, simulations, temperature_moves,
-                                 c_puct, temperature, final_temperature, actions, policy, recs, plies};
+                                 tactics, c_puct, temperature, final_temperature, actions, policy, recs, plies};
         pthread_create(&tid[t], NULL, selfplay_worker, &jobs[t]);
         ++started;
     }

@@ -56,17 +56,18 @@ int gko_puct_search_batch(const int32_t* recs, int64_t n, int simulations, doubl
 
 /* Self-play of one game with the injected evaluator and no root noise, as the
  * device engine plays it (temperature schedule of collect_gpu_puct_games,
- * move draws from PCG32 (sample_seed ^ salt, game * 256 + ply)). Outputs:
+ * move draws from PCG32 (sample_seed ^ salt, game * 256 + ply); tactics: the
+ * root tactical checks narrow every root). Outputs:
  * actions[GK_MAX_PLIES + 2], policy[GK_MAX_PLIES + 2][82] (visit shares per
  * ply), the final record rec[170]. Returns the plies played, or < 0. */
 int gko_selfplay_hash_game(uint64_t sample_seed, uint64_t game, int neutral_cell, int simulations, double c_puct,
-                           int temperature_moves, double temperature, double final_temperature, uint8_t* actions,
-                           float* policy, int32_t* rec);
+                           int temperature_moves, double temperature, double final_temperature, int tactics,
+                           uint8_t* actions, float* policy, int32_t* rec);
 /* Games first_game .. first_game + n - 1 of the above on `threads` threads;
  * plies[n] receives each game's return value. */
 void gko_selfplay_hash_games(uint64_t sample_seed, uint64_t first_game, int64_t n, int neutral_cell,
                              int simulations, double c_puct, int temperature_moves, double temperature,
-                             double final_temperature, uint8_t* actions, float* policy, int32_t* recs,
+                             double final_temperature, int tactics, uint8_t* actions, float* policy, int32_t* recs,
                              int32_t* plies, int threads);
 
 /* BatchedPUCT (mcts/src/BatchedPUCT.cpp): a persistent searcher with leaf

@@ -85,12 +85,13 @@ class Oracle:
         _bind(L, "gko_root_tactics", [_i32p, _i8p, _u8p])
         _bind(L, "gko_puct_search_tactics", [_i32p, _int, ctypes.c_double, _int, _i32p, _f64p, _i32p, _f64p], _int)
         _bind(L, "gko_selfplay_hash_games", [_u64, _u64, _i64, _int, _int, ctypes.c_double, _int, ctypes.c_double,
-                                             ctypes.c_double, _u8p, _f32p, _i32p, _i32p, _int])
+                                             ctypes.c_double, _int, _u8p, _f32p, _i32p, _i32p, _int])
         _bind_batched(L, "gko")
 
     def selfplay_hash(self, sample_seed: int, games: int, simulations: int, *, first_game: int = 0,
                       c_puct: float = 1.5, temperature_moves: int = 10, temperature: float = 1.0,
-                      final_temperature: float = 0.0, neutral: int = 40, threads: int | None = None):
+                      final_temperature: float = 0.0, neutral: int = 40, tactics: bool = False,
+                      threads: int | None = None):
         """Games first_game .. first_game + games - 1 as the device self-play
         engine plays them with the injected evaluator and no root noise.
 
@@ -104,8 +105,8 @@ class Oracle:
         plies = np.zeros(games, dtype=np.int32)
         threads = threads or max(1, min(len(os.sched_getaffinity(0)), 64))
         self.lib.gko_selfplay_hash_games(sample_seed, first_game, games, neutral, simulations, c_puct,
-                                         temperature_moves, temperature, final_temperature, actions, policy, recs,
-                                         plies, threads)
+                                         temperature_moves, temperature, final_temperature, int(tactics), actions,
+                                         policy, recs, plies, threads)
         return plies, actions, policy, recs
 
     def batched(self, simulations, c_puct=1.5, leaf_batch=8, reuse=True, evaluator="hash"):

@@ -98,16 +98,18 @@ def finished_games(engine):
     return log, rows_of(engine)
 
 
-def test_injected_evaluator_games_equal_the_oracle_bit_for_bit(oracle):
+@pytest.mark.parametrize("tactics", [False, True])
+def test_injected_evaluator_games_equal_the_oracle_bit_for_bit(oracle, tactics):
     """No root noise, T = 1 for 10 plies then the best action: every finished
     game - its moves, visit-share targets, planes, masks, values and final
-    position - equals the oracle's restatement of the same game id."""
+    position - equals the oracle's restatement of the same game id; with the
+    root tactical checks on as well."""
     from kingdom_ai.gpu_puct import GpuPUCTOptions, HashEvaluator
     from kingdom_ai.gpu_rules import bits_to_records
     from kingdom_ai.selfplay import SelfPlayEngine
 
     lanes, plies, sims, seed = 256, 90, 32, 77
-    opts = GpuPUCTOptions(simulations=sims, c_puct=1.5, dirichlet_epsilon=0.0, seed=3)
+    opts = GpuPUCTOptions(simulations=sims, c_puct=1.5, dirichlet_epsilon=0.0, seed=3, tactical_checks=tactics)
     engine = SelfPlayEngine(HashEvaluator(), lanes, opts, temperature_moves=10, replay_capacity=1 << 16,
                             sample_seed=seed, game_log=4096)
     engine.step(plies)
@@ -119,7 +121,8 @@ def test_injected_evaluator_games_equal_the_oracle_bit_for_bit(oracle):
     ids = log["game_id"].astype(np.int64)
     finals = bits_to_records(torch.from_numpy(log["final_state"]).cuda()).cpu().numpy()
     for gid in np.unique(ids):
-        o_plies, o_actions, o_policy, o_final = oracle.selfplay_hash(seed, 1, sims, first_game=int(gid))
+        o_plies, o_actions, o_policy, o_final = oracle.selfplay_hash(seed, 1, sims, first_game=int(gid),
+                                                                     tactics=tactics)
         slot = int(np.nonzero(ids == gid)[0][0])
         k, first = int(log["plies"][slot]), int(log["first_row"][slot])
         assert k == o_plies[0] > 0, gid
@@ -181,22 +184,25 @@ def test_engine_visit_targets_equal_gpupuct_searches(oracle):
     assert np.array_equal(result.visits.cpu().numpy()[pick], visits)
 
 
-def test_network_games_replay_in_the_reference_engine(oracle, reference):
+@pytest.mark.parametrize("net,sims,plies", [("6x64", 400, 64), ("groupnorm32x2", 128, 80)])
+def test_network_games_replay_in_the_reference_engine(oracle, reference, net, sims, plies):
     """C5 settings (6x64 network, Dirichlet 0.3 / 0.25, T = 1 for 10 plies then
-    the best action, 400 simulations) on 256 lanes for 64 plies: every finished
-    game replays move by move in the reference's kingdom::State; every replay
-    row carries that state's planes and mask, the mover, and +1 exactly on the
-    winner's moves; the final position equals the reference's."""
+    the best action, 400 simulations) on 256 lanes for 64 plies, and the
+    Trainer's defaults (the reference's own 32 x 2 GroupNorm network, 128
+    simulations): every finished game replays move by move in the reference's
+    kingdom::State; every replay row carries that state's planes and mask, the
+    mover, and +1 exactly on the winner's moves; the final position equals
+    the reference's."""
     from kingdom_ai.gpu_puct import GpuPUCTOptions
     from kingdom_ai.gpu_rules import bits_to_records
-    from kingdom_ai.model import random_network
+    from kingdom_ai.model import random_groupnorm_network, random_network
     from kingdom_ai.selfplay import SelfPlayEngine
     from oracle.oracle import RefState
 
-    opts = GpuPUCTOptions(simulations=400, c_puct=1.5, dirichlet_alpha=0.3, dirichlet_epsilon=0.25, seed=19)
-    engine = SelfPlayEngine(random_network(64, 6, 7), 256, opts, temperature_moves=10, replay_capacity=1 << 16,
-                            game_log=4096)
-    engine.step(64)
+    model = random_network(64, 6, 7) if net == "6x64" else random_groupnorm_network(32, 2, 7)
+    opts = GpuPUCTOptions(simulations=sims, c_puct=1.5, dirichlet_alpha=0.3, dirichlet_epsilon=0.25, seed=19)
+    engine = SelfPlayEngine(model, 256, opts, temperature_moves=10, replay_capacity=1 << 16, game_log=4096)
+    engine.step(plies)
     torch.cuda.synchronize()
     engine.check()
     log, (feats, masks, policy, value, to_play) = finished_games(engine)

@@ -365,3 +365,27 @@ def test_oracle_batched_search_known_answers(oracle):
         assert np.array_equal(r["visits"], legacy["visits"]) and np.array_equal(r["priors"], legacy["priors"])
         assert (r["best"], r["nodes"], r["evaluations"]) == (legacy["best"], legacy["nodes"], legacy["evaluations"])
         assert (r["root_value"], r["best_value"]) == (legacy["root_value"], legacy["best_value"])
+
+
+def test_oracle_selfplay_games_follow_the_reference_engine(oracle, reference):
+    """The self-play restatement against the reference itself: every game
+    replays in kingdom::State, every ply's visit-share target is the reference
+    PUCT::search's visits over its simulations (the same injected evaluator),
+    every move played after the sampled opening is the reference's best move,
+    and the final position is the reference's."""
+    import numpy as np
+
+    from oracle.oracle import RefState
+
+    sims = 24
+    plies, actions, policy, finals = oracle.selfplay_hash(3, 6, sims, temperature_moves=4)
+    for g in range(6):
+        state = RefState.initial(reference)
+        assert plies[g] > 0
+        for ply in range(plies[g]):
+            r = state.puct(sims)
+            assert np.array_equal(policy[g, ply], (r["visits"].astype(np.float32) / np.float32(sims))), (g, ply)
+            if ply >= 4:
+                assert actions[g, ply] == r["best"], (g, ply)
+            assert state.play(int(actions[g, ply]))
+        assert np.array_equal(state.record(), finals[g])
