@@ -820,8 +820,16 @@ __global__ void __launch_bounds__(Cols64::THREADS, 1)
                     // layers ago and now overwrites in place) before the accumulator
                     // is ready. Row 127 belongs to the next tile and is not stored.
                     float pre[32];
+                    // Eight 16-byte loads (bias + 32 h is 128-byte aligned), not 32 scalar ones:
+                    // the L1 data pipe is the one the MMA operands and the stores use.
 #pragma unroll
-                    for (int j = 0; j < 32; ++j) pre[j] = __ldg(bias + j);
+                    for (int j = 0; j < 8; ++j) {
+                        const float4 b4 = __ldg(reinterpret_cast<const float4*>(bias) + j);
+                        pre[4 * j] = b4.x;
+                        pre[4 * j + 1] = b4.y;
+                        pre[4 * j + 2] = b4.z;
+                        pre[4 * j + 3] = b4.w;
+                    }
                     if (residual) {
 #pragma unroll
                         for (int k2 = 0; k2 < 4; ++k2) {
@@ -907,13 +915,21 @@ __global__ void __launch_bounds__(Cols64::THREADS, 1)
                 for (int kk = 0; kk < C / 8; ++kk) {
                     const uint4 rv = *reinterpret_cast<const uint4*>(row + kk * K::CHUNK);
                     const uint32_t w[4] = {rv.x, rv.y, rv.z, rv.w};
+                    // The 8 channels' weights of the three head rows as 16-byte broadcast loads.
+                    float hw[3][8];
+#pragma unroll
+                    for (int o = 0; o < 3; ++o) {
+                        const float4 lo = *reinterpret_cast<const float4*>(headw + o * C + kk * 8);
+                        const float4 hi = *reinterpret_cast<const float4*>(headw + o * C + kk * 8 + 4);
+                        hw[o][0] = lo.x, hw[o][1] = lo.y, hw[o][2] = lo.z, hw[o][3] = lo.w;
+                        hw[o][4] = hi.x, hw[o][5] = hi.y, hw[o][6] = hi.z, hw[o][7] = hi.w;
+                    }
 #pragma unroll
                     for (int j = 0; j < 8; ++j) {
                         const float xv = (j & 1) ? bf16_hi(w[j >> 1]) : bf16_lo(w[j >> 1]);
-                        const int ch = kk * 8 + j;
-                        h0 = fmaf(xv, headw[ch], h0);
-                        h1 = fmaf(xv, headw[C + ch], h1);
-                        h2 = fmaf(xv, headw[2 * C + ch], h2);
+                        h0 = fmaf(xv, hw[0][j], h0);
+                        h1 = fmaf(xv, hw[1][j], h1);
+                        h2 = fmaf(xv, hw[2][j], h2);
                     }
                 }
                 float* hf = headfeat + (int64_t)(base_img + img) * 243 + r * 9 + cc;
