@@ -1305,10 +1305,20 @@ inline bool valid_net(const gk_net_t* net) {
     return net->norm == 1 && net->norm_w && net->norm_b && net->head_norm;
 }
 
+// Records `e` on `stream`; inside a stream capture as an external event node,
+// so that replays of the graph record it (and its times can be read).
+inline void record_event(cudaEvent_t e, cudaStream_t stream) {
+    cudaStreamCaptureStatus capturing = cudaStreamCaptureStatusNone;
+    if (cudaStreamIsCapturing(stream, &capturing) == cudaSuccess && capturing == cudaStreamCaptureStatusActive)
+        cudaEventRecordWithFlags(e, stream, cudaEventRecordExternal);
+    else
+        cudaEventRecord(e, stream);
+}
+
 int run_forward(const gk_net_t* net, const NetInput& in, float* headfeat, const HeadOut& out, uint32_t* status,
                 cudaStream_t stream, cudaEvent_t tower_start = nullptr, cudaEvent_t tower_stop = nullptr) {
     const NetParams p = make_params(net);
-    if (tower_start) cudaEventRecord(tower_start, stream);
+    if (tower_start) record_event(tower_start, stream);
     // The column-fused kernel serves the 64-channel batch-norm layout; GroupNorm
     // needs whole-image statistics between layers, which the templated tower
     // gathers (its conv_w is per tap for every width).
@@ -1322,7 +1332,7 @@ int run_forward(const gk_net_t* net, const NetInput& in, float* headfeat, const 
             : net->channels == 64 ? launch_tower<64, true>(p, in, headfeat, status, stream)
                                   : launch_tower<128, true>(p, in, headfeat, status, stream);
     }
-    if (tower_stop) cudaEventRecord(tower_stop, stream);
+    if (tower_stop) record_event(tower_stop, stream);
     if (s) return s;
     return launch_heads(p, headfeat, in, out, stream);
 }

@@ -214,6 +214,9 @@ class SelfPlayEngine:
         self.last_policy = self.storage[bufs.last_policy - base:bufs.last_policy - base + self.lanes * 82 * 4].view(
             torch.float32).view(self.lanes, 82)
         self.timer = None
+        self._graph = None
+        self._timed_graph = None  # (timer, graph): a ply whose tower launches record the timer's events
+        self._stepped = False
         self.reset()
 
     def reset(self):
@@ -231,9 +234,56 @@ class SelfPlayEngine:
         """Search `simulations` per move from the next ply on (at most the options' count)."""
         if type(simulations) is not int or not 1 <= simulations <= self.options.simulations:
             raise ValueError("simulations must be an integer in [1, options.simulations]")
+        if simulations != self.params.simulations:
+            self._graph = self._timed_graph = None  # a captured ply has the old count baked in
         self.params.simulations = simulations
 
+    def capture(self):
+        """Record one ply as a CUDA graph; ``step()`` then replays it instead of
+        issuing its 4 + 4 (S + 1) + S launches one by one.
+
+        A ply's launches and their arguments are the same every ply (lane
+        states, ply counters, game ids, counters and rings all live in device
+        memory), so a replay is exactly a ``gk_selfplay_ply`` call. With a
+        tower timer attached (``enable_timer``) a second graph is captured
+        whose tower launches record the timer's first ply of event pairs;
+        plies stepped with that timer replay it, so after them the timer holds
+        the last such ply's tower times. Call after at least one ``step()`` at
+        the current settings (the first ply sets per-device kernel attributes,
+        which a capture may not do).
+        """
+        if not self._stepped:
+            raise RuntimeError("step() once before capture()")
+        self._graph = self._capture(None)
+        if self.timer is not None:
+            self.timer.reset()
+            self._timed_graph = (self.timer, self._capture(self.timer))
+
+    def _capture(self, timer):
+        with torch.cuda.device(self.device):
+            capture_stream = torch.cuda.Stream(self.device)
+            capture_stream.wait_stream(torch.cuda.current_stream(self.device))
+            graph = torch.cuda.CUDAGraph()
+            with torch.cuda.stream(capture_stream), torch.cuda.graph(graph, stream=capture_stream):
+                self._launch(1, timer=timer)
+            torch.cuda.current_stream(self.device).wait_stream(capture_stream)
+        return graph
+
     def step(self, plies: int = 1):
+        graph = None
+        if self.timer is None:
+            graph = self._graph
+        elif self._timed_graph is not None and self._timed_graph[0] is self.timer:
+            graph = self._timed_graph[1]
+        if graph is not None:
+            with torch.cuda.device(self.device):
+                for _ in range(plies):
+                    graph.replay()
+            return
+        self._launch(plies, self.timer)
+        self._stepped = True
+
+    def _launch(self, plies: int, timer):
         with torch.cuda.device(self.device):
             stream = _launch_scope(self.device, self.storage, self.search.storage, self.headfeat)
             replay = self.replay.struct if self.replay is not None else None
@@ -242,7 +292,7 @@ class SelfPlayEngine:
             for _ in range(plies):
                 native.call("gk_selfplay_ply", native.ptr(self.storage), self.search.pointer, self.lanes,
                             net, self.params, replay, games, native.ptr(self.headfeat),
-                            native.ptr(self.status), self.timer.handle if self.timer else None, stream)
+                            native.ptr(self.status), timer.handle if timer else None, stream)
 
     def load_records(self, records: torch.Tensor):
         """Set every lane's position from wire records (int32 [lanes,170], host

@@ -44,8 +44,6 @@ TOWER_FLOPS_PER_EVAL = (2 * 81 * 9 * 10 * CHANNELS + 2 * BLOCKS * 2 * 81 * 9 * C
 # weights streamed once per image group plus the packed input states;
 # activations never leave shared memory and the head features stay in L2.
 TOWER_DRAM_BYTES_PER_LAUNCH = 1_257_216
-# The tower's per-launch CUDA events are recorded on every TIMER_EVERY-th timed ply.
-TIMER_EVERY = 4
 # Kernel launches per ply: begin, noise, finish, advance; (compact, tower,
 # heads, expand/backup) per evaluation; select per simulation.
 LAUNCHES_PER_PLY = 4 + 4 * (SIMULATIONS + 1) + SIMULATIONS
@@ -456,10 +454,13 @@ def main():
     engine.set_simulations(SIMULATIONS)
     for _ in range(args.warmup):
         step()
+    # Each ply replays one captured CUDA graph of its launches; a second
+    # graph's tower launches also record CUDA events (the roofline sample).
+    timer = engine.enable_timer(1)
+    engine.capture()
     torch.cuda.synchronize(device)
     engine.check()
     before = engine.stats()
-    timer = engine.enable_timer(args.steps)
     sampled_evals = torch.zeros((), dtype=torch.int64, device=device)
     start_ev, stop_ev = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     if world > 1:
@@ -468,10 +469,10 @@ def main():
     with ClockSampler(local) as clocks:
         start_ev.record()
         for i in range(args.steps):
-            # CUDA events bracket every tower launch of every TIMER_EVERY-th
-            # timed ply: a live sample that costs the step little. The
-            # evaluations of those plies are summed on the device.
-            sampled_ply = i % TIMER_EVERY == 0
+            # CUDA events bracket every tower launch of the last timed ply: a
+            # live sample (the timer keeps the last replay's times). The
+            # evaluations of that ply are counted on the device.
+            sampled_ply = i == args.steps - 1
             engine.timer = timer if sampled_ply else None
             if sampled_ply:
                 evals_before = engine.counters[7].clone()
@@ -569,13 +570,14 @@ def main():
                        "lanes_per_gpu": LANES, "simulations": SIMULATIONS, "parallelism": f"games sharded x{world}",
                        "steady_state": f"{args.preroll_plies} pre-roll plies at {args.preroll_sims} sims/move, "
                                        f"then {args.warmup} warm-up plies at {SIMULATIONS}",
+                       "launch": f"each ply replays a captured CUDA graph of its {LAUNCHES_PER_PLY} kernel launches",
                        "l2": "working set (search trees 3.2 GB/GPU) far larger than L2"},
             "roofline": {"bound": "tensor", "kernel": "net_tower_cols_kernel",
                          "achieved": tflops, "peak": peak_tf, "unit": "TFLOP/s",
                          "frac": (tflops / peak_tf) if tflops else None, "traffic": TOWER_DRAM_BYTES_PER_LAUNCH,
                          "peak_kind": f"{peak_kind} bf16 sustained",
                          "flops_per_eval": TOWER_FLOPS_PER_EVAL, "launches": tower_launches,
-                         "sampled": f"every tower launch of every {TIMER_EVERY}th timed ply",
+                         "sampled": "every tower launch of the last timed ply",
                          "avg_launch_ms": tower_ms / max(tower_launches, 1)},
             "cpu_baseline": extras.get("cpu_baseline"),
             "nvrtc": extras.get("nvrtc"),

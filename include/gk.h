@@ -388,7 +388,8 @@ GK_API int gk_selfplay_buffers(void* ws, int64_t lanes, gk_selfplay_buffers_t* o
  * restart, or park once params->game_limit is reached. `puct_ws` is a search
  * workspace for (lanes, simulations + 1); `headfeat` holds
  * gk_net_headfeat_bytes(lanes); `timer` (may be NULL, see gk_timer_create)
- * records the network tower's launches. `net` may be NULL: leaves are then
+ * records the network tower's launches (inside a stream capture, as external
+ * event nodes, so a graph replay records them). `net` may be NULL: leaves are then
  * scored by the injected evaluator (gk_puct_hash_eval) and headfeat may be
  * NULL. Replaces one iteration of the reference's per-ply loop
  * (gpu_training.py:59-87). */

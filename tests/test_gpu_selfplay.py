@@ -226,3 +226,30 @@ def test_network_games_replay_in_the_reference_engine(oracle, reference, net, si
         assert winner == final[GPU_WINNER]
         movers = to_play[first:first + k]
         assert np.array_equal(value[first:first + k], np.where(movers == winner, 1.0, -1.0).astype(np.float32))
+
+
+def test_graph_replay_plays_the_same_games():
+    """A captured ply replayed as a CUDA graph is the same computation as the
+    direct launches: same counters, same replay rows, same game log."""
+    from kingdom_ai.gpu_puct import GpuPUCTOptions
+    from kingdom_ai.selfplay import SelfPlayEngine
+
+    def run(graph):
+        opts = GpuPUCTOptions(simulations=24, c_puct=1.5, dirichlet_alpha=0.3, dirichlet_epsilon=0.25, seed=4)
+        engine = SelfPlayEngine(small_net(), 64, opts, temperature_moves=6, replay_capacity=1 << 14, game_log=1024)
+        engine.step(1)
+        if graph:
+            engine.capture()
+        engine.step(59)
+        torch.cuda.synchronize()
+        engine.check()
+        return engine
+
+    direct, replayed = run(False), run(True)
+    assert direct.stats() == replayed.stats() and direct.stats()["games"] > 0
+    assert keyset(rows_of(direct)) == keyset(rows_of(replayed))
+    n = direct.stats()["games"]
+    a, b = direct.games.read(n), replayed.games.read(n)
+    order_a, order_b = a["game_id"].argsort(), b["game_id"].argsort()
+    for key in ("game_id", "plies", "winner", "reason", "actions", "final_state"):
+        assert np.array_equal(a[key][order_a], b[key][order_b]), key
