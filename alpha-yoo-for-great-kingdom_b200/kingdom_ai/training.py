@@ -169,7 +169,8 @@ def _run_engine(engine, count):
 
     The host reads the finished-game counter one ply behind the GPU: after
     enqueueing ply p it waits for ply p-1's counter copy, so the device always
-    has the next ply queued and never idles on the host.
+    has the next ply queued and never idles on the host. Plies after the first
+    replay a CUDA graph of its launches.
     """
     from .selfplay import GAME_ACTIONS
 
@@ -179,6 +180,8 @@ def _run_engine(engine, count):
     bound = (-(-count // engine.lanes)) * GAME_ACTIONS + 2
     for ply in range(bound + 1):
         engine.step()
+        if ply == 0:
+            engine.capture()  # later plies replay the first one's launches as a CUDA graph
         host[ply % 2].copy_(engine.counters, non_blocking=True)
         done[ply % 2].record(stream)
         if ply >= 1:

@@ -386,7 +386,7 @@ def main():
     parser.add_argument("--no-extras", action="store_true",
                         help="skip the component lines, the CPU baseline and the NVRTC figure")
     parser.add_argument("--workload", choices=["selfplay", "network", "rules", "encode", "puct", "replay", "batched",
-                                                   "selfplay_reference", "evaluation"],
+                                                   "selfplay_reference", "evaluation", "collect"],
                         default="selfplay",
                         help="selfplay is the headline; the others time one kernel family each")
     parser.add_argument("--net", default="128x10", help="network workload: CHANNELSxBLOCKS")
@@ -401,8 +401,9 @@ def main():
     parser.add_argument("--searchers", type=int, default=4096, help="batched workload: games searched together")
     parser.add_argument("--sims-batched", type=int, default=128, help="batched workload: simulations per search")
     parser.add_argument("--leaf", type=int, default=8, help="batched workload: leaf batch per tree")
-    parser.add_argument("--lanes", type=int, default=4096, help="selfplay_reference workload: games at once")
-    parser.add_argument("--games", type=int, default=512, help="evaluation workload: games in the match")
+    parser.add_argument("--lanes", type=int, default=4096,
+                        help="selfplay_reference and collect workloads: games at once")
+    parser.add_argument("--games", type=int, default=512, help="evaluation and collect workloads: games")
     args = parser.parse_args()
     if args.impl == "reference":
         reference_arm(args)

@@ -8,6 +8,7 @@
     batched  the evaluation searcher (BatchedPUCT) for 4096 games x 128 simulations, leaf batch 8
     selfplay_reference  self-play with the reference's 32 x 2 GroupNorm network and its 128 simulations
     evaluation  a 512-game evaluation match between two 6 x 64 networks (evaluate_models_gpu)
+    collect  the Trainer's hook: collect_gpu_puct_games for --games games, --lanes in flight
 
 Every timed launch is bracketed by CUDA events on the launching stream; an L2
 flush (a 256 MB write) separates timed launches so each one reads its inputs
@@ -463,3 +464,31 @@ def bench_evaluation(args, peaks):
           "moves_per_s": result.total_plies / seconds, "simulations_per_s": result.total_plies * 128 / seconds,
           "seconds": seconds, "wall_seconds": wall, "total_plies": result.total_plies,
           "candidate_win_rate": result.win_rate, "endings": result.endings}
+
+
+def bench_collect(args, peaks):
+    """The Trainer's self-play hook end to end (python/kingdom_ai/loop.py:
+    524-541 calling collect_gpu_puct_games): `--games` complete games with
+    `--lanes` in flight, the 6 x 64 network, 400 simulations, Dirichlet 0.3 /
+    0.25, T = 1 for 10 plies then the best action. Wall clock around the whole
+    call, which returns GameData built on the host; after one warm-up call."""
+    import time
+
+    from kingdom_ai.gpu_puct import GpuPUCTOptions
+    from kingdom_ai.model import random_network
+    from kingdom_ai.training import collect_gpu_puct_games
+
+    model = random_network(64, 6, 1234)
+    opts = GpuPUCTOptions(simulations=400, c_puct=1.5, dirichlet_alpha=0.3, dirichlet_epsilon=0.25, seed=7)
+    kw = dict(options=opts, temperature=1.0, temperature_moves=10, final_temperature=0.0, seed=11)
+    collect_gpu_puct_games(model, 8, batch_size=8, **kw)
+    torch.cuda.synchronize()
+    start = time.perf_counter()
+    games = collect_gpu_puct_games(model, args.games, batch_size=args.lanes, **kw)
+    seconds = time.perf_counter() - start
+    moves = sum(len(g.samples) for g in games)
+    return {"workload": f"collect_gpu_puct_games: {args.games} games, {args.lanes} in flight, 64ch x 6-block bf16 net, "
+                        "400 sims/move, Dirichlet 0.3/0.25, T=1 for 10 plies then best",
+            "metric": "simulations/s", "unit": "simulations/s", "value": moves * 400 / seconds,
+            "moves_per_s": moves / seconds, "games_per_s": len(games) / seconds, "seconds": seconds,
+            "moves": moves, "timing": "wall clock around the call, GameData returned on the host"}
