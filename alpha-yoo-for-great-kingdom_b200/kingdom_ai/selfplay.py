@@ -264,7 +264,10 @@ class SelfPlayEngine:
             capture_stream = torch.cuda.Stream(self.device)
             capture_stream.wait_stream(torch.cuda.current_stream(self.device))
             graph = torch.cuda.CUDAGraph()
-            with torch.cuda.stream(capture_stream), torch.cuda.graph(graph, stream=capture_stream):
+            # thread_local: other threads' CUDA calls (NCCL's, under torchrun)
+            # do not invalidate this capture.
+            with torch.cuda.stream(capture_stream), torch.cuda.graph(graph, stream=capture_stream,
+                                                                     capture_error_mode="thread_local"):
                 self._launch(1, timer=timer)
             torch.cuda.current_stream(self.device).wait_stream(capture_stream)
         return graph
