@@ -650,6 +650,36 @@ __device__ __forceinline__ void store_row32(uint8_t* row, const float (&pre)[32]
     }
 }
 
+// The k-th image group of CTA b out of P for `count` images. Rounds of full
+// groups (5 images, 4 tiles) come first; the images left over after the last
+// full round are spread over as many CTAs as take at least two each (2 to 5
+// images), so the last round keeps every SM busy with shorter groups instead
+// of a few SMs with full ones. A group has at least two tiles, so both MMA
+// warps and both epilogue sets have work in every layer.
+struct ColsGroup {
+    int base, nimg, tiles;
+};
+
+__device__ __forceinline__ bool cols_group(int k, int b, int P, int count, ColsGroup& g) {
+    const int full_rounds = count / (Cols64::G * P);
+    if (k < full_rounds) {
+        g.base = (k * P + b) * Cols64::G;
+        g.nimg = Cols64::G;
+        g.tiles = Cols64::T;
+        return true;
+    }
+    const int tail0 = full_rounds * Cols64::G * P, tail = count - tail0;
+    if (k > full_rounds || tail <= 0) return false;
+    const int m = tail >= 2 * P ? P : (tail / 2 > 0 ? tail / 2 : 1);  // CTAs that take a tail group
+    if (b >= m) return false;
+    const int per = tail / m, extra = tail % m;
+    g.nimg = per + (b < extra ? 1 : 0);
+    g.base = tail0 + b * per + (b < extra ? b : extra);
+    const int t = (g.nimg * 100 + Cols64::STRIDE - 1) / Cols64::STRIDE;
+    g.tiles = t < 2 ? 2 : t;
+    return true;
+}
+
 __global__ void __launch_bounds__(Cols64::THREADS, 1)
     net_tower_cols_kernel(NetParams p, NetInput in, float* headfeat, uint32_t* status) {
     using K = Cols64;
@@ -675,7 +705,7 @@ __global__ void __launch_bounds__(Cols64::THREADS, 1)
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int NL = 1 + 2 * p.blocks;
     const int count = input_count(in);
-    const int groups = (count + K::G - 1) / K::G;
+    const int P = (int)gridDim.x, cta = (int)blockIdx.x;
 
     for (int i = threadIdx.x; i < 2 * K::ACT / 16; i += blockDim.x)
         reinterpret_cast<uint4*>(smem)[i] = make_uint4(0, 0, 0, 0);
@@ -705,7 +735,8 @@ __global__ void __launch_bounds__(Cols64::THREADS, 1)
     if (warp == 0 && lane == 0) {
         // ---------------- weight producer: slot dr <- row offset dr's [Cin/8][3][64][8] block ----------------
         int u = 0;  // layers issued so far (each layer fills every slot once)
-        for (int g = blockIdx.x; g < groups; g += gridDim.x) {
+        ColsGroup grp;
+        for (int gk = 0; cols_group(gk, cta, P, count, grp); ++gk) {
             for (int l = 0; l < NL; ++l, ++u) {
                 const int chunks = l == 0 ? 2 : C / 8;  // 8-channel input chunks (stem input padded to 16)
                 for (int dr = 0; dr < 3; ++dr) {
@@ -732,31 +763,35 @@ __global__ void __launch_bounds__(Cols64::THREADS, 1)
         const bool leader = lane == 0;
         const int ms = warp - 1;
         int c = 0, u = 0, i = 0;
-        for (int g = blockIdx.x; g < groups; g += gridDim.x, ++i) {
+        ColsGroup grp;
+        for (int gk = 0; cols_group(gk, cta, P, count, grp); ++gk, ++i) {
+            const int T = grp.tiles;
             for (int l = 0; l < NL; ++l, ++u) {
                 const uint32_t a_lo = (uint32_t)(l % 2 == 0 ? adescQ : adescP);
                 const int ks = l == 0 ? 1 : C / 16;
-                for (int t = 0; t < K::T; ++t, ++c) {
+                const int t_first = (ms - c) & 1;  // this warp's first tile of the layer (tiles alternate warps)
+                for (int t = 0; t < T; ++t, ++c) {
                     if ((c & 1) != ms) continue;
-                    const bool first_use = t == ms;  // this warp's first tile of the layer waits for the weights
-                    const bool last_use = t + 2 >= K::T;  // and its last one releases them
+                    const bool first_use = t == t_first;  // this warp's first tile of the layer waits for the weights
+                    const bool last_use = t + 2 >= T;     // and its last one releases them
                     if (l == 0 && first_use && !warp_wait(input_ready, (uint32_t)i & 1u, status, leader))
                         goto mma_drain;
                     // Tile t reads the rows the previous layer's tiles t-1..t+1 wrote
-                    // (tiles c-5, c-4, c-3), and tile c-4's epilogue also frees this
+                    // (tiles c-T-1, c-T, c-T+1), and tile c-4's epilogue frees this
                     // tile's accumulator. Each epilogue set finishes its tiles in order,
-                    // so tile c-3 stands for c-5 when t < T-1; the last tile has no
-                    // tile below it and waits for c-5 itself. The epilogue-done ring is
-                    // NDONE deep: no tile waited for here can be overtaken NDONE tiles
-                    // later before this tile is issued.
-                    if (c >= 4 && !warp_wait(epi_done + 8 * ((c - 4) % K::NDONE), (uint32_t)((c - 4) / K::NDONE) & 1u,
-                                             status, leader))
-                        goto mma_drain;
+                    // so of c-T-1 and c-T+1 (the same set) the later one stands for
+                    // both; the last tile has no tile below it and waits for c-T-1.
+                    // The epilogue-done ring is NDONE deep: no tile waited for here can
+                    // be overtaken NDONE tiles later before this tile is issued.
                     {
-                        const int dep = t == K::T - 1 ? c - 5 : c - 3;
-                        if (dep >= 0 && !warp_wait(epi_done + 8 * (dep % K::NDONE), (uint32_t)(dep / K::NDONE) & 1u,
-                                                   status, leader))
-                            goto mma_drain;
+                        const int deps[3] = {c - 4, c - T, t == T - 1 ? c - T - 1 : c - T + 1};
+#pragma unroll
+                        for (int j = 0; j < 3; ++j) {
+                            const int dep = deps[j];
+                            if (dep >= 0 && !warp_wait(epi_done + 8 * (dep % K::NDONE),
+                                                       (uint32_t)(dep / K::NDONE) & 1u, status, leader))
+                                goto mma_drain;
+                        }
                     }
                     const uint32_t d = tmem + (uint32_t)((c % K::NBUF) * K::NACC);
 #pragma unroll
@@ -793,9 +828,11 @@ __global__ void __launch_bounds__(Cols64::THREADS, 1)
         const uint32_t xbar = xchg + 8 * s;
         int c = 0, i = 0;
         bool first = true;
-        for (int g = blockIdx.x; g < groups; g += gridDim.x, ++i) {
-            const int base_img = g * K::G;
-            const int nimg = count - base_img < K::G ? count - base_img : K::G;
+        ColsGroup grp;
+        for (int gk = 0; cols_group(gk, cta, P, count, grp); ++gk, ++i) {
+            const int base_img = grp.base;
+            const int nimg = grp.nimg;
+            const int T = grp.tiles;
             if (first) {
                 for (int m = etid; m < K::G * 100; m += 32 * K::EPI_WARPS) build_input_row<C>(bufQ, m, base_img, nimg, in);
                 tc::fence_proxy_async_smem();
@@ -810,7 +847,7 @@ __global__ void __launch_bounds__(Cols64::THREADS, 1)
                 uint8_t* const out = l % 2 == 0 ? bufP : bufQ;
                 const bool residual = l >= 2 && l % 2 == 0;
                 const float* const bias = p.conv_b + l * C + ch0;
-                for (int t = 0; t < K::T; ++t, ++c) {
+                for (int t = 0; t < T; ++t, ++c) {
                     if ((c & 1) != s) continue;
                     const int b = c % K::NBUF, k = c >> 1;  // k: this set's tile count
                     const int x = k % 3;
@@ -890,13 +927,13 @@ __global__ void __launch_bounds__(Cols64::THREADS, 1)
             // so its MMAs can start, once the group's last MMAs (which read Q)
             // are complete: the last tile of each MMA warp.
             {
-                const int gn = g + gridDim.x;
-                if (gn < groups) {
+                ColsGroup next;
+                if (cols_group(gk + 1, cta, P, count, next)) {
                     for (int cl = c - 2; cl < c; ++cl)  // the last tile of each MMA warp
                         if (!warp_wait(acc_full + 8 * (cl % K::NBUF), (uint32_t)(cl / K::NBUF) & 1u, status, lane == 0))
                             goto epi_exit;
-                    const int nb = gn * K::G;
-                    const int nn = count - nb < K::G ? count - nb : K::G;
+                    const int nb = next.base;
+                    const int nn = next.nimg;
                     for (int mm = etid; mm < K::G * 100; mm += 32 * K::EPI_WARPS) build_input_row<C>(bufQ, mm, nb, nn, in);
                     tc::fence_proxy_async_smem();
                     __syncwarp();
@@ -960,8 +997,9 @@ int launch_tower_cols(const NetParams& p, const NetInput& in, float* headfeat, u
                    cudaSuccess;
         }))
         return launch_status();
-    const int64_t groups = (in.n + K::G - 1) / K::G;
-    const int grid = (int)(groups < kSmCount ? groups : kSmCount);
+    // Every CTA of a tail round takes at least two images (cols_group).
+    const int64_t half = (in.n + 1) / 2;
+    const int grid = (int)(half < kSmCount ? half : kSmCount);
     net_tower_cols_kernel<<<grid < 1 ? 1 : grid, K::THREADS, K::SMEM, stream>>>(p, in, headfeat, status);
     return launch_status();
 }
