@@ -876,7 +876,19 @@ __global__ void __launch_bounds__(Cols64::THREADS, 1)
                             for (int j = 0; j < 8; ++j) pre[8 * k2 + j] += (j & 1) ? bf16_hi(w[j >> 1]) : bf16_lo(w[j >> 1]);
                         }
                     }
-                    if (!warp_wait(acc_full + 8 * b, (uint32_t)(c / K::NBUF) & 1u, status, lane == 0)) goto epi_exit;
+                    // One warp of the set polls the accumulator's barrier; the other
+                    // seven sleep on the set's named barrier, which also carries a
+                    // timeout to all eight. Polling from every warp took shared-memory
+                    // cycles from the MMA operand reads.
+                    {
+                        int ok = 1;
+                        if ((e & 7) == 0 && lane == 0)
+                            ok = tc::mbar_wait(acc_full + 8 * b, (uint32_t)(c / K::NBUF) & 1u, status) ? 1 : 0;
+                        __syncwarp();
+                        const bool all_ok = tc::named_barrier_and(1 + s, 256, ok != 0);
+                        tc::tc_fence_after();
+                        if (!all_ok) goto epi_exit;
+                    }
                     const uint32_t taddr = tmem + lane_base + (uint32_t)(b * K::NACC + ch0);
                     float p1[32], p0[16];
                     tc::tmem_ld32_16(taddr + C, taddr, p1, p0);

@@ -101,6 +101,22 @@ __device__ __forceinline__ void named_barrier(int id, int threads) {
     asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");
 }
 
+// Named barrier `id` over `threads` threads (whole warps, converged) that also
+// reduces a predicate: true when every participant passed true. Waiting
+// threads sleep in the barrier unit rather than polling shared memory.
+__device__ __forceinline__ bool named_barrier_and(int id, int threads, bool value) {
+    uint32_t r;
+    asm volatile(
+        "{\n\t.reg .pred p, q;\n\t"
+        "setp.ne.u32 q, %1, 0;\n\t"
+        "bar.red.and.pred p, %2, %3, q;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(r)
+        : "r"((uint32_t)value), "r"(id), "r"(threads)
+        : "memory");
+    return r != 0;
+}
+
 // ---- tcgen05 -------------------------------------------------------------------
 __device__ __forceinline__ void tmem_alloc(uint32_t dst_smem, uint32_t cols) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(dst_smem), "r"(cols)
