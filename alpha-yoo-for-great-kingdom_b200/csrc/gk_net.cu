@@ -623,9 +623,8 @@ struct Cols64 {
     static constexpr int EPI0 = 1 + SETS;         // first epilogue warp (warp 0 loads weights)
     static constexpr int THREADS = 32 * (EPI0 + EPI_WARPS);
     static constexpr int NDONE = 8;               // epilogue-done barriers, a ring over tiles
-    // slot_full[3], slot_free[3], acc_full[4], epi_done[8], xchg[2], input_ready, mma_idle, heads_ready,
-    // heads_done
-    static constexpr int NBARS = 2 * NSLOT + NBUF + NDONE + SETS + 4;
+    // slot_full[3], slot_free[3], acc_full[4], epi_done[8], input_ready, mma_idle, heads_ready, heads_done
+    static constexpr int NBARS = 2 * NSLOT + NBUF + NDONE + 4;
     static constexpr int HEADW = (3 * C + 3 + 3) / 4 * 4;
     static constexpr int XFLOATS = SETS * 3 * 4 * 2 * 32;  // [set][3 tiles][4 quadrants][2 halves][32]
     static constexpr int SMEM = 2 * ACT + NSLOT * SLOT + NBARS * 8 + 16 + HEADW * 4 + XFLOATS * 4;
@@ -696,8 +695,7 @@ __global__ void __launch_bounds__(Cols64::THREADS, 1)
     const uint32_t slot_free = slot_full + 8 * K::NSLOT;
     const uint32_t acc_full = slot_free + 8 * K::NSLOT;
     const uint32_t epi_done = acc_full + 8 * K::NBUF;
-    const uint32_t xchg = epi_done + 8 * K::NDONE;
-    const uint32_t input_ready = xchg + 8 * K::SETS;
+    const uint32_t input_ready = epi_done + 8 * K::NDONE;
     const uint32_t mma_idle = input_ready + 8;
     const uint32_t heads_ready = mma_idle + 8;
     const uint32_t heads_done = heads_ready + 8;
@@ -717,7 +715,7 @@ __global__ void __launch_bounds__(Cols64::THREADS, 1)
             const uint32_t bar = slot_full + 8 * b;
             uint32_t n = 1u;                                           // producer / commit arrivals
             if ((bar >= slot_free && bar < acc_full) || bar == mma_idle) n = (uint32_t)K::SETS;  // each MMA warp
-            if (bar >= epi_done && bar < input_ready) n = 8u;          // one epilogue set (done, exchange)
+            if (bar >= epi_done && bar < input_ready) n = 8u;          // one epilogue set
             if (bar == input_ready || bar == heads_ready || bar == heads_done) n = (uint32_t)K::EPI_WARPS;
             tc::mbar_init(bar, n);
         }
@@ -825,7 +823,19 @@ __global__ void __launch_bounds__(Cols64::THREADS, 1)
         const int ch0 = 32 * h;
         const int etid = threadIdx.x - 32 * K::EPI0;
         const uint32_t lane_base = (uint32_t)(q * 32) << 16;
-        const uint32_t xbar = xchg + 8 * s;
+        // A wait of the whole set: its first warp polls the barrier (bounded)
+        // and the set's named barrier releases the other seven with the
+        // outcome, so they sleep instead of polling shared memory (which the
+        // MMA operand reads saturate). Named barrier 1 + s belongs to set s,
+        // 3 + s to its P1 exchange; a timeout ends all eight warps together.
+        auto set_wait = [&](uint32_t bar, uint32_t parity) -> bool {
+            int ok = 1;
+            if ((e & 7) == 0 && lane == 0) ok = tc::mbar_wait(bar, parity, status) ? 1 : 0;
+            __syncwarp();
+            const bool all_ok = tc::named_barrier_and(1 + s, 256, ok != 0);
+            tc::tc_fence_after();
+            return all_ok;
+        };
         int c = 0, i = 0;
         bool first = true;
         ColsGroup grp;
@@ -841,7 +851,7 @@ __global__ void __launch_bounds__(Cols64::THREADS, 1)
                 first = false;
             } else {
                 // The previous group's head pass (all warps) must have read buffer P.
-                if (!warp_wait(heads_done, (uint32_t)(i - 1) & 1u, status, lane == 0)) goto epi_exit;
+                if (!set_wait(heads_done, (uint32_t)(i - 1) & 1u)) goto epi_exit;
             }
             for (int l = 0; l < NL; ++l) {
                 uint8_t* const out = l % 2 == 0 ? bufP : bufQ;
@@ -876,19 +886,7 @@ __global__ void __launch_bounds__(Cols64::THREADS, 1)
                             for (int j = 0; j < 8; ++j) pre[8 * k2 + j] += (j & 1) ? bf16_hi(w[j >> 1]) : bf16_lo(w[j >> 1]);
                         }
                     }
-                    // One warp of the set polls the accumulator's barrier; the other
-                    // seven sleep on the set's named barrier, which also carries a
-                    // timeout to all eight. Polling from every warp took shared-memory
-                    // cycles from the MMA operand reads.
-                    {
-                        int ok = 1;
-                        if ((e & 7) == 0 && lane == 0)
-                            ok = tc::mbar_wait(acc_full + 8 * b, (uint32_t)(c / K::NBUF) & 1u, status) ? 1 : 0;
-                        __syncwarp();
-                        const bool all_ok = tc::named_barrier_and(1 + s, 256, ok != 0);
-                        tc::tc_fence_after();
-                        if (!all_ok) goto epi_exit;
-                    }
+                    if (!set_wait(acc_full + 8 * b, (uint32_t)(c / K::NBUF) & 1u)) goto epi_exit;
                     const uint32_t taddr = tmem + lane_base + (uint32_t)(b * K::NACC + ch0);
                     float p1[32], p0[16];
                     tc::tmem_ld32_16(taddr + C, taddr, p1, p0);
@@ -899,7 +897,6 @@ __global__ void __launch_bounds__(Cols64::THREADS, 1)
                         for (int j = 0; j < 8; ++j) w[j] = make_float4(p1[4 * j], p1[4 * j + 1], p1[4 * j + 2], p1[4 * j + 3]);
                     }
                     __syncwarp();
-                    if (lane == 0) tc::mbar_arrive(xbar);
                     // y[m] = P0[m] + P1[m + 1]: P1 of the next row comes from the next lane.
 #pragma unroll
                     for (int j = 0; j < 32; ++j) p1[j] = __shfl_down_sync(0xffffffffu, p1[j], 1);
@@ -914,7 +911,7 @@ __global__ void __launch_bounds__(Cols64::THREADS, 1)
                     // above; the wait comes after this warp's own TMEM reads so the
                     // other warps' publishing overlaps them. Quadrant 3's lane 31 is
                     // row 127, which belongs to the next tile and is not stored.
-                    if (!warp_wait(xbar, (uint32_t)k & 1u, status, lane == 0)) goto epi_exit;
+                    tc::named_barrier(3 + s, 256);
                     if (q < 3) {
                         const float4* const nb = reinterpret_cast<const float4*>(xp1 + (((s * 3 + x) * 4 + q + 1) * 2 + h) * 32);
 #pragma unroll
@@ -942,8 +939,7 @@ __global__ void __launch_bounds__(Cols64::THREADS, 1)
                 ColsGroup next;
                 if (cols_group(gk + 1, cta, P, count, next)) {
                     for (int cl = c - 2; cl < c; ++cl)  // the last tile of each MMA warp
-                        if (!warp_wait(acc_full + 8 * (cl % K::NBUF), (uint32_t)(cl / K::NBUF) & 1u, status, lane == 0))
-                            goto epi_exit;
+                        if (!set_wait(acc_full + 8 * (cl % K::NBUF), (uint32_t)(cl / K::NBUF) & 1u)) goto epi_exit;
                     const int nb = next.base;
                     const int nn = next.nimg;
                     for (int mm = etid; mm < K::G * 100; mm += 32 * K::EPI_WARPS) build_input_row<C>(bufQ, mm, nb, nn, in);
@@ -954,7 +950,7 @@ __global__ void __launch_bounds__(Cols64::THREADS, 1)
             }
             __syncwarp();
             if (lane == 0) tc::mbar_arrive(heads_ready);
-            if (!warp_wait(heads_ready, (uint32_t)i & 1u, status, lane == 0)) goto epi_exit;
+            if (!set_wait(heads_ready, (uint32_t)i & 1u)) goto epi_exit;
             for (int mm = etid; mm < K::G * 100; mm += 32 * K::EPI_WARPS) {
                 const int img = mm / 100, pos = mm - img * 100, r = pos / 10, cc = pos - r * 10;
                 if (!(img < nimg && r < 9 && cc < 9)) continue;

@@ -85,7 +85,30 @@ __global__ void puct_begin_kernel(PuctView v, int64_t B, int C, const gk_bits* r
     }
 }
 
-// One selection pass of tree t by its warp (every lane calls it).
+// This lane's three edges (actions lane, lane+32, lane+64) of node vtx.
+__device__ __forceinline__ void load_edges(const PuctView& v, int64_t vtx, int lane, int (&en)[3], double (&ep)[3],
+                                           double (&ew)[3], int (&ech)[3]) {
+    const int64_t ebase = vtx * GK_ACTIONS;
+#pragma unroll
+    for (int k = 0; k < 3; ++k) {
+        const int a = lane + 32 * k;
+        const bool in_row = a < GK_ACTIONS;
+        en[k] = in_row ? v.visits[ebase + a] : 0;
+        ep[k] = in_row ? v.prior[ebase + a] : 0.0;
+        ew[k] = in_row ? v.wsum[ebase + a] : 0.0;
+        ech[k] = in_row ? v.child[ebase + a] : -1;
+    }
+}
+
+// A path entry: the action taken (bits 0-7) and the player to move at the
+// parent (bits 8-9), so the backup needs neither the parent's state nor the
+// edge's child index (the child of entry d is the node of entry d + 1).
+__device__ __forceinline__ int32_t path_entry(int action, int actor) { return action | (actor << 8); }
+
+// One selection pass of tree t by its warp (every lane calls it). kPrefetch
+// loads a chosen child's edges with its state (one round trip per level, more
+// registers); without it a level loads its edges after its state.
+template <bool kPrefetch>
 __device__ __forceinline__ void select_tree(const PuctView& v, int64_t t, int C, const PuctOptions& o, int lane) {
     const int P = path_cap(C);
     if (lane == 0) v.needs_eval[t] = 0;
@@ -95,16 +118,21 @@ __device__ __forceinline__ void select_tree(const PuctView& v, int64_t t, int C,
     }
     const int64_t tbase = t * C;
     int node = 0, depth = 0;
-    // The current node's state and statistics stay in registers. All loads a
-    // tree level needs are issued together - the node's statistics with its
-    // state, and this lane's three edges (visits, prior, W, child) in one go -
-    // so a level costs two dependent global round trips. A child created
-    // during this pass is known to be unexpanded, so no lane reads memory
-    // another lane of this warp has just written.
+    // The current node's state, statistics and this lane's three edges
+    // (visits, prior, W, child) stay in registers. With kPrefetch, when an
+    // edge is chosen the child's state and statistics and its edges are
+    // loaded together, so a level costs one dependent global round trip; the
+    // edges of a leaf (unexpanded or terminal) are loaded and not used. They
+    // lie inside the tree's arrays, which are never read as anything but plain
+    // memory. A child created during this pass is known to be unexpanded, so
+    // no lane reads memory another lane of this warp has just written.
     gk_bits st = v.node_state[tbase];
     bool expanded = v.expanded[tbase] != 0;
     int node_n = v.node_visits[tbase];
     float node_q = v.node_value[tbase];
+    int en[3], ech[3];
+    double ep[3], ew[3];
+    if (kPrefetch) load_edges(v, tbase, lane, en, ep, ew, ech);
     bool fresh = false;
     for (;;) {
         const int64_t vtx = tbase + node;
@@ -120,17 +148,7 @@ __device__ __forceinline__ void select_tree(const PuctView& v, int64_t t, int C,
             break;
         }
         const int64_t ebase = vtx * GK_ACTIONS;
-        int en[3], ech[3];
-        double ep[3], ew[3];
-#pragma unroll
-        for (int k = 0; k < 3; ++k) {
-            const int a = lane + 32 * k;
-            const bool in_row = a < GK_ACTIONS;
-            en[k] = in_row ? v.visits[ebase + a] : 0;
-            ep[k] = in_row ? v.prior[ebase + a] : 0.0;
-            ew[k] = in_row ? v.wsum[ebase + a] : 0.0;
-            ech[k] = in_row ? v.child[ebase + a] : -1;
-        }
+        if (!kPrefetch) load_edges(v, vtx, lane, en, ep, ew, ech);
         const double scale = sqrt((double)node_n);
         const gk_b96 placements = legal_placements(st);
         bool allowed[3];
@@ -175,6 +193,7 @@ __device__ __forceinline__ void select_tree(const PuctView& v, int64_t t, int C,
             }
             break;
         }
+        const int actor = gk_actor(&st);  // the parent's player, recorded with the action
         // The chosen edge's child index is already in the lane that owns it.
         const int slot = best >> 5;
         int ch = __shfl_sync(kFull, slot == 0 ? ech[0] : slot == 1 ? ech[1] : ech[2], best & 31);
@@ -204,11 +223,12 @@ __device__ __forceinline__ void select_tree(const PuctView& v, int64_t t, int C,
             expanded = v.expanded[tbase + ch] != 0;
             node_n = v.node_visits[tbase + ch];
             node_q = v.node_value[tbase + ch];
+            if (kPrefetch) load_edges(v, tbase + ch, lane, en, ep, ew, ech);
             fresh = false;
         }
         if (lane == 0) {
             v.path_nodes[t * P + depth] = node;
-            v.path_actions[t * P + depth] = best;
+            v.path_actions[t * P + depth] = path_entry(best, actor);
         }
         ++depth;
         node = ch;
@@ -222,22 +242,41 @@ __device__ __forceinline__ void select_tree(const PuctView& v, int64_t t, int C,
 __global__ void __launch_bounds__(32 * kWarpsPerBlock, 7) puct_select_kernel(PuctView v, int64_t B, int C, PuctOptions o) {
     const int lane = threadIdx.x & 31;
     const int64_t t = (blockIdx.x * (int64_t)blockDim.x + threadIdx.x) >> 5;
-    if (t < B) select_tree(v, t, C, o, lane);
+    if (t < B) select_tree<true>(v, t, C, o, lane);
 }
 
 // Expansion of tree t's leaf with the evaluator's output and, if `backup`,
 // the backup along the selected path, by the tree's warp.
 __device__ __forceinline__ void expand_backup_tree(const PuctView& v, int64_t t, int C, const PuctOptions& o,
                                                    int backup, int lane) {
-    if (v.node_count[t] == 0) return;
+    // The tree's scalars, its policy row and the path length are loaded
+    // together, then the leaf's state with this lane's path entry, so the
+    // expansion and the backup take three dependent global round trips.
     const int P = path_cap(C);
+    const int64_t row = t * GK_ACTIONS;
+    const int count = v.node_count[t];
     const int node = v.leaf[t];
+    float leaf_value = v.leaf_value[t];
+    const bool eval = v.needs_eval[t] != 0;
+    const int len = backup ? v.path_len[t] : 0;
+    float pol[3];
+#pragma unroll
+    for (int k = 0; k < 3; ++k) pol[k] = lane + 32 * k < GK_ACTIONS ? v.policy[row + lane + 32 * k] : 0.0f;
+    if (count == 0) return;
     const int64_t vtx = t * C + node;
     const gk_bits st = v.node_state[vtx];
-    float leaf_value = v.leaf_value[t];
-    if (v.needs_eval[t]) {
+    // Depth `lane` of the path: parent node, entry (action and the parent's
+    // player) and child, the next entry's node or the leaf.
+    int path_parent = 0, path_action = 0, path_child = 0;
+    if (lane < len) {
+        path_parent = v.path_nodes[t * P + lane];
+        path_action = v.path_actions[t * P + lane];
+        path_child = lane + 1 < len ? v.path_nodes[t * P + lane + 1] : node;
+    }
+    if (eval) {
         const gk_b96 placements = legal_placements(st);
-        const int64_t ebase = vtx * GK_ACTIONS, row = t * GK_ACTIONS;
+        const int64_t ebase = vtx * GK_ACTIONS;
+        const bool mix = node == 0 && o.epsilon != 0.0;
         bool allowed[3];
         allow_bits(v, t, node, lane, allowed);
         bool bad = !(isfinite(leaf_value) && fabsf(leaf_value) <= 1.0f);
@@ -252,10 +291,10 @@ __device__ __forceinline__ void expand_backup_tree(const PuctView& v, int64_t t,
             w[k] = 0.0;
             nz[k] = 0.0;
             if (use[k]) {
-                const float p = v.policy[row + a];
+                const float p = pol[k];
                 bad |= !(isfinite(p) && p >= 0.0f);
                 w[k] = (double)p;
-                nz[k] = (double)v.noise[row + a];
+                if (mix) nz[k] = (double)v.noise[row + a];
                 largest = fmax(largest, w[k]);
                 ++legal_count;
             }
@@ -283,7 +322,6 @@ __device__ __forceinline__ void expand_backup_tree(const PuctView& v, int64_t t,
             total = (double)legal_count;
             leaf_value = 0.0f;
         }
-        const bool mix = node == 0 && o.epsilon != 0.0;
         double noise_total = 0.0;
         if (mix) noise_total = ordered_sum(nz, use);
         double prior[3];
@@ -326,18 +364,17 @@ __device__ __forceinline__ void expand_backup_tree(const PuctView& v, int64_t t,
     const int leaf_actor = gk_actor(&st);
     const double lv = (double)leaf_value;
     const int64_t tbase = t * C;
-    const int len = v.path_len[t];
     if (lane == 0) v.node_visits[tbase] += 1;
     for (int d = lane; d < len; d += 32) {
-        const int parent = v.path_nodes[t * P + d];
-        const int a = v.path_actions[t * P + d];
-        const int64_t pv = tbase + parent;
-        const int64_t e = pv * GK_ACTIONS + a;
-        const int parent_actor = (int)(v.node_state[pv].w[15] & 3u);
-        const double value = parent_actor == leaf_actor ? lv : -lv;
+        const bool first = d == lane;
+        const int parent = first ? path_parent : v.path_nodes[t * P + d];
+        const int entry = first ? path_action : v.path_actions[t * P + d];
+        const int child = first ? path_child : d + 1 < len ? v.path_nodes[t * P + d + 1] : node;
+        const int64_t e = (tbase + parent) * GK_ACTIONS + (entry & 0xff);
+        const double value = (entry >> 8) == leaf_actor ? lv : -lv;
         v.visits[e] += 1;
         v.wsum[e] = GK_DADD(v.wsum[e], value);
-        v.node_visits[tbase + v.child[e]] += 1;
+        v.node_visits[tbase + child] += 1;
     }
     if (lane == 0) v.sims[t] += 1;
 }
@@ -478,7 +515,7 @@ __global__ void __launch_bounds__(32 * kWarpsPerBlock, 8) puct_search_hash_kerne
     expand_backup_tree(v, t, C, o, 0, lane);
     __syncwarp();
     for (int i = 0; i < simulations; ++i) {
-        select_tree(v, t, C, o, lane);
+        select_tree<false>(v, t, C, o, lane);
         __syncwarp();
         hash_eval_tree(v, t, lane);
         __syncwarp();
