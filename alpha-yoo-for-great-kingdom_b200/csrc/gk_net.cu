@@ -1345,9 +1345,10 @@ int launch_heads(const NetParams& p, const float* headfeat, const NetInput& in, 
 inline bool valid_net(const gk_net_t* net) {
     if (!net || (net->channels != 32 && net->channels != 64 && net->channels != 128) || net->blocks < 0 ||
         net->blocks > 64 || !net->conv_w || !net->head_w || !net->pol_w || !net->pol_b || !net->val_w1 ||
-        !net->val_b1 || !net->val_w2 || !net->val_b2 || !aligned16(net->conv_w))
+        !net->val_b1 || !net->val_w2 || !net->val_b2 || !aligned16(net->conv_w) || !aligned16(net->pol_w) ||
+        !aligned16(net->val_w1))  // 16-byte copies and loads
         return false;
-    if (net->norm == 0) return net->conv_b && net->head_b;
+    if (net->norm == 0) return net->conv_b && aligned16(net->conv_b) && net->head_b;
     return net->norm == 1 && net->norm_w && net->norm_b && net->head_norm;
 }
 

@@ -241,7 +241,10 @@ GK_API int gk_puct_search_hash_noalloc(int64_t batch, int simulations, const uin
  * with norm_w/norm_b fp32 [layers][C] (eps 1e-5), the policy and value 1x1
  * convolutions by GroupNorm(1, 2) and GroupNorm(1, 1) with head_norm fp32[6] =
  * {policy weight[2], policy bias[2], value weight, value bias}, and a value
- * hidden width of C; conv_b and head_b are unused. */
+ * hidden width of C; conv_b and head_b are unused.
+ *
+ * conv_w, pol_w, val_w1 and (norm 0) conv_b must be 16-byte aligned: the
+ * kernels read them with 16-byte copies. Anything else is GK_EINVAL. */
 typedef struct {
     int channels; /* 32, 64 or 128 */
     int blocks;   /* residual blocks */

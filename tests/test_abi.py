@@ -107,3 +107,26 @@ def test_collect_gpu_puct_games_validates_like_the_reference():
         games = args.pop("games")
         with pytest.raises(exc):
             collect_gpu_puct_games(HashEvaluator(), games, **args)
+
+
+def test_network_pointers_must_be_16_byte_aligned():
+    """gk_net_forward refuses a network whose bulk-copied arrays are not
+    16-byte aligned before it touches the GPU (the pointers are never read)."""
+    if not LIBRARY.exists():
+        pytest.skip("libgk.so not built")
+    from kingdom_ai._native import NetStruct
+
+    lib = ctypes.CDLL(str(LIBRARY))
+    fn = lib.gk_net_forward
+    fn.argtypes = [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int64, ctypes.c_void_p,
+                   ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p]
+    fn.restype = ctypes.c_int
+    base = 1 << 20
+    names = ["conv_w", "conv_b", "head_w", "head_b", "pol_w", "pol_b", "val_w1", "val_b1", "val_w2", "val_b2"]
+    for bad in ("conv_w", "conv_b", "pol_w", "val_w1"):
+        net = NetStruct()
+        net.channels, net.blocks, net.norm = 64, 6, 0
+        for k, name in enumerate(names):
+            setattr(net, name, base + 4096 * k + (4 if name == bad else 0))
+        rc = fn(ctypes.byref(net), base, None, 8, base, base, base, base, None)
+        assert rc == -22, bad
