@@ -912,17 +912,17 @@ __global__ void __launch_bounds__(Cols64::THREADS, 1)
                     // other warps' publishing overlaps them. Quadrant 3's lane 31 is
                     // row 127, which belongs to the next tile and is not stored.
                     tc::named_barrier(3 + s, 256);
-                    if (q < 3) {
+                    // Only lane 31 loads: a load every lane issues returns 512 bytes
+                    // per 16-byte load through the shared-memory pipe.
+                    if (q < 3 && lane == 31) {
                         const float4* const nb = reinterpret_cast<const float4*>(xp1 + (((s * 3 + x) * 4 + q + 1) * 2 + h) * 32);
 #pragma unroll
                         for (int j = 0; j < 8; ++j) {
                             const float4 v = nb[j];
-                            if (lane == 31) {
-                                p1[4 * j] = v.x;
-                                p1[4 * j + 1] = v.y;
-                                p1[4 * j + 2] = v.z;
-                                p1[4 * j + 3] = v.w;
-                            }
+                            p1[4 * j] = v.x;
+                            p1[4 * j + 1] = v.y;
+                            p1[4 * j + 2] = v.z;
+                            p1[4 * j + 3] = v.w;
                         }
                     }
                     if (m < K::G * 100 && !(q == 3 && lane == 31)) store_row32(row, pre, p1, valid);
