@@ -240,6 +240,34 @@ def test_integer_network_is_exact(selftest, channels, blocks, n):
     assert (logits - ref_logits).abs().max().item() <= 1e-5 * scale
 
 
+@pytest.mark.parametrize("channels,blocks", [(64, 6), (128, 2)])
+def test_outputs_do_not_depend_on_batch_size_or_slot(selftest, channels, blocks):
+    """A position's outputs are bit-identical whatever the batch around it.
+
+    Every batch size maps images to different CTAs, image groups and 128-row
+    tiles (full rounds of five-image groups, then the balanced tail of 2-5
+    images per CTA), so sizes around the round boundaries of a 148-SM grid
+    check that every image is computed exactly once; a permuted batch checks
+    that the row a position lands on does not change its arithmetic.
+    """
+    from kingdom_ai.model import NativePolicyValueNet, random_network
+
+    native_or_fail(selftest)
+    n = 3001
+    bits = positions(n, 4242)
+    net = NativePolicyValueNet(random_network(channels, blocks, 5), device="cuda")
+    full_logits, full_values = net.forward_states(bits)
+    for m in (1, 2, 3, 7, 11, 147, 148, 149, 295, 296, 297, 739, 740, 741, 1479, 1481, 2221, 2960, 3000):
+        logits, values = net.forward_states(bits[:m].contiguous())
+        assert torch.equal(logits, full_logits[:m]), m
+        assert torch.equal(values, full_values[:m]), m
+    perm = torch.randperm(n, generator=torch.Generator().manual_seed(9)).cuda()
+    logits, values = net.forward_states(bits[perm].contiguous())
+    torch.cuda.synchronize()
+    net.check()
+    assert torch.equal(logits, full_logits[perm]) and torch.equal(values, full_values[perm])
+
+
 def test_native_network_in_search(selftest, oracle):
     """GpuPUCT routes a PolicyValueNet to the native evaluator; results are a valid search."""
     import kingdom_ai
