@@ -443,7 +443,18 @@ __global__ void __launch_bounds__(NetCfg<C>::THREADS, NetCfg<C>::MIN_BLOCKS)
         const int col0 = (e >> 2) * HALF; // this warp's channels [col0, col0 + C/2)
         const int etid = threadIdx.x - 64;
         constexpr bool gn = GN;
-        uint32_t gn_phase = 0;
+        // A wait of all eight epilogue warps: warp 0 polls the barrier
+        // (bounded) and named barrier 1 releases the other seven with the
+        // outcome, so they sleep instead of polling shared memory while the
+        // MMAs read their operands from it; a timeout ends all eight together.
+        auto group_wait = [&](uint32_t bar, uint32_t parity) -> bool {
+            int ok = 1;
+            if (e == 0 && lane == 0) ok = tc::mbar_wait(bar, parity, status) ? 1 : 0;
+            __syncwarp();
+            const bool all_ok = tc::named_barrier_and(1, 32 * K::EPI_WARPS, ok != 0);
+            tc::tc_fence_after();
+            return all_ok;
+        };
         int i = 0;
         for (int g = blockIdx.x; g < groups; g += gridDim.x, ++i) {
             const int base_img = g * K::G;
@@ -470,19 +481,17 @@ __global__ void __launch_bounds__(NetCfg<C>::THREADS, NetCfg<C>::MIN_BLOCKS)
                     // GroupNorm statistics: sums of x and x^2 per (image,
                     // group) slot, then a bounded barrier of the eight warps.
                     for (int t = 0; t < K::T; ++t) {
-                        if (!warp_wait(acc_full + 8 * t, (uint32_t)a & 1u, status, lane == 0)) goto epi_done_label;
-                        tc::tc_fence_after();
+                        if (!group_wait(acc_full + 8 * t, (uint32_t)a & 1u)) goto epi_done_label;
                         gn_partials<C>(tq + t * C, t, q, lane, col0, nimg, gn_sum, gn_sq);
                     }
+                    // Every warp's partial sums are written (no warp leaves between
+                    // the waits above and this barrier).
                     __syncwarp();
-                    if (lane == 0) tc::mbar_arrive(gn_ready);
-                    if (!warp_wait(gn_ready, gn_phase & 1u, status, lane == 0)) goto epi_done_label;
-                    ++gn_phase;
+                    tc::named_barrier(2, 32 * K::EPI_WARPS);
                     __threadfence_block();
                 }
                 for (int t = 0; t < K::T; ++t) {
-                    if (!gn && !warp_wait(acc_full + 8 * t, (uint32_t)a & 1u, status, lane == 0)) goto epi_done_label;
-                    tc::tc_fence_after();
+                    if (!gn && !group_wait(acc_full + 8 * t, (uint32_t)a & 1u)) goto epi_done_label;
                     const int m = t * 128 + q * 32 + lane;
                     const int img = m / 100, pos = m - img * 100, r = pos / 10, cc = pos - r * 10;
                     const bool valid = img < nimg && r < 9 && cc < 9;
@@ -547,8 +556,7 @@ __global__ void __launch_bounds__(NetCfg<C>::THREADS, NetCfg<C>::MIN_BLOCKS)
             // Head pass: the 1x1 policy (2) and value (1) convolutions over the
             // final rows, once all eight warps have written them.
             __syncwarp();
-            if (lane == 0) tc::mbar_arrive(heads_ready);
-            if (!warp_wait(heads_ready, (uint32_t)i & 1u, status, lane == 0)) goto epi_done_label;
+            tc::named_barrier(3, 32 * K::EPI_WARPS);
             for (int m = etid; m < K::T * 128; m += 32 * K::EPI_WARPS) {
                 const int img = m / 100, pos = m - img * 100, r = pos / 10, cc = pos - r * 10;
                 if (!(img < nimg && r < 9 && cc < 9)) continue;
