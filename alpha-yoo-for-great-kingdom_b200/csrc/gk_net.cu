@@ -71,7 +71,7 @@ struct NetCfg {
     // GroupNorm partial sums: [image][group][32-row chunk of the image, <= 5]
     static constexpr int GN_PARTS = G * 8 * 5;
     static constexpr int THREADS = 64 + 32 * EPI_WARPS;
-    static constexpr int NBARS = 2 * NSLOT + 2 * T + 3;  // + mma_idle, heads_ready, gn_ready
+    static constexpr int NBARS = 2 * NSLOT + 2 * T + 1;  // + mma_idle
     static constexpr int HEADW = (3 * C + 3 + 3) / 4 * 4;  // head 1x1 weights + biases (floats)
     static constexpr int SMEM = 2 * ACT + NSLOT * SLOT + NBARS * 8 + 16 + HEADW * 4 + 2 * GN_PARTS * 4;
     static constexpr uint32_t IDESC = tc::idesc_bf16(128, C);
@@ -362,8 +362,6 @@ __global__ void __launch_bounds__(NetCfg<C>::THREADS, NetCfg<C>::MIN_BLOCKS)
     const uint32_t acc_full = slot_free + 8 * K::NSLOT;
     const uint32_t epi_done = acc_full + 8 * K::T;
     const uint32_t mma_idle = epi_done + 8 * K::T;
-    const uint32_t heads_ready = mma_idle + 8;
-    const uint32_t gn_ready = heads_ready + 8;
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int NL = 1 + 2 * p.blocks;  // MMA layers per group
@@ -377,10 +375,10 @@ __global__ void __launch_bounds__(NetCfg<C>::THREADS, NetCfg<C>::MIN_BLOCKS)
     if (threadIdx.x < 3) headw[3 * C + threadIdx.x] = p.norm ? 0.0f : p.head_b[threadIdx.x];
     tc::fence_proxy_async_smem();
     if (threadIdx.x == 0) {
-        // epi_done and heads_ready complete when every epilogue warp has arrived.
+        // epi_done completes when every epilogue warp has arrived.
         for (int b = 0; b < K::NBARS; ++b) {
             const uint32_t bar = slot_full + 8 * b;
-            const bool per_warp = (bar >= epi_done && bar < mma_idle) || bar == heads_ready || bar == gn_ready;
+            const bool per_warp = bar >= epi_done && bar < mma_idle;
             tc::mbar_init(bar, per_warp ? (uint32_t)K::EPI_WARPS : 1u);
         }
         tc::fence_mbar_init();
@@ -479,7 +477,7 @@ __global__ void __launch_bounds__(NetCfg<C>::THREADS, NetCfg<C>::MIN_BLOCKS)
                 }
                 if constexpr (GN) {
                     // GroupNorm statistics: sums of x and x^2 per (image,
-                    // group) slot, then a bounded barrier of the eight warps.
+                    // group) slot, then a named barrier of the eight warps.
                     for (int t = 0; t < K::T; ++t) {
                         if (!group_wait(acc_full + 8 * t, (uint32_t)a & 1u)) goto epi_done_label;
                         gn_partials<C>(tq + t * C, t, q, lane, col0, nimg, gn_sum, gn_sq);
