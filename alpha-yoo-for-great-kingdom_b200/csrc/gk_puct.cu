@@ -122,10 +122,11 @@ __device__ __forceinline__ void select_tree(const PuctView& v, int64_t t, int C,
     // (visits, prior, W, child) stay in registers. With kPrefetch, when an
     // edge is chosen the child's state and statistics and its edges are
     // loaded together, so a level costs one dependent global round trip; the
-    // edges of a leaf (unexpanded or terminal) are loaded and not used. They
-    // lie inside the tree's arrays, which are never read as anything but plain
-    // memory. A child created during this pass is known to be unexpanded, so
-    // no lane reads memory another lane of this warp has just written.
+    // edges of a leaf (unexpanded or terminal) are loaded and not used. Those
+    // loads stay inside the tree's edge arrays (every node slot is below the
+    // capacity), so rows never written are read harmlessly and ignored. A child
+    // created during this pass is known to be unexpanded, so no lane reads
+    // memory another lane of this warp has just written.
     gk_bits st = v.node_state[tbase];
     bool expanded = v.expanded[tbase] != 0;
     int node_n = v.node_visits[tbase];
