@@ -45,19 +45,23 @@ __device__ __forceinline__ float terminal_value(const gk_bits& s) {
     return gk_winner(&s) == gk_actor(&s) ? 1.0f : -1.0f;
 }
 
+// Per-warp shared scratch of an ordered sum: one double per action.
+constexpr int kSumScratch = 96;
+
 // Sum of per-lane values v[k] (action a = lane + 32k) over selected actions in
-// increasing action order; every lane returns the same total.
-__device__ __forceinline__ double ordered_sum(const double (&v)[3], const bool (&use)[3]) {
+// increasing action order; every lane returns the same total. The values pass
+// through the warp's scratch `sc`, unselected ones as +0.0: every caller's
+// selected values are >= +0 or sums that start at +0, so the running total is
+// never -0 and adding +0.0 leaves it bit-identical to skipping the action.
+__device__ __forceinline__ double ordered_sum(const double (&v)[3], const bool (&use)[3], double* sc, int lane) {
+#pragma unroll
+    for (int k = 0; k < 3; ++k)
+        if (lane + 32 * k < GK_ACTIONS) sc[lane + 32 * k] = use[k] ? v[k] : 0.0;
+    __syncwarp();
     double total = 0.0;
-    // Unrolled so the shuffles of later actions issue while the adds, which
-    // stay in action order, wait on one another.
 #pragma unroll 8
-    for (int a = 0; a < GK_ACTIONS; ++a) {
-        const int k = a >> 5, src = a & 31;
-        const double x = __shfl_sync(kFull, k == 0 ? v[0] : k == 1 ? v[1] : v[2], src);
-        const bool u = __shfl_sync(kFull, k == 0 ? use[0] : k == 1 ? use[1] : use[2], src);
-        if (u) total = GK_DADD(total, x);
-    }
+    for (int a = 0; a < GK_ACTIONS; ++a) total = GK_DADD(total, sc[a]);
+    __syncwarp();  // every lane has read the scratch before it is written again
     return total;
 }
 
@@ -249,7 +253,7 @@ __global__ void __launch_bounds__(32 * kWarpsPerBlock, 7) puct_select_kernel(Puc
 // Expansion of tree t's leaf with the evaluator's output and, if `backup`,
 // the backup along the selected path, by the tree's warp.
 __device__ __forceinline__ void expand_backup_tree(const PuctView& v, int64_t t, int C, const PuctOptions& o,
-                                                   int backup, int lane) {
+                                                   int backup, int lane, double* sc) {
     // The tree's scalars, its policy row and the path length are loaded
     // together, then the leaf's state with this lane's path entry, so the
     // expansion and the backup take three dependent global round trips.
@@ -311,7 +315,7 @@ __device__ __forceinline__ void expand_backup_tree(const PuctView& v, int64_t t,
             double scaled[3];
 #pragma unroll
             for (int k = 0; k < 3; ++k) scaled[k] = use[k] ? w[k] / largest : 0.0;
-            total = ordered_sum(scaled, use);
+            total = ordered_sum(scaled, use, sc, lane);
         }
         if (bad || legal_count == 0 || !(total > 0.0) || !isfinite(total)) {
             // Mirrors the reference's handling of a bad evaluation: flag it,
@@ -324,7 +328,7 @@ __device__ __forceinline__ void expand_backup_tree(const PuctView& v, int64_t t,
             leaf_value = 0.0f;
         }
         double noise_total = 0.0;
-        if (mix) noise_total = ordered_sum(nz, use);
+        if (mix) noise_total = ordered_sum(nz, use, sc, lane);
         double prior[3];
 #pragma unroll
         for (int k = 0; k < 3; ++k) {
@@ -339,7 +343,7 @@ __device__ __forceinline__ void expand_backup_tree(const PuctView& v, int64_t t,
         }
         if (mix) {
             bool all[3] = {true, true, lane + 64 < GK_ACTIONS};
-            const double combined = ordered_sum(prior, all);
+            const double combined = ordered_sum(prior, all, sc, lane);
 #pragma unroll
             for (int k = 0; k < 3; ++k) prior[k] = prior[k] / combined;
         }
@@ -384,7 +388,8 @@ __global__ void __launch_bounds__(32 * kWarpsPerBlock) puct_expand_backup_kernel
                                                                                  PuctOptions o, int backup) {
     const int lane = threadIdx.x & 31;
     const int64_t t = (blockIdx.x * (int64_t)blockDim.x + threadIdx.x) >> 5;
-    if (t < B) expand_backup_tree(v, t, C, o, backup, lane);
+    __shared__ double sum_scratch[kWarpsPerBlock][kSumScratch];
+    if (t < B) expand_backup_tree(v, t, C, o, backup, lane, sum_scratch[threadIdx.x >> 5]);
 }
 
 struct PuctOutputs {
@@ -402,6 +407,7 @@ struct PuctOutputs {
 };
 
 __global__ void __launch_bounds__(32 * kWarpsPerBlock) puct_finish_kernel(PuctView v, int64_t B, int C, PuctOutputs out) {
+    __shared__ double sum_scratch[kWarpsPerBlock][kSumScratch];
     const int lane = threadIdx.x & 31;
     const int64_t t = (blockIdx.x * (int64_t)blockDim.x + threadIdx.x) >> 5;
     if (t >= B) return;
@@ -470,7 +476,7 @@ __global__ void __launch_bounds__(32 * kWarpsPerBlock) puct_finish_kernel(PuctVi
             best_p = op;
         }
     }
-    const double root_sum = ordered_sum(ws, use);
+    const double root_sum = ordered_sum(ws, use, sum_scratch[threadIdx.x >> 5], lane);
     if (lane == 0) {
         const double rv = sims > 0 ? root_sum / (double)sims : 0.0;
         if (out.actions) out.actions[t] = best;
@@ -506,21 +512,24 @@ __global__ void __launch_bounds__(32 * kWarpsPerBlock) puct_hash_eval_kernel(Puc
 // and each warp runs root expansion and every simulation back to back. The
 // per-tree arithmetic is that of the separate select / evaluate / expand
 // kernels; __syncwarp orders each phase's writes before the next phase reads.
-__global__ void __launch_bounds__(32 * kWarpsPerBlock, 8) puct_search_hash_kernel(PuctView v, int64_t B, int C,
+// Four blocks per SM: up to 128 registers, so the fused loop does not spill;
+// the C3 search (1,024 trees) needs fewer than two blocks per SM.
+__global__ void __launch_bounds__(32 * kWarpsPerBlock, 4) puct_search_hash_kernel(PuctView v, int64_t B, int C,
                                                                                   PuctOptions o, int simulations) {
+    __shared__ double sum_scratch[kWarpsPerBlock][kSumScratch];
     const int lane = threadIdx.x & 31;
     const int64_t t = (blockIdx.x * (int64_t)blockDim.x + threadIdx.x) >> 5;
     if (t >= B) return;
     hash_eval_tree(v, t, lane);
     __syncwarp();
-    expand_backup_tree(v, t, C, o, 0, lane);
+    expand_backup_tree(v, t, C, o, 0, lane, sum_scratch[threadIdx.x >> 5]);
     __syncwarp();
     for (int i = 0; i < simulations; ++i) {
         select_tree<false>(v, t, C, o, lane);
         __syncwarp();
         hash_eval_tree(v, t, lane);
         __syncwarp();
-        expand_backup_tree(v, t, C, o, 1, lane);
+        expand_backup_tree(v, t, C, o, 1, lane, sum_scratch[threadIdx.x >> 5]);
         __syncwarp();
     }
 }
