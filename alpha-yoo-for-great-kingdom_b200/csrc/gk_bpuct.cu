@@ -155,14 +155,22 @@ __device__ __forceinline__ bool same_state(const gk_bits& a, const gk_bits& b) {
 }
 
 // Sum in action order of v[k] (action lane + 32k) over the actions with use[k].
+// The values pass through the warp's slice of a block-wide scratch (every
+// tree kernel runs kWarps warps per block), unselected ones as +0.0: the
+// callers' values are >= +0 or differences of sums that start at +0, so the
+// running total is never -0 and adding +0.0 equals skipping the action.
 __device__ __forceinline__ double ordered_sum(const double (&v)[3], const bool (&use)[3]) {
+    __shared__ double scratch[kWarps][96];
+    const int lane = threadIdx.x & 31;
+    double* const sc = scratch[threadIdx.x >> 5];
+#pragma unroll
+    for (int k = 0; k < 3; ++k)
+        if (lane + 32 * k < GK_ACTIONS) sc[lane + 32 * k] = use[k] ? v[k] : 0.0;
+    __syncwarp();
     double total = 0.0;
-    for (int a = 0; a < GK_ACTIONS; ++a) {
-        const int k = a >> 5, src = a & 31;
-        const double x = __shfl_sync(kFull, k == 0 ? v[0] : k == 1 ? v[1] : v[2], src);
-        const bool u = __shfl_sync(kFull, k == 0 ? use[0] : k == 1 ? use[1] : use[2], src);
-        if (u) total = GK_DADD(total, x);
-    }
+#pragma unroll 8
+    for (int a = 0; a < GK_ACTIONS; ++a) total = GK_DADD(total, sc[a]);
+    __syncwarp();  // every lane has read the scratch before it is written again
     return total;
 }
 
