@@ -613,32 +613,48 @@ __global__ void puct_noise_kernel(PuctView v, int64_t B, int C, uint64_t seed, u
 
 // Ordered compaction of trees whose leaf needs the evaluator (single block).
 __global__ void __launch_bounds__(1024) puct_compact_kernel(PuctView v, int64_t B) {
+    // Each thread takes kPer consecutive trees, so one pass of the block covers
+    // 4,096 trees; the active list keeps increasing tree order.
+    constexpr int kPer = 4;
     __shared__ int warp_sums[32];
     __shared__ int carry;
     if (threadIdx.x == 0) carry = 0;
     __syncthreads();
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    for (int64_t base = 0; base < B; base += blockDim.x) {
-        const int64_t t = base + threadIdx.x;
-        const int flag = (t < B && v.needs_eval[t]) ? 1 : 0;
-        const unsigned ballot = __ballot_sync(kFull, flag);
-        const int in_warp = __popc(ballot & ((1u << lane) - 1u));
-        if (lane == 31) warp_sums[warp] = in_warp + flag;
+    const int warps = (int)(blockDim.x >> 5);
+    for (int64_t base = 0; base < B; base += (int64_t)blockDim.x * kPer) {
+        const int64_t t0 = base + (int64_t)threadIdx.x * kPer;
+        bool flag[kPer];
+        int count = 0;
+#pragma unroll
+        for (int j = 0; j < kPer; ++j) {
+            flag[j] = t0 + j < B && v.needs_eval[t0 + j] != 0;
+            count += flag[j] ? 1 : 0;
+        }
+        int x = count;  // inclusive prefix over the warp's threads
+#pragma unroll
+        for (int off = 1; off < 32; off <<= 1) {
+            const int y = __shfl_up_sync(kFull, x, off);
+            if (lane >= off) x += y;
+        }
+        if (lane == 31) warp_sums[warp] = x;
         __syncthreads();
         if (warp == 0) {
-            int x = lane < (int)(blockDim.x >> 5) ? warp_sums[lane] : 0;
+            int w = lane < warps ? warp_sums[lane] : 0;
 #pragma unroll
             for (int off = 1; off < 32; off <<= 1) {
-                const int y = __shfl_up_sync(kFull, x, off);
-                if (lane >= off) x += y;
+                const int y = __shfl_up_sync(kFull, w, off);
+                if (lane >= off) w += y;
             }
-            warp_sums[lane] = x;  // inclusive prefix over warps
+            warp_sums[lane] = w;  // inclusive prefix over warps
         }
         __syncthreads();
-        const int before = (warp > 0 ? warp_sums[warp - 1] : 0) + in_warp;
-        if (flag) v.active[carry + before] = (int32_t)t;
+        int pos = carry + (warp > 0 ? warp_sums[warp - 1] : 0) + x - count;
+#pragma unroll
+        for (int j = 0; j < kPer; ++j)
+            if (flag[j]) v.active[pos++] = (int32_t)(t0 + j);
         __syncthreads();
-        if (threadIdx.x == 0) carry += warp_sums[(blockDim.x >> 5) - 1];
+        if (threadIdx.x == 0) carry += warp_sums[warps - 1];
         __syncthreads();
     }
     if (threadIdx.x == 0) *v.active_count = carry;
