@@ -1131,7 +1131,7 @@ __global__ void __launch_bounds__(32 * kHeadWarps) net_heads_kernel(NetParams p,
         float la[kHeadPos], lb[kHeadPos], lc[kHeadPos];
 #pragma unroll
         for (int u = 0; u < kHeadPos; ++u) la[u] = lb[u] = lc[u] = 0.f;
-#pragma unroll 3
+#pragma unroll 9
         for (int j = 0; j < 162; ++j) {
             const float xa = wa[j * GK_ACTIONS], xb = wb[j * GK_ACTIONS], xc = wc[j * GK_ACTIONS];
 #pragma unroll
@@ -1149,7 +1149,7 @@ __global__ void __launch_bounds__(32 * kHeadWarps) net_heads_kernel(NetParams p,
 #pragma unroll
             for (int u = 0; u < kHeadPos; ++u) hv[k][u] = b;
         }
-#pragma unroll 3
+#pragma unroll 9
         for (int j = 0; j < 81; ++j) {
             float x[HU];
 #pragma unroll
