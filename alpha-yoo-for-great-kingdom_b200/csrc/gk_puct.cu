@@ -178,19 +178,33 @@ __device__ __forceinline__ void select_tree(const PuctView& v, int64_t t, int C,
             }
         }
         // Warp argmax: higher score, then higher prior, then lower action index.
+        // Each lane's candidate is already the best of its own edges in that
+        // order, so when a single lane holds the highest score its candidate
+        // is the answer; ties (and no candidate at all) take the full
+        // reduction.
+        {
+            double top = best >= 0 ? best_score : -INFINITY;
 #pragma unroll
-        for (int off = 16; off; off >>= 1) {
-            const double os = __shfl_down_sync(kFull, best_score, off);
-            const double op = __shfl_down_sync(kFull, best_prior, off);
-            const int oa = __shfl_down_sync(kFull, best, off);
-            if (oa >= 0 && (best < 0 || os > best_score ||
-                            (os == best_score && (op > best_prior || (op == best_prior && oa < best))))) {
-                best = oa;
-                best_score = os;
-                best_prior = op;
+            for (int off = 16; off; off >>= 1) top = fmax(top, __shfl_xor_sync(kFull, top, off));
+            const unsigned holders = __ballot_sync(kFull, best >= 0 && best_score == top);
+            if (__popc(holders) == 1) {
+                best = __shfl_sync(kFull, best, __ffs(holders) - 1);
+            } else {
+#pragma unroll
+                for (int off = 16; off; off >>= 1) {
+                    const double os = __shfl_down_sync(kFull, best_score, off);
+                    const double op = __shfl_down_sync(kFull, best_prior, off);
+                    const int oa = __shfl_down_sync(kFull, best, off);
+                    if (oa >= 0 && (best < 0 || os > best_score ||
+                                    (os == best_score && (op > best_prior || (op == best_prior && oa < best))))) {
+                        best = oa;
+                        best_score = os;
+                        best_prior = op;
+                    }
+                }
+                best = __shfl_sync(kFull, best, 0);
             }
         }
-        best = __shfl_sync(kFull, best, 0);
         if (best < 0 || depth >= P) {
             if (lane == 0) {
                 v.errors[t] |= GK_ERR_CAPACITY;
