@@ -355,22 +355,39 @@ __device__ int select_leaf(const BpuctView& v, int64_t t, int C, double c_puct, 
                 best_prior = p;
             }
         }
+        // Warp argmax (higher score, then higher prior, then lower action).
+        // Each lane's candidate is already the best of its own edges in that
+        // order, so a single lane holding the highest score has the answer;
+        // ties (and no candidate) take the full reduction.
+        int ch;
+        {
+            double top = best >= 0 ? best_score : -INFINITY;
 #pragma unroll
-        for (int off = 16; off; off >>= 1) {
-            const double os = __shfl_down_sync(kFull, best_score, off);
-            const double op = __shfl_down_sync(kFull, best_prior, off);
-            const int oa = __shfl_down_sync(kFull, best, off);
-            const int oc = __shfl_down_sync(kFull, best_child, off);
-            if (oa >= 0 && (best < 0 || os > best_score ||
-                            (os == best_score && (op > best_prior || (op == best_prior && oa < best))))) {
-                best = oa;
-                best_child = oc;
-                best_score = os;
-                best_prior = op;
+            for (int off = 16; off; off >>= 1) top = fmax(top, __shfl_xor_sync(kFull, top, off));
+            const unsigned holders = __ballot_sync(kFull, best >= 0 && best_score == top);
+            if (__popc(holders) == 1) {
+                const int src = __ffs(holders) - 1;
+                best = __shfl_sync(kFull, best, src);
+                ch = __shfl_sync(kFull, best_child, src);
+            } else {
+#pragma unroll
+                for (int off = 16; off; off >>= 1) {
+                    const double os = __shfl_down_sync(kFull, best_score, off);
+                    const double op = __shfl_down_sync(kFull, best_prior, off);
+                    const int oa = __shfl_down_sync(kFull, best, off);
+                    const int oc = __shfl_down_sync(kFull, best_child, off);
+                    if (oa >= 0 && (best < 0 || os > best_score ||
+                                    (os == best_score && (op > best_prior || (op == best_prior && oa < best))))) {
+                        best = oa;
+                        best_child = oc;
+                        best_score = os;
+                        best_prior = op;
+                    }
+                }
+                best = __shfl_sync(kFull, best, 0);
+                ch = __shfl_sync(kFull, best_child, 0);
             }
         }
-        best = __shfl_sync(kFull, best, 0);
-        int ch = __shfl_sync(kFull, best_child, 0);
         if (best < 0 || depth >= P) {
             if (lane == 0) v.errors[t] |= GK_ERR_CAPACITY;
             return -2;
