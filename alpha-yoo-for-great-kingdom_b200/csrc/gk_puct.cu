@@ -109,10 +109,7 @@ __device__ __forceinline__ void load_edges(const PuctView& v, int64_t vtx, int l
 // edge's child index (the child of entry d is the node of entry d + 1).
 __device__ __forceinline__ int32_t path_entry(int action, int actor) { return action | (actor << 8); }
 
-// One selection pass of tree t by its warp (every lane calls it). kPrefetch
-// loads a chosen child's edges with its state (one round trip per level, more
-// registers); without it a level loads its edges after its state.
-template <bool kPrefetch>
+// One selection pass of tree t by its warp (every lane calls it).
 __device__ __forceinline__ void select_tree(const PuctView& v, int64_t t, int C, const PuctOptions& o, int lane) {
     const int P = path_cap(C);
     if (lane == 0) v.needs_eval[t] = 0;
@@ -122,13 +119,11 @@ __device__ __forceinline__ void select_tree(const PuctView& v, int64_t t, int C,
     }
     const int64_t tbase = t * C;
     int node = 0, depth = 0;
-    // The current node's state, statistics and this lane's three edges
-    // (visits, prior, W, child) stay in registers. With kPrefetch, when an
-    // edge is chosen the child's state and statistics and its edges are
-    // loaded together, so a level costs one dependent global round trip; the
-    // edges of a leaf (unexpanded or terminal) are loaded and not used. Those
-    // loads stay inside the tree's edge arrays (every node slot is below the
-    // capacity), so rows never written are read harmlessly and ignored. A child
+    // The current node's state and statistics stay in registers; a level
+    // loads its edges (this lane's three: visits, prior, W, child) once the
+    // node is known to be expanded. Loading a chosen child's edges together
+    // with its state (one dependent round trip per level instead of two) was
+    // measured and gained nothing in self-play or in the fused search. A child
     // created during this pass is known to be unexpanded, so no lane reads
     // memory another lane of this warp has just written.
     gk_bits st = v.node_state[tbase];
@@ -137,7 +132,6 @@ __device__ __forceinline__ void select_tree(const PuctView& v, int64_t t, int C,
     float node_q = v.node_value[tbase];
     int en[3], ech[3];
     double ep[3], ew[3];
-    if (kPrefetch) load_edges(v, tbase, lane, en, ep, ew, ech);
     bool fresh = false;
     for (;;) {
         const int64_t vtx = tbase + node;
@@ -153,7 +147,7 @@ __device__ __forceinline__ void select_tree(const PuctView& v, int64_t t, int C,
             break;
         }
         const int64_t ebase = vtx * GK_ACTIONS;
-        if (!kPrefetch) load_edges(v, vtx, lane, en, ep, ew, ech);
+        load_edges(v, vtx, lane, en, ep, ew, ech);
         const double scale = sqrt((double)node_n);
         const gk_b96 placements = legal_placements(st);
         bool allowed[3];
@@ -242,7 +236,6 @@ __device__ __forceinline__ void select_tree(const PuctView& v, int64_t t, int C,
             expanded = v.expanded[tbase + ch] != 0;
             node_n = v.node_visits[tbase + ch];
             node_q = v.node_value[tbase + ch];
-            if (kPrefetch) load_edges(v, tbase + ch, lane, en, ep, ew, ech);
             fresh = false;
         }
         if (lane == 0) {
@@ -261,7 +254,7 @@ __device__ __forceinline__ void select_tree(const PuctView& v, int64_t t, int C,
 __global__ void __launch_bounds__(32 * kWarpsPerBlock, 7) puct_select_kernel(PuctView v, int64_t B, int C, PuctOptions o) {
     const int lane = threadIdx.x & 31;
     const int64_t t = (blockIdx.x * (int64_t)blockDim.x + threadIdx.x) >> 5;
-    if (t < B) select_tree<true>(v, t, C, o, lane);
+    if (t < B) select_tree(v, t, C, o, lane);
 }
 
 // Expansion of tree t's leaf with the evaluator's output and, if `backup`,
@@ -539,7 +532,7 @@ __global__ void __launch_bounds__(32 * kWarpsPerBlock, 4) puct_search_hash_kerne
     expand_backup_tree(v, t, C, o, 0, lane, sum_scratch[threadIdx.x >> 5]);
     __syncwarp();
     for (int i = 0; i < simulations; ++i) {
-        select_tree<false>(v, t, C, o, lane);
+        select_tree(v, t, C, o, lane);
         __syncwarp();
         hash_eval_tree(v, t, lane);
         __syncwarp();
